@@ -1,0 +1,414 @@
+#!/usr/bin/env python
+"""Benchmark of the paged GQA decode path on B200.
+
+One step = one com.microsoft.PagedAttention call for a batch of decode sequences: append the
+new token's K/V into the paged pool, then split-K paged decode over the whole ragged batch.
+
+Workload: per GPU 128 sequences x 1 query token, 32 q / 8 kv heads,
+head 128, bf16, block 16, context lengths seeded U[512, 8192], block tables = consecutive
+slices of a seeded permutation of a 131072-block pool, Q/K/V/pool ~ N(0,1)/sqrt(128).
+Multi-GPU (torchrun, N ranks): the kv heads are sharded across ranks (rank r owns kv heads
+[r*8/N, (r+1)*8/N) and their q heads) and the batch grows to 128*N sequences so per-GPU work is
+fixed (weak scaling); one NCCL all-gather reassembles the head-sharded outputs.
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the CPU reference restatement
+(oracle/, all host threads) on a bounded sample of the same workload instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "onnxruntime-ep-mlx_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "paged GQA decode tokens/s"
+UNIT = "tokens/s"
+H, KV, D, BS = 32, 8, 128, 16
+B_PER_GPU = 128
+NB_PER_GPU = 131072
+L_LO, L_HI = 512, 8192
+SEED = 3
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU work budget of the cpu_baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------------------------------
+# Workload metadata (identical on every rank)
+# --------------------------------------------------------------------------------------------
+def make_metadata(n_gpus: int):
+    B = B_PER_GPU * n_gpus
+    rng = np.random.default_rng(SEED)
+    L = rng.integers(L_LO, L_HI, size=B, endpoint=True).astype(np.int64)
+    maxb = -(-L_HI // BS)
+    nblk = -(-L // BS)
+    NB = max(NB_PER_GPU, int(nblk.sum()))
+    perm = rng.permutation(NB).astype(np.int32)
+    bt = np.zeros((B, maxb), np.int32)
+    off = 0
+    for b in range(B):
+        bt[b, :nblk[b]] = perm[off:off + nblk[b]]
+        off += int(nblk[b])
+    cum = np.arange(B + 1, dtype=np.int32)
+    past = (L - 1).astype(np.int32)
+    return dict(B=B, L=L, NB=NB, maxb=maxb, bt=bt, cum=cum, past=past)
+
+
+def decode_bytes(meta, kv_heads):
+    """Algorithmic bytes of one decode call on one GPU: every K/V element of every visible
+    position read once, block-table entries, q read, output written, new K/V rows appended."""
+    L = meta["L"]
+    kv = int(L.sum()) * kv_heads * D * 2 * 2
+    table = int((-(-L // BS)).sum()) * 4
+    q_heads = H * kv_heads // KV
+    qo = meta["B"] * q_heads * D * 2 * 2
+    append = meta["B"] * kv_heads * D * 2 * 2 * 2
+    return kv + table + qo + append, kv
+
+
+# --------------------------------------------------------------------------------------------
+# Clock sampling during the timed region (NVML)
+# --------------------------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons = [], 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            handle = None
+            try:
+                import torch
+                uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+                handle = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+            except Exception:
+                visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(visible.split(",")[device_index]) if visible else device_index
+                handle = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.handle = handle
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM))
+                self.reasons |= self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.nvml:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        if not self.nvml:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        names = [n for n, bit in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------------------------------------
+# CPU baseline / reference arm: the C restatement of the reference on host cores
+# --------------------------------------------------------------------------------------------
+def cpu_sample(meta, budget_s, seqs=None):
+    """Time the CPU oracle on a sample of the workload's sequences; tokens/s."""
+    import ml_dtypes
+    from oracle import cpu_oracle
+
+    rng = np.random.default_rng(1234)
+    L = meta["L"]
+    seqs = seqs or 16
+    idx = np.arange(min(seqs, len(L)))
+    Ls = L[idx]
+    nblk = -(-Ls // BS)
+    NB = int(nblk.sum())
+    bt = np.zeros((len(idx), meta["maxb"]), np.int32)
+    off = 0
+    for i, n in enumerate(nblk):
+        bt[i, :n] = np.arange(off, off + n)
+        off += int(n)
+    s = 1.0 / math.sqrt(D)
+    bf = ml_dtypes.bfloat16
+    kc = (rng.standard_normal((NB, BS, KV, D), np.float32) * s).astype(bf)
+    vc = (rng.standard_normal((NB, BS, KV, D), np.float32) * s).astype(bf)
+    q = (rng.standard_normal((len(idx), H * D), np.float32) * s).astype(bf)
+    k = (rng.standard_normal((len(idx), KV * D), np.float32) * s).astype(bf)
+    v = (rng.standard_normal((len(idx), KV * D), np.float32) * s).astype(bf)
+    cum = np.arange(len(idx) + 1, dtype=np.int32)
+    past = (Ls - 1).astype(np.int32)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    tokens = 0
+    while True:
+        cpu_oracle.paged_attention(q, k, v, kc, vc, cum, past, bt, H, KV, threads=threads)
+        tokens += len(idx)
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return {"value": tokens / el, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{len(idx)} of the workload's sequences (L={int(Ls.min())}..{int(Ls.max())}), "
+                      f"repeated for {el:.1f} s with the C oracle (oracle/paged_ref.c, pthreads)"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    meta = make_metadata(1)
+    per_step = []
+    sample = None
+    for i in range(args.warmup + args.steps):
+        r = cpu_sample(meta, 0.0, seqs=8)
+        if i >= args.warmup:
+            per_step.append(r["value"])
+            sample = r
+    value = statistics.median(per_step)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 8 / value * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded)",
+            "config": {"workload": "BASELINE config 3: paged GQA decode, 128 seq x 1 token, 32q/8kv, d128, bs16, ctx U[512,8192]",
+                       "sample": "first 8 sequences per step"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": sample["cores"], "kind": "port",
+                             "sample": "first 8 sequences of the workload per step, C oracle on all host threads"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------------------------
+# B200 arm
+# --------------------------------------------------------------------------------------------
+def run_b200(args):
+    import ctypes
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    n = world if world > 1 else 1
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if KV % n:
+        raise SystemExit(f"--gpus {n} must divide the 8 kv heads")
+
+    from onnxruntime_ep_b200 import _capi, paged
+
+    meta = make_metadata(n)
+    kvh = KV // n
+    qh = H // n
+    B, NB, maxb = meta["B"], meta["NB"], meta["maxb"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    s = 1.0 / math.sqrt(D)
+    kc = torch.empty((NB, BS, kvh, D), dtype=torch.bfloat16, device=dev)
+    vc = torch.empty_like(kc)
+    kc.normal_(0.0, s, generator=g)
+    vc.normal_(0.0, s, generator=g)
+    q = (torch.randn((B, qh * D), generator=g, device=dev) * s).to(torch.bfloat16)
+    k = (torch.randn((B, kvh * D), generator=g, device=dev) * s).to(torch.bfloat16)
+    v = (torch.randn((B, kvh * D), generator=g, device=dev) * s).to(torch.bfloat16)
+    cum_d = torch.from_numpy(meta["cum"]).to(dev)
+    past_d = torch.from_numpy(meta["past"]).to(dev)
+    bt_d = torch.from_numpy(meta["bt"]).to(dev)
+    out = torch.empty((B, qh * D), dtype=torch.bfloat16, device=dev)
+    host = {"cumulative_sequence_length": meta["cum"], "past_seqlens": meta["past"], "block_table": meta["bt"]}
+    p, keep, out = paged.build_params(q, k, v, kc, vc, cum_d, past_d, bt_d, num_heads=qh, kv_num_heads=kvh,
+                                      output=out, host_metadata=host)
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    pp = ctypes.byref(p)
+    gathered = torch.empty((n, B, qh * D), dtype=torch.bfloat16, device=dev) if n > 1 else None
+
+    def step():
+        _capi.check(_capi.LIB.b200_paged_attention(pp, sp))
+        if n > 1:
+            dist.all_gather_into_tensor(gathered, out)
+            # [N, B, qh*D] -> [B, H*D]: rank r's heads are q heads [r*qh, (r+1)*qh)
+            return gathered.permute(1, 0, 2).reshape(B, H * D)
+        return out
+
+    for _ in range(args.warmup):
+        step()
+    _capi.check(_capi.LIB.b200_read_status(pp, sp))
+
+    # per-launch attention timing on the launch stream
+    ev_pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(args.steps)]
+    for a, b in ev_pairs:  # torch creates the CUDA event on first record
+        a.record(stream)
+        b.record(stream)
+    launches0 = _capi.LIB.b200_launch_count()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t_start.record(stream)
+        for i in range(args.steps):
+            p.attention_event_begin = ctypes.c_void_p(ev_pairs[i][0].cuda_event)
+            p.attention_event_end = ctypes.c_void_p(ev_pairs[i][1].cuda_event)
+            step()
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    p.attention_event_begin = p.attention_event_end = None
+    launches = _capi.LIB.b200_launch_count() - launches0
+    elapsed_ms = t_start.elapsed_time(t_end)
+    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_pairs)
+    if dist:
+        t = torch.tensor([elapsed_ms, attn_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        elapsed_ms, attn_ms = float(t[0]), float(t[1])
+    _capi.check(_capi.LIB.b200_read_status(pp, sp))
+    ms_per_step = elapsed_ms / args.steps
+    value = B / (ms_per_step / 1e3)
+
+    # ---- end to end through the public API with host buffers (pinned), per step H2D of the new
+    # rows + metadata and D2H of the output, caches resident
+    e2e = None
+    if not args.no_e2e:
+        hq = q.cpu().pin_memory(); hk = k.cpu().pin_memory(); hv = v.cpu().pin_memory()
+        hcum = torch.from_numpy(meta["cum"]).pin_memory()
+        hpast = torch.from_numpy(meta["past"]).pin_memory()
+        hbt = torch.from_numpy(meta["bt"]).pin_memory()
+        hout = torch.empty((B, H * D), dtype=torch.bfloat16).pin_memory()
+        h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hcum, hpast, hbt))
+        d2h = hout.numel() * hout.element_size()
+
+        def e2e_step():
+            q.copy_(hq, non_blocking=True); k.copy_(hk, non_blocking=True); v.copy_(hv, non_blocking=True)
+            cum_d.copy_(hcum, non_blocking=True); past_d.copy_(hpast, non_blocking=True)
+            bt_d.copy_(hbt, non_blocking=True)
+            res = step()
+            hout.copy_(res, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t[0])
+        e2e = {"value": B / (e_ms / args.steps / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h)}
+
+    # ---- roofline of the dominant kernels (append is inside the step, decode + combine timed)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    peak = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    alg_bytes, kv_bytes = decode_bytes(meta, kvh)
+    achieved = alg_bytes / (attn_ms / 1e3) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "paged_decode_traffic.json")) as f:
+            prof = json.load(f)
+        traffic = prof["dram_bytes_per_kv_byte"] * kv_bytes
+    except Exception:
+        pass
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and n == 1:
+            cpu = cpu_sample(meta, args.cpu_seconds)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded numpy metadata, torch-seeded N(0,1)/sqrt(128) values)",
+            "config": {"workload": "BASELINE config 3: paged GQA decode, 128 seq/GPU x 1 token, 32q/8kv heads "
+                                   "(sharded by kv head across GPUs), d128, bf16, bs16, ctx U[512,8192]",
+                       "global_batch": B, "num_blocks_per_gpu": NB, "kv_heads_per_gpu": kvh,
+                       "l2": "inputs larger than L2 (KV pool 2 x %.1f GiB, %.2f GB read per step)" %
+                             (kc.numel() * 2 / 2**30, kv_bytes / 1e9),
+                       "parallelism": f"kv-head shard x{n}" + (" + NCCL all-gather" if n > 1 else "")},
+            "kv_read_gbs": kv_bytes / (attn_ms / 1e3) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": peak_src, "frac_of_8tbs": achieved / 8000.0,
+                         "kernel": "attention section (paged_decode_kernel + decode_combine_kernel)",
+                         "alg_bytes_per_launch": alg_bytes, "ms_per_launch": attn_ms},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks.summary(),
+            "gpu_launches": int(launches),
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

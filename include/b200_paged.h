@@ -1,0 +1,200 @@
+/*
+ * b200_paged.h - C ABI of the B200-native paged-KV attention path.
+ *
+ * This library replaces the KV-cache attention hot path of the onnxruntime-ep-mlx plugin
+ * execution provider (reference: rust/src/ops/attention.rs, rust/src/ops/paged_attention.rs,
+ * rust/src/ops/kv_cache.rs) with hand-written sm_100a CUDA kernels.  Every entry point takes
+ * plain pointers and sizes, returns a B200_* status code and never throws; a failing call
+ * leaves a human-readable message in b200_last_error() (thread local).
+ *
+ * Device pointers are CUDA device addresses on the current device; `stream` is a
+ * cudaStream_t passed as void*.  Host pointers are marked host_*.
+ */
+#ifndef B200_PAGED_H
+#define B200_PAGED_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200_API __attribute__((visibility("default")))
+#else
+#define B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (map to OrtErrorCode in the EP shell) ---------------------------- */
+#define B200_OK 0
+#define B200_ERR_INVALID_ARGUMENT 1 /* bad attributes / shapes: ORT_INVALID_ARGUMENT */
+#define B200_ERR_FAIL 2             /* invalid runtime metadata: ORT_EP_FAIL          */
+#define B200_ERR_CUDA 3             /* a CUDA runtime call failed                     */
+#define B200_ERR_UNSUPPORTED 4      /* form the kernels do not implement              */
+#define B200_ERR_WORKSPACE 5        /* workspace missing or too small                 */
+#define B200_ERR_DEVICE 6           /* device-side check failed (see message)         */
+
+/* ---- element types: ONNX TensorProto.DataType values -------------------------------- */
+#define B200_DTYPE_FLOAT 1
+#define B200_DTYPE_UINT8 2 /* int4 cache: two +8-biased nibbles per byte */
+#define B200_DTYPE_INT8 3
+#define B200_DTYPE_INT32 6
+#define B200_DTYPE_FLOAT16 10
+#define B200_DTYPE_BFLOAT16 16
+#define B200_DTYPE_FLOAT8E4M3FN 17
+
+/*
+ * One com.microsoft.PagedAttention call.  Field meanings follow the operator's inputs,
+ * outputs and attributes (reference claim rust/src/ops/attention.rs:4384-4645, op
+ * :3857-4382).  Zero-initialise and fill what is present.
+ */
+typedef struct B200PagedAttentionParams {
+  /* attributes */
+  int32_t num_heads;          /* H                                                        */
+  int32_t kv_num_heads;       /* KV, H % KV == 0                                          */
+  int32_t head_size;          /* d (query hidden / H, or packed hidden / (H + 2 KV))      */
+  float scale;                /* 0 -> 1/sqrt(d) (attention.rs:448-453)                    */
+  int32_t is_causal;          /* operator default is 1: callers set it from the attribute */
+  int32_t local_window_size;  /* -1 or 0 = no window, > 0 = left window                   */
+  float softcap;              /* 0 = off                                                  */
+  int32_t do_rotary;          /* RoPE on new Q/K at positions [past, past + n)            */
+  int32_t rotary_interleaved;
+  int32_t rotary_offset;      /* first rotated channel, multiple of 8                     */
+  int32_t rotary_dim;         /* 2 * cos_cache.shape[1]                                   */
+  int32_t rotary_positions;   /* cos_cache.shape[0]                                       */
+  float qk_norm_epsilon;      /* used when q_norm_weight is set (1e-6 default)            */
+  int32_t act_dtype;          /* FLOAT16 or BFLOAT16 (T)                                  */
+  int32_t cache_dtype;        /* T, INT8, UINT8 (int4) or FLOAT8E4M3FN                    */
+  int32_t k_quant_per_channel;/* int caches: 0 PER_TENSOR, 1 PER_CHANNEL                  */
+  int32_t v_quant_per_channel;
+
+  /* geometry */
+  int32_t num_tokens;         /* nt: packed new tokens                                    */
+  int32_t batch;              /* B: sequences, cumulative_sequence_length has B + 1       */
+  int32_t num_blocks;         /* NB                                                       */
+  int32_t block_size;         /* bs                                                       */
+  int32_t max_blocks_per_seq; /* block_table is [B, max_blocks_per_seq]                   */
+  int64_t query_row_stride;   /* elements between tokens; 0 -> H*d (packed: (H+2KV)*d)   */
+  int64_t key_row_stride;     /* 0 -> KV*d                                                */
+  int64_t value_row_stride;   /* 0 -> KV*d                                                */
+
+  /* device tensors (inputs 0-15, output 0; caches are updated in place) */
+  const void* query;          /* [nt, H*d] (packed: [nt, (H+2KV)*d])                      */
+  const void* key;            /* [nt, KV*d]; packed: query + H*d                          */
+  const void* value;          /* [nt, KV*d]; packed: query + (H+KV)*d                     */
+  void* key_cache;            /* [NB, bs, KV, d] (int4: ceil(d/2) bytes)                  */
+  void* value_cache;          /* [NB, bs, KV, d]                                          */
+  const int32_t* cumulative_sequence_length; /* [B + 1]                                   */
+  const int32_t* past_seqlens;               /* [B]                                       */
+  const int32_t* block_table;                /* [B, max_blocks_per_seq]                   */
+  const void* cos_cache;      /* [rotary_positions, rotary_dim/2] in T                    */
+  const void* sin_cache;
+  const int32_t* slot_mapping;/* [nt] or NULL; -1 skips the write                         */
+  const void* head_sink;      /* [H] in T or NULL                                         */
+  const void* q_norm_weight;  /* [d] in T or NULL (k_norm_weight set together)            */
+  const void* k_norm_weight;
+  const float* k_scale;       /* int caches: [1] or [KV*d]; fp8: [NB, KV] per block/head  */
+  const float* v_scale;
+  void* output;               /* [nt, H*d] in T                                           */
+
+  /* optional host copies of the metadata: enable the reference's host validation
+   * (attention.rs:3934-3990) before any launch, and skip device-side duplicate-slot work
+   * when the host proves slots unique */
+  const int32_t* host_cumulative_sequence_length;
+  const int32_t* host_past_seqlens;
+  const int32_t* host_block_table;
+  const int32_t* host_slot_mapping;
+
+  /* scratch */
+  void* workspace;            /* device, >= b200_paged_attention_workspace_size()         */
+  size_t workspace_bytes;
+  int32_t* device_status;     /* optional device int32; NULL -> a word in the workspace   */
+
+  /* tuning (session options ep.b200.*) */
+  int32_t decode_tiles_per_split; /* 0 -> automatic                                       */
+  int32_t force_generic;          /* 1 -> run the generic kernel for every sequence       */
+  int32_t num_sms;                /* 0 -> query the device                                */
+
+  /* optional cudaEvent_t handles recorded on `stream` right before the first and right after
+   * the last attention kernel of the call (decode + combine + prefill), for live timing */
+  void* attention_event_begin;
+  void* attention_event_end;
+} B200PagedAttentionParams;
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+B200_API int b200_version(void);
+
+/* sizeof(B200PagedAttentionParams) and sizeof(B200NodeInfo) as compiled into the library, so a
+ * binding (ctypes, cgo) can check its struct layout at load time. */
+B200_API size_t b200_params_size(void);
+B200_API size_t b200_node_info_size(void);
+
+/* Number of kernels (and device memsets) this library has enqueued since load. */
+B200_API uint64_t b200_launch_count(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+B200_API const char* b200_last_error(void);
+
+/* Bytes of device workspace the call needs (depends on shapes only, not on metadata). */
+B200_API int b200_paged_attention_workspace_size(const B200PagedAttentionParams* p, size_t* bytes);
+
+/* Host-side metadata validation, restating attention.rs:3934-3990.  Needs the host_*
+ * metadata copies.  Returns B200_OK or B200_ERR_FAIL with the reference's message. */
+B200_API int b200_paged_attention_validate_host(const B200PagedAttentionParams* p);
+
+/* Whole PagedAttention node on `stream`: KV append (+ RoPE / q-k norm / integer or fp8
+ * encode), paged decode (split-K), ragged prefill, output packing.  Replaces
+ * paged_attention_op (rust/src/ops/attention.rs:3857-4382) and the direct Metal decode
+ * (rust/src/ops/paged_attention.rs:229-334).  Asynchronous: device-side metadata checks
+ * land in the status word, read by b200_read_status(). */
+B200_API int b200_paged_attention(const B200PagedAttentionParams* p, void* stream);
+
+/* KV append alone (reshape-and-cache): the scatter of attention.rs:4064-4120 plus the
+ * in-place write-back of engine.rs:1212-1364, without attention.  Uses the same params. */
+B200_API int b200_kv_append(const B200PagedAttentionParams* p, void* stream);
+
+/* Synchronise `stream`, read and clear the device status word of the last call with these
+ * params, and turn set bits into B200_ERR_FAIL / B200_ERR_DEVICE with the reference's
+ * messages. */
+B200_API int b200_read_status(const B200PagedAttentionParams* p, void* stream);
+
+/*
+ * Claim predicate, restating paged_attention_claim (rust/src/ops/attention.rs:4384-4645)
+ * and the integer-cache claim (rust/src/ops/kv_cache.rs:16-108) over a plain description of
+ * the node.  Returns 1 (claim) or 0 (decline, reason written to `reason`).
+ */
+#define B200_MAX_RANK 8
+typedef struct B200TensorInfo {
+  int32_t present;              /* 0 = absent optional input/output                     */
+  int32_t dtype;                /* B200_DTYPE_* (ONNX enum)                             */
+  int32_t rank;                 /* -1 = unknown rank                                    */
+  int64_t shape[B200_MAX_RANK]; /* -1 = symbolic dimension                              */
+} B200TensorInfo;
+
+typedef struct B200NodeInfo {
+  int32_t num_inputs;
+  int32_t num_outputs;
+  B200TensorInfo inputs[17];
+  B200TensorInfo outputs[3];
+  /* integer attributes (value used when has_* is 0 is the operator default) */
+  int64_t num_heads, kv_num_heads, is_causal, local_window_size, do_rotary, rotary_interleaved,
+      rotary_offset, v_head_size;
+  int32_t has_scale;
+  float scale;
+  float softcap;
+  float qk_norm_epsilon;
+  char kv_cache_layout[16]; /* "SEPARATE" (default) or "LATENT"                       */
+  char k_quant_type[16];    /* "NONE" (default), "PER_TENSOR", "PER_CHANNEL"          */
+  char v_quant_type[16];
+  char k_cache_dtype[16];   /* "" (default), "int8", "int4", "float16", "bfloat16"    */
+  char v_cache_dtype[16];
+} B200NodeInfo;
+
+B200_API int b200_paged_attention_claim(const B200NodeInfo* node, char* reason, size_t reason_len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_PAGED_H */

@@ -1,0 +1,94 @@
+// Internal kernel argument blocks and launchers (not part of the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace b200 {
+
+// Device status word.  Bit flags, OR-ed by any thread that detects a problem; the host maps
+// them to the reference's error messages (attention.rs:3934-3990).
+// ---------------------------------------------------------------------------------------
+enum StatusBits : int {
+  kStatusBadCumulative = 1 << 0,   // cum[0] != 0, not monotone, cum[B] != nt
+  kStatusBadPast = 1 << 1,         // past < 0
+  kStatusBadCapacity = 1 << 2,     // total > max_blocks * block_size
+  kStatusBadBlock = 1 << 3,        // block id outside [0, num_blocks)
+  kStatusBadSlot = 1 << 4,         // slot outside [-1, num_blocks * block_size)
+  kStatusTimeout = 1 << 5,         // a bounded wait ran out
+  kStatusBadPosition = 1 << 6,     // RoPE position outside the cos/sin cache
+};
+
+
+// KV append / Q-K preprocessing (kv_append.cu).
+struct PrologueArgs {
+  int num_heads, kv_heads, head_size;
+  int num_tokens, batch, num_blocks, block_size, max_blocks;
+  int act_dtype, cache_dtype, k_per_channel, v_per_channel;
+  int do_norm, do_rotary, rotary_interleaved, rotary_offset, rotary_dim, rotary_positions;
+  int kv_only;  // append alone: skip Q processing
+  float norm_eps;
+  int64_t query_stride, key_stride, value_stride;
+  const void* query; const void* key; const void* value;
+  void* key_cache; void* value_cache;
+  const int32_t* cum; const int32_t* past; const int32_t* block_table; const int32_t* slot_mapping;
+  const void* cos_cache; const void* sin_cache; const void* q_norm; const void* k_norm;
+  const float* k_scale; const float* v_scale;
+  void* q_proc; void* k_proc;  // processed rows [nt, H*d], [nt, KV*d] in T (norm/RoPE only)
+  int* owner_keys; int* owner_vals; uint32_t owner_capacity;  // duplicate-slot table or null
+  int* status;
+};
+
+void launch_meta_check(const PrologueArgs& a, cudaStream_t stream);
+size_t prologue_smem_bytes(const PrologueArgs& a);
+cudaError_t launch_prologue(const PrologueArgs& a, cudaStream_t stream);
+
+// Attention over the paged cache (paged_generic.cu, paged_decode.cu).
+struct AttnArgs {
+  int num_heads, kv_heads, head_size, group;
+  int num_tokens, batch, num_blocks, block_size, max_blocks;
+  int act_dtype, cache_dtype, k_per_channel, v_per_channel;
+  int is_causal, window;
+  float scale, softcap;
+  // processed new rows (Q after norm/RoPE, K after norm/RoPE, V raw) and their row strides
+  const void* q; const void* k_new; const void* v_new;
+  int64_t q_stride, k_stride, v_stride;
+  const void* key_cache; const void* value_cache;
+  const float* k_scale; const float* v_scale;
+  const int32_t* cum; const int32_t* past; const int32_t* block_table;
+  const void* head_sink;
+  void* out;
+  int* status;
+  int skip_decode;   // generic kernel: leave sequences with nq*group <= kDecodeRows to the decode kernel
+};
+
+constexpr int kDecodeRows = 8;   // q rows (query x head-in-group) one decode unit covers
+constexpr int kTile = 16;        // tokens per decode tile (one mma M tile)
+
+cudaError_t launch_generic(const AttnArgs& a, cudaStream_t stream);
+
+// Split-K decode plan, written by decode_plan_kernel into the workspace.
+struct DecodePlan {
+  int* n_units;        // [1]   units = (sequence, split) pairs x kv heads
+  int2* units;         // [max_items] (sequence, split)
+  int* seq_nsplit;     // [B]   0 = sequence not on the decode path
+  int* seq_part_off;   // [B]   first partial row of the sequence
+  float* partials;     // [rows][head_size + 2]  (m, l, o[d]) per unit row
+  int max_items;
+  int tiles_per_split;
+};
+
+struct DecodeMaps {
+  CUtensorMap k_map;
+  CUtensorMap v_map;
+};
+
+// Plan kernel; also clears the status word, so it must be the call's first launch.
+cudaError_t launch_decode_plan(const AttnArgs& a, const DecodePlan& plan, cudaStream_t stream);
+cudaError_t launch_decode(const AttnArgs& a, const DecodePlan& plan, const DecodeMaps& maps, int num_sms,
+                          cudaStream_t stream);
+bool decode_supported(int head_size, int block_size, int act_dtype, int cache_dtype);
+
+}  // namespace b200

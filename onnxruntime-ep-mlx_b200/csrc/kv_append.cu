@@ -1,0 +1,278 @@
+// KV append ("reshape and cache") and the per-call metadata checks.
+//
+// Reference behaviour (rust/src/ops/attention.rs):
+//  * :4064-4079  slot of new token j of sequence b: slot_mapping[token] if given, else
+//                block_table[b, (past+j)/bs] * bs + (past+j) % bs; slot < 0 skips the write
+//  * :4045-4057  optional per-head RMS norm of new Q/K, then RoPE at positions [past, total)
+//  * :4080-4120  scatter of the (optionally integer-encoded, kv_cache.rs:170-220) rows into the
+//                flattened [NB*bs, KV, d] caches, applied in token order so a later token
+//                overwrites an earlier one at the same slot
+//  * engine.rs:1212-1364  the updated rows land in the caller's input cache buffers
+//
+// B200 design: one CTA per token row.  The plain path (no norm/RoPE, float cache) is a 16-byte
+// vectorised copy of the token's whole [KV*d] row, which is contiguous in both the packed input
+// and the [NB, bs, KV, d] pool.  Duplicate slots are resolved deterministically: a per-call
+// open-addressing table maps slot -> largest token index (atomicMax), and only that token
+// writes.  The table is skipped when the host proved the slots unique.
+#include "b200_common.cuh"
+#include "b200_kernels.h"
+
+namespace b200 {
+
+__device__ __forceinline__ uint32_t slot_hash(int32_t slot) {
+  uint32_t x = static_cast<uint32_t>(slot);
+  x ^= x >> 16;
+  x *= 0x7feb352dU;
+  x ^= x >> 15;
+  x *= 0x846ca68bU;
+  x ^= x >> 16;
+  return x;
+}
+
+// Slot of token t, or -1 (skip).  Returns false when the metadata makes it invalid.
+__device__ __forceinline__ bool token_slot(const PrologueArgs& a, int t, int b, int64_t& slot) {
+  if (a.slot_mapping) {
+    slot = a.slot_mapping[t];
+    return slot >= -1 && slot < (int64_t)a.num_blocks * a.block_size;
+  }
+  int64_t logical = (int64_t)a.past[b] + (t - a.cum[b]);
+  if (logical < 0) return false;
+  int64_t page = logical / a.block_size;
+  if (page >= a.max_blocks) return false;
+  int32_t blk = a.block_table[(int64_t)b * a.max_blocks + page];
+  if (blk < 0 || blk >= a.num_blocks) return false;
+  slot = (int64_t)blk * a.block_size + logical % a.block_size;
+  return true;
+}
+
+// Device-side metadata validation (the checks of attention.rs:3934-3990) and, when asked,
+// the slot -> last-token table.  One thread per sequence and one per token.
+__global__ void meta_check_kernel(PrologueArgs a) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < a.batch) {
+    int c0 = a.cum[i], c1 = a.cum[i + 1];
+    int bits = 0;
+    if ((i == 0 && c0 != 0) || c0 < 0 || c0 > c1 || (i == a.batch - 1 && c1 != a.num_tokens)) bits |= kStatusBadCumulative;
+    int p = a.past[i];
+    if (p < 0) bits |= kStatusBadPast;
+    int64_t total = (int64_t)p + (c1 - c0);
+    if (total > (int64_t)a.max_blocks * a.block_size) bits |= kStatusBadCapacity;
+    if (!(bits & (kStatusBadPast | kStatusBadCapacity)) && c1 >= c0) {
+      int64_t needed = (total + a.block_size - 1) / a.block_size;
+      const int32_t* row = a.block_table + (int64_t)i * a.max_blocks;
+      for (int64_t j = 0; j < needed; ++j) {
+        int32_t blk = row[j];
+        if (blk < 0 || blk >= a.num_blocks) { bits |= kStatusBadBlock; break; }
+      }
+    }
+    if (a.rotary_positions > 0 && total > a.rotary_positions) bits |= kStatusBadPosition;
+    if (bits) set_status(a.status, bits);
+  }
+  if (i < a.num_tokens) {
+    int b = seq_of_token(a.cum, a.batch, i);
+    int64_t slot;
+    if (!token_slot(a, i, b, slot)) {
+      set_status(a.status, a.slot_mapping ? kStatusBadSlot : kStatusBadBlock);
+      return;
+    }
+    if (slot < 0 || !a.owner_keys) return;
+    uint32_t mask = a.owner_capacity - 1;
+    uint32_t h = slot_hash((int32_t)slot) & mask;
+    for (uint32_t probe = 0; probe < a.owner_capacity; ++probe) {
+      int prev = atomicCAS(&a.owner_keys[h], -1, (int)slot);
+      if (prev == -1 || prev == (int)slot) {
+        atomicMax(&a.owner_vals[h], i);
+        return;
+      }
+      h = (h + 1) & mask;
+    }
+  }
+}
+
+__device__ __forceinline__ bool owns_slot(const PrologueArgs& a, int t, int64_t slot) {
+  if (!a.owner_keys) return true;
+  uint32_t mask = a.owner_capacity - 1;
+  uint32_t h = slot_hash((int32_t)slot) & mask;
+  for (uint32_t probe = 0; probe < a.owner_capacity; ++probe) {
+    int key = a.owner_keys[h];
+    if (key == (int)slot) return a.owner_vals[h] == t;
+    if (key == -1) return true;
+    h = (h + 1) & mask;
+  }
+  return true;
+}
+
+// Encode one [d] row (fp32 values in `src`, stride 1) of kv head `kh` into the cache slot.
+__device__ void write_cache_row(const PrologueArgs& a, bool is_key, int64_t slot, int kh, const float* src,
+                                int tid, int nthreads) {
+  const int d = a.head_size;
+  const int dtype = a.cache_dtype;
+  void* cache = is_key ? a.key_cache : a.value_cache;
+  const float* scale = is_key ? a.k_scale : a.v_scale;
+  const int per_channel = is_key ? a.k_per_channel : a.v_per_channel;
+  if (dtype == B200_DTYPE_UINT8) {
+    int width = (d + 1) / 2;
+    uint8_t* row = reinterpret_cast<uint8_t*>(cache) + (slot * a.kv_heads + kh) * (int64_t)width;
+    for (int j = tid; j < width; j += nthreads) {
+      int d0 = 2 * j, d1 = 2 * j + 1;
+      float s0 = per_channel ? scale[kh * d + d0] : scale[0];
+      int lo = quant_code(src[d0], s0, 4) + 8;
+      int hi = 8;
+      if (d1 < d) {
+        float s1 = per_channel ? scale[kh * d + d1] : scale[0];
+        hi = quant_code(src[d1], s1, 4) + 8;
+      }
+      row[j] = (uint8_t)(lo | (hi << 4));
+    }
+    return;
+  }
+  int64_t base = (slot * a.kv_heads + kh) * (int64_t)d;
+  for (int j = tid; j < d; j += nthreads) {
+    float x = src[j];
+    if (dtype == B200_DTYPE_INT8) {
+      float s = per_channel ? scale[kh * d + j] : scale[0];
+      reinterpret_cast<int8_t*>(cache)[base + j] = (int8_t)quant_code(x, s, 8);
+    } else if (dtype == B200_DTYPE_FLOAT8E4M3FN) {
+      int64_t blk = slot / a.block_size;
+      float s = scale[blk * a.kv_heads + kh];
+      reinterpret_cast<uint8_t*>(cache)[base + j] = fp8_code(x, s);
+    } else {
+      store_act(cache, base + j, x, dtype);
+    }
+  }
+}
+
+// One CTA per token.  Shared memory (processing path): fp32 rows [H*d] for Q and [KV*d] for
+// K, plus [KV*d] for V when the cache is integer/fp8 encoded.
+__global__ void kv_prologue_kernel(PrologueArgs a) {
+  extern __shared__ float smem[];
+  const int t = blockIdx.x;
+  const int b = seq_of_token(a.cum, a.batch, t);
+  const int H = a.num_heads, KV = a.kv_heads, d = a.head_size;
+  const int tid = threadIdx.x, nthreads = blockDim.x;
+  const int dt = a.act_dtype;
+
+  int64_t slot = -1;
+  bool valid = token_slot(a, t, b, slot);
+  bool write = valid && slot >= 0 && owns_slot(a, t, slot);
+  if (!valid && tid == 0) set_status(a.status, a.slot_mapping ? kStatusBadSlot : kStatusBadBlock);
+  if (a.kv_only && !write) return;
+
+  const bool process = a.do_norm || a.do_rotary;
+  const bool float_cache = a.cache_dtype == dt;
+
+  if (!process && float_cache) {
+    if (!write) return;
+    // Plain reshape-and-cache: the token's [KV*d] K and V rows are contiguous in the pool.
+    const int64_t row_elems = (int64_t)KV * d;
+    char* kdst = reinterpret_cast<char*>(a.key_cache) + slot * row_elems * 2;
+    char* vdst = reinterpret_cast<char*>(a.value_cache) + slot * row_elems * 2;
+    const char* ksrc = reinterpret_cast<const char*>(a.key) + (int64_t)t * a.key_stride * 2;
+    const char* vsrc = reinterpret_cast<const char*>(a.value) + (int64_t)t * a.value_stride * 2;
+    const int64_t bytes = row_elems * 2;
+    bool vec = ((reinterpret_cast<uintptr_t>(kdst) | reinterpret_cast<uintptr_t>(vdst) |
+                 reinterpret_cast<uintptr_t>(ksrc) | reinterpret_cast<uintptr_t>(vsrc) | bytes) & 15) == 0;
+    if (vec) {
+      for (int64_t j = tid; j < bytes / 16; j += nthreads) {
+        reinterpret_cast<uint4*>(kdst)[j] = reinterpret_cast<const uint4*>(ksrc)[j];
+        reinterpret_cast<uint4*>(vdst)[j] = reinterpret_cast<const uint4*>(vsrc)[j];
+      }
+    } else {
+      for (int64_t j = tid; j < bytes / 2; j += nthreads) {
+        reinterpret_cast<uint16_t*>(kdst)[j] = reinterpret_cast<const uint16_t*>(ksrc)[j];
+        reinterpret_cast<uint16_t*>(vdst)[j] = reinterpret_cast<const uint16_t*>(vsrc)[j];
+      }
+    }
+    return;
+  }
+
+  float* qs = smem;                 // [H*d]  (processing path only)
+  float* ks = qs + (int64_t)H * d;  // [KV*d]
+  float* vs = ks + (int64_t)KV * d; // [KV*d]
+  const int nq_heads = process && !a.kv_only ? H : 0;
+  const int64_t seq_pos = (int64_t)a.past[b] + (t - a.cum[b]);
+
+  for (int j = tid; j < nq_heads * d; j += nthreads)
+    qs[j] = load_act(a.query, (int64_t)t * a.query_stride + j, dt);
+  for (int j = tid; j < KV * d; j += nthreads) {
+    ks[j] = load_act(a.key, (int64_t)t * a.key_stride + j, dt);
+    vs[j] = load_act(a.value, (int64_t)t * a.value_stride + j, dt);
+  }
+  __syncthreads();
+
+  if (a.do_norm) {
+    // RMS norm per head (attention.rs:4045-4049): x / sqrt(mean(x^2) + eps) * w, rounded to T.
+    const int warp = tid >> 5, lane = tid & 31, nwarps = nthreads >> 5;
+    for (int hh = warp; hh < nq_heads + KV; hh += nwarps) {
+      float* row = hh < nq_heads ? qs + (int64_t)hh * d : ks + (int64_t)(hh - nq_heads) * d;
+      const void* w = hh < nq_heads ? a.q_norm : a.k_norm;
+      float acc = 0.f;
+      for (int j = lane; j < d; j += 32) acc += row[j] * row[j];
+      for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      float denom = sqrtf(__fdiv_rn(acc, (float)d) + a.norm_eps);
+      for (int j = lane; j < d; j += 32)
+        row[j] = round_act(__fmul_rn(__fdiv_rn(row[j], denom), load_act(w, j, dt)), dt);
+    }
+    __syncthreads();
+  }
+  if (a.do_rotary) {
+    // RoPE over channels [offset, offset + rot) at position past + j
+    // (test_paged_attention.py:27-58 / attention.rs:3812-3855), products not fused.
+    if (seq_pos < a.rotary_positions) {
+      const int half = a.rotary_dim / 2;
+      const int pairs = (nq_heads + KV) * half;
+      for (int pidx = tid; pidx < pairs; pidx += nthreads) {
+        int hh = pidx / half, i = pidx % half;
+        float* row = hh < nq_heads ? qs + (int64_t)hh * d : ks + (int64_t)(hh - nq_heads) * d;
+        int i0, i1;
+        if (a.rotary_interleaved) { i0 = a.rotary_offset + 2 * i; i1 = i0 + 1; }
+        else { i0 = a.rotary_offset + i; i1 = i0 + half; }
+        float c = load_act(a.cos_cache, seq_pos * half + i, dt);
+        float s = load_act(a.sin_cache, seq_pos * half + i, dt);
+        float x0 = row[i0], x1 = row[i1];
+        row[i0] = round_act(__fadd_rn(__fmul_rn(x0, c), __fmul_rn(-x1, s)), dt);
+        row[i1] = round_act(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s)), dt);
+      }
+    } else if (tid == 0) {
+      set_status(a.status, kStatusBadPosition);
+    }
+    __syncthreads();
+  }
+  if (process && !a.kv_only) {
+    for (int j = tid; j < H * d; j += nthreads) store_act(a.q_proc, (int64_t)t * H * d + j, qs[j], dt);
+    for (int j = tid; j < KV * d; j += nthreads) store_act(a.k_proc, (int64_t)t * KV * d + j, ks[j], dt);
+  }
+  if (!write) return;
+  const int warp = tid >> 5, lane = tid & 31, nwarps = nthreads >> 5;
+  for (int hh = warp; hh < 2 * KV; hh += nwarps) {
+    bool is_key = hh < KV;
+    int kh = is_key ? hh : hh - KV;
+    write_cache_row(a, is_key, slot, kh, (is_key ? ks : vs) + (int64_t)kh * d, lane, 32);
+  }
+}
+
+void launch_meta_check(const PrologueArgs& a, cudaStream_t stream) {
+  int n = a.batch > a.num_tokens ? a.batch : a.num_tokens;
+  if (n <= 0) return;
+  meta_check_kernel<<<(n + 255) / 256, 256, 0, stream>>>(a);
+}
+
+size_t prologue_smem_bytes(const PrologueArgs& a) {
+  const bool process = a.do_norm || a.do_rotary;
+  if (!process && a.cache_dtype == a.act_dtype) return 0;
+  int qheads = process && !a.kv_only ? a.num_heads : 0;
+  return sizeof(float) * (size_t)a.head_size * (qheads + 2 * a.kv_heads);
+}
+
+cudaError_t launch_prologue(const PrologueArgs& a, cudaStream_t stream) {
+  if (a.num_tokens <= 0) return cudaSuccess;
+  size_t smem = prologue_smem_bytes(a);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kv_prologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  kv_prologue_kernel<<<a.num_tokens, 128, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace b200

@@ -1,0 +1,136 @@
+"""ctypes binding of ``include/b200_paged.h`` (the library's C ABI).
+
+The library is loaded from this package folder.  A missing or stale library raises at import
+time: there is no CPU fallback for the claimed path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_NAME = "libb200_paged.so"
+
+B200_OK = 0
+B200_ERR_INVALID_ARGUMENT = 1
+B200_ERR_FAIL = 2
+B200_ERR_CUDA = 3
+B200_ERR_UNSUPPORTED = 4
+B200_ERR_WORKSPACE = 5
+B200_ERR_DEVICE = 6
+
+DTYPE_FLOAT = 1
+DTYPE_UINT8 = 2
+DTYPE_INT8 = 3
+DTYPE_INT32 = 6
+DTYPE_FLOAT16 = 10
+DTYPE_BFLOAT16 = 16
+DTYPE_FLOAT8E4M3FN = 17
+
+_i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
+
+
+class PagedAttentionParams(ctypes.Structure):
+    """Mirror of ``B200PagedAttentionParams``."""
+
+    _fields_ = [
+        ("num_heads", _i32), ("kv_num_heads", _i32), ("head_size", _i32), ("scale", _f32),
+        ("is_causal", _i32), ("local_window_size", _i32), ("softcap", _f32),
+        ("do_rotary", _i32), ("rotary_interleaved", _i32), ("rotary_offset", _i32),
+        ("rotary_dim", _i32), ("rotary_positions", _i32), ("qk_norm_epsilon", _f32),
+        ("act_dtype", _i32), ("cache_dtype", _i32), ("k_quant_per_channel", _i32),
+        ("v_quant_per_channel", _i32),
+        ("num_tokens", _i32), ("batch", _i32), ("num_blocks", _i32), ("block_size", _i32),
+        ("max_blocks_per_seq", _i32),
+        ("query_row_stride", _i64), ("key_row_stride", _i64), ("value_row_stride", _i64),
+        ("query", _vp), ("key", _vp), ("value", _vp), ("key_cache", _vp), ("value_cache", _vp),
+        ("cumulative_sequence_length", _vp), ("past_seqlens", _vp), ("block_table", _vp),
+        ("cos_cache", _vp), ("sin_cache", _vp), ("slot_mapping", _vp), ("head_sink", _vp),
+        ("q_norm_weight", _vp), ("k_norm_weight", _vp), ("k_scale", _vp), ("v_scale", _vp),
+        ("output", _vp),
+        ("host_cumulative_sequence_length", _vp), ("host_past_seqlens", _vp),
+        ("host_block_table", _vp), ("host_slot_mapping", _vp),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t), ("device_status", _vp),
+        ("decode_tiles_per_split", _i32), ("force_generic", _i32), ("num_sms", _i32),
+        ("attention_event_begin", _vp), ("attention_event_end", _vp),
+    ]
+
+
+MAX_RANK = 8
+
+
+class TensorInfo(ctypes.Structure):
+    _fields_ = [("present", _i32), ("dtype", _i32), ("rank", _i32), ("shape", _i64 * MAX_RANK)]
+
+
+class NodeInfo(ctypes.Structure):
+    """Mirror of ``B200NodeInfo`` (claim predicate input)."""
+
+    _fields_ = [
+        ("num_inputs", _i32), ("num_outputs", _i32),
+        ("inputs", TensorInfo * 17), ("outputs", TensorInfo * 3),
+        ("num_heads", _i64), ("kv_num_heads", _i64), ("is_causal", _i64),
+        ("local_window_size", _i64), ("do_rotary", _i64), ("rotary_interleaved", _i64),
+        ("rotary_offset", _i64), ("v_head_size", _i64),
+        ("has_scale", _i32), ("scale", _f32), ("softcap", _f32), ("qk_norm_epsilon", _f32),
+        ("kv_cache_layout", ctypes.c_char * 16), ("k_quant_type", ctypes.c_char * 16),
+        ("v_quant_type", ctypes.c_char * 16), ("k_cache_dtype", ctypes.c_char * 16),
+        ("v_cache_dtype", ctypes.c_char * 16),
+    ]
+
+
+# Every entry point the header declares, with its ctypes signature.
+SIGNATURES = {
+    "b200_version": (ctypes.c_int, []),
+    "b200_params_size": (ctypes.c_size_t, []),
+    "b200_node_info_size": (ctypes.c_size_t, []),
+    "b200_last_error": (ctypes.c_char_p, []),
+    "b200_launch_count": (ctypes.c_uint64, []),
+    "b200_paged_attention_workspace_size": (
+        ctypes.c_int, [ctypes.POINTER(PagedAttentionParams), ctypes.POINTER(ctypes.c_size_t)]),
+    "b200_paged_attention_validate_host": (ctypes.c_int, [ctypes.POINTER(PagedAttentionParams)]),
+    "b200_paged_attention": (ctypes.c_int, [ctypes.POINTER(PagedAttentionParams), _vp]),
+    "b200_kv_append": (ctypes.c_int, [ctypes.POINTER(PagedAttentionParams), _vp]),
+    "b200_read_status": (ctypes.c_int, [ctypes.POINTER(PagedAttentionParams), _vp]),
+    "b200_paged_attention_claim": (
+        ctypes.c_int, [ctypes.POINTER(NodeInfo), ctypes.c_char_p, ctypes.c_size_t]),
+}
+
+
+class B200Error(RuntimeError):
+    """A failing library call; ``code`` is the B200_ERR_* status."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(message)
+        self.code = code
+
+
+def library_file() -> str:
+    return os.path.join(HERE, LIB_NAME)
+
+
+def load() -> ctypes.CDLL:
+    path = library_file()
+    if not os.path.exists(path):
+        raise ImportError(
+            f"{path} is missing: build it with `make -C onnxruntime-ep-mlx_b200/csrc` "
+            "(the B200 path has no CPU fallback)")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if lib.b200_params_size() != ctypes.sizeof(PagedAttentionParams):
+        raise ImportError("libb200_paged.so: B200PagedAttentionParams layout differs from the binding")
+    if lib.b200_node_info_size() != ctypes.sizeof(NodeInfo):
+        raise ImportError("libb200_paged.so: B200NodeInfo layout differs from the binding")
+    return lib
+
+
+LIB = load()
+
+
+def check(code: int) -> None:
+    if code != B200_OK:
+        raise B200Error(code, LIB.b200_last_error().decode() or f"B200 status {code}")
