@@ -186,10 +186,11 @@ __global__ void kv_prologue_kernel(PrologueArgs a) {
     return;
   }
 
-  float* qs = smem;                 // [H*d]  (processing path only)
-  float* ks = qs + (int64_t)H * d;  // [KV*d]
-  float* vs = ks + (int64_t)KV * d; // [KV*d]
+  // Staged rows: Q (processing path only) then K and V; sized by prologue_smem_bytes().
   const int nq_heads = process && !a.kv_only ? H : 0;
+  float* qs = smem;                        // [nq_heads*d]
+  float* ks = qs + (int64_t)nq_heads * d;  // [KV*d]
+  float* vs = ks + (int64_t)KV * d;        // [KV*d]
   const int64_t seq_pos = (int64_t)a.past[b] + (t - a.cum[b]);
 
   for (int j = tid; j < nq_heads * d; j += nthreads)

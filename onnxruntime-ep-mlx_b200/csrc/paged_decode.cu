@@ -75,9 +75,9 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(AttnArgs a, DecodePla
     int b = base + threadIdx.x;
     int ns = 0, rows = 0;
     if (b < a.batch) {
-      int c0 = a.cum[b], nq = a.cum[b + 1] - c0, past = a.past[b];
+      int c0 = a.cum[b], c1 = a.cum[b + 1], nq = c1 - c0, past = a.past[b];
       int64_t total = (int64_t)past + nq;
-      if (nq >= 1 && nq * a.group <= kDecodeRows && past >= 0 &&
+      if (c0 >= 0 && c1 <= a.num_tokens && nq >= 1 && nq * a.group <= kDecodeRows && past >= 0 &&
           total <= (int64_t)a.max_blocks * a.block_size) {
         int tiles = (int)((total + kTile - 1) / kTile);
         ns = (tiles + P - 1) / P;

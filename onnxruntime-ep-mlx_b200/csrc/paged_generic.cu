@@ -33,7 +33,8 @@ __global__ void __launch_bounds__(128) generic_attention_kernel(AttnArgs a) {
   const int D = a.head_size;
   const int i = t - c0;
   const int past = a.past[b];
-  if (past < 0 || i < 0 || i >= nq) return;  // invalid metadata: flagged by the check kernel
+  // invalid metadata (flagged by the check kernel): never index outside the new rows
+  if (past < 0 || i < 0 || i >= nq || c0 < 0 || a.cum[b + 1] > a.num_tokens) return;
   const int total = past + nq;
   const int kh = h / a.group;
   const bool quant = a.cache_dtype != a.act_dtype;
