@@ -51,19 +51,21 @@ def parse():
                     help="CPU work budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--seqs", type=int, default=B_PER_GPU, help="sequences per GPU (profiling runs use fewer)")
+    ap.add_argument("--pool-blocks", type=int, default=NB_PER_GPU, help="KV pool blocks per GPU")
     return ap.parse_args()
 
 
 # --------------------------------------------------------------------------------------------
 # Workload metadata (identical on every rank)
 # --------------------------------------------------------------------------------------------
-def make_metadata(n_gpus: int):
-    B = B_PER_GPU * n_gpus
+def make_metadata(n_gpus: int, seqs: int = B_PER_GPU, pool_blocks: int = NB_PER_GPU):
+    B = seqs * n_gpus
     rng = np.random.default_rng(SEED)
     L = rng.integers(L_LO, L_HI, size=B, endpoint=True).astype(np.int64)
     maxb = -(-L_HI // BS)
     nblk = -(-L // BS)
-    NB = max(NB_PER_GPU, int(nblk.sum()))
+    NB = max(pool_blocks, int(nblk.sum()))
     perm = rng.permutation(NB).astype(np.int32)
     bt = np.zeros((B, maxb), np.int32)
     off = 0
@@ -241,7 +243,7 @@ def run_b200(args):
 
     from onnxruntime_ep_b200 import _capi, paged
 
-    meta = make_metadata(n)
+    meta = make_metadata(n, args.seqs, args.pool_blocks)
     kvh = KV // n
     qh = H // n
     B, NB, maxb = meta["B"], meta["NB"], meta["maxb"]

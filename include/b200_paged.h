@@ -112,7 +112,8 @@ typedef struct B200PagedAttentionParams {
   int32_t* device_status;     /* optional device int32; NULL -> a word in the workspace   */
 
   /* tuning (session options ep.b200.*) */
-  int32_t decode_tiles_per_split; /* 0 -> automatic                                       */
+  int32_t decode_min_tiles_per_warp; /* decode stream-K: smallest 16-token tile range a warp
+                                      * of the persistent grid takes (0 -> 4)              */
   int32_t force_generic;          /* 1 -> run the generic kernel for every sequence       */
   int32_t num_sms;                /* 0 -> query the device                                */
 
@@ -192,6 +193,14 @@ typedef struct B200NodeInfo {
 } B200NodeInfo;
 
 B200_API int b200_paged_attention_claim(const B200NodeInfo* node, char* reason, size_t reason_len);
+
+/* ---- diagnostics (no counterpart in the reference) ------------------------------------ */
+
+/* Known-answer test of the tcgen05 tensor-core path: one CTA computes, for 128x128 fp16/bf16
+ * row-major device matrices a, b, v, the fp32 products c_qk = a . b^T and c_pv = a . v through
+ * TMA, shared-memory matrix descriptors, tcgen05.mma into tensor memory and tcgen05.ld. */
+B200_API int b200_selftest_tcgen05(int32_t dtype, const void* a, const void* b, const void* v, float* c_qk,
+                                   float* c_pv, int32_t* device_status, void* stream);
 
 #ifdef __cplusplus
 }

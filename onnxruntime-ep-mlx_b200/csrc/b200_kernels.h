@@ -69,16 +69,18 @@ constexpr int kTile = 16;        // tokens per decode tile (one mma M tile)
 
 cudaError_t launch_generic(const AttnArgs& a, cudaStream_t stream);
 
-// Split-K decode plan, written by decode_plan_kernel into the workspace.
+// Decode plan (stream-K layout), written by decode_plan_kernel into the workspace.
 struct DecodePlan {
-  int* n_units;        // [1]   units = (sequence, split) pairs x kv heads
-  int2* units;         // [max_items] (sequence, split)
-  int* seq_nsplit;     // [B]   0 = sequence not on the decode path
-  int* seq_part_off;   // [B]   first partial row of the sequence
-  float* partials;     // [rows][head_size + 2]  (m, l, o[d]) per unit row
-  int max_items;
-  int tiles_per_split;
+  int64_t* total_tiles;  // [1]   tiles over all decode sequences x kv heads
+  int* seq_tile_off;     // [B+1] exclusive prefix of decode tiles (per kv head) over sequences
+  int* done;             // [B*KV] pieces finished per (sequence, kv head), for the fused combine
+  float* part_o;         // [max_warps * 2 * 8][head_size] partial outputs (2 slots per warp)
+  float* part_ml;        // [max_warps * 2 * 8][2]          partial (max, sum), log2 domain
+  int min_tiles_per_warp;
 };
+
+constexpr int kDecodeMaxCtasPerSm = 4;  // grid cap of the decode kernel (bounds partial storage)
+constexpr int kDecodeWarpsPerCta = 4;
 
 struct DecodeMaps {
   CUtensorMap k_map;
@@ -87,8 +89,15 @@ struct DecodeMaps {
 
 // Plan kernel; also clears the status word, so it must be the call's first launch.
 cudaError_t launch_decode_plan(const AttnArgs& a, const DecodePlan& plan, cudaStream_t stream);
+// Host: encode a tiled TMA tensor map (rank 2-5), 128B swizzle, no OOB fill.  `strides` are
+// the byte strides of dims 1..rank-1.  Returns the CUresult.
+int encode_tensor_map(CUtensorMap* map, bool bf16, int rank, const void* base, const uint64_t* dims,
+                      const uint64_t* strides, const uint32_t* box);
+
 cudaError_t launch_decode(const AttnArgs& a, const DecodePlan& plan, const DecodeMaps& maps, int num_sms,
                           cudaStream_t stream);
+cudaError_t launch_tc_selftest(bool bf16, const void* a, const void* b, const void* v, float* c_qk, float* c_pv,
+                               int* status, cudaStream_t stream, int* cu_result);
 bool decode_supported(int head_size, int block_size, int act_dtype, int cache_dtype);
 
 }  // namespace b200

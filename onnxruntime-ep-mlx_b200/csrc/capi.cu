@@ -60,8 +60,8 @@ struct Layout {
   size_t owner_keys = 0, owner_vals = 0;
   uint32_t owner_cap = 0;
   size_t q_proc = 0, k_proc = 0;
-  size_t n_units = 0, units = 0, seq_nsplit = 0, seq_part_off = 0, partials = 0;
-  int max_items = 0, tiles_per_split = 0;
+  size_t total_tiles = 0, seq_tile_off = 0, done = 0, part_o = 0, part_ml = 0;
+  int min_tiles_per_warp = 0;
   bool fast_decode = false;
   bool process = false;
   size_t total = 0;
@@ -94,23 +94,15 @@ Layout make_layout(const B200PagedAttentionParams* p) {
   }
   L.fast_decode = fast_decode_enabled(p);
   if (L.fast_decode) {
-    const int64_t max_tiles =
-        ((int64_t)p->max_blocks_per_seq * p->block_size + b200::kTile - 1) / b200::kTile;
-    int P = p->decode_tiles_per_split;
-    if (P <= 0) {
-      const int64_t target = 8LL * device_sm_count(p);
-      P = 32;
-      while (P > 4 && (int64_t)p->batch * p->kv_num_heads * ((max_tiles + P - 1) / P) < target) P /= 2;
-    }
-    const int64_t max_splits = std::max<int64_t>(1, (max_tiles + P - 1) / P);
-    L.tiles_per_split = P;
-    L.max_items = (int)std::min<int64_t>((int64_t)p->batch * max_splits, INT32_MAX / 4);
-    L.n_units = take(sizeof(int));
-    L.units = take(sizeof(int2) * (size_t)L.max_items);
-    L.seq_nsplit = take(sizeof(int) * (size_t)p->batch);
-    L.seq_part_off = take(sizeof(int) * (size_t)p->batch);
-    const size_t rows = (size_t)L.max_items * p->kv_num_heads * b200::kDecodeRows;
-    L.partials = take(sizeof(float) * rows * (d + 2));
+    // Stream-K decode: at most 2 partial slots of 8 rows per warp of the persistent grid.
+    const size_t max_warps = (size_t)device_sm_count(p) * b200::kDecodeMaxCtasPerSm * b200::kDecodeWarpsPerCta;
+    const size_t part_rows = max_warps * 2 * b200::kDecodeRows;
+    L.min_tiles_per_warp = p->decode_min_tiles_per_warp > 0 ? p->decode_min_tiles_per_warp : 4;
+    L.total_tiles = take(sizeof(int64_t));
+    L.seq_tile_off = take(sizeof(int) * ((size_t)p->batch + 1));
+    L.done = take(sizeof(int) * (size_t)p->batch * p->kv_num_heads);
+    L.part_o = take(sizeof(float) * part_rows * d);
+    L.part_ml = take(sizeof(float) * part_rows * 2);
   }
   L.total = off;
   return L;
@@ -241,20 +233,13 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // [NB*bs, KV, d] view of a cache: box {64 channels, 1 head, 16 slots}, 128-byte swizzle.
 int encode_cache_map(CUtensorMap* map, const void* base, const B200PagedAttentionParams* p) {
-  auto enc = tensor_map_encoder();
-  if (!enc) return fail(B200_ERR_CUDA, "PagedAttention: cuTensorMapEncodeTiled is unavailable");
-  const int elem = 2;
-  cuuint64_t dims[3] = {(cuuint64_t)p->head_size, (cuuint64_t)p->kv_num_heads,
-                        (cuuint64_t)p->num_blocks * (cuuint64_t)p->block_size};
-  cuuint64_t strides[2] = {(cuuint64_t)p->head_size * elem, (cuuint64_t)p->kv_num_heads * p->head_size * elem};
-  cuuint32_t box[3] = {64, 1, (cuuint32_t)b200::kTile};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUtensorMapDataType dt = p->act_dtype == B200_DTYPE_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const uint64_t dims[3] = {(uint64_t)p->head_size, (uint64_t)p->kv_num_heads,
+                            (uint64_t)p->num_blocks * (uint64_t)p->block_size};
+  const uint64_t strides[2] = {(uint64_t)p->head_size * 2, (uint64_t)p->kv_num_heads * p->head_size * 2};
+  const uint32_t box[3] = {64, 1, (uint32_t)b200::kTile};
+  int r = b200::encode_tensor_map(map, p->act_dtype == B200_DTYPE_BFLOAT16, 3, base, dims, strides, box);
   if (r != CUDA_SUCCESS)
-    return fail(B200_ERR_CUDA, "PagedAttention: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return fail(B200_ERR_CUDA, "PagedAttention: cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
   return B200_OK;
 }
 
@@ -347,6 +332,26 @@ int run_prologue(const B200PagedAttentionParams* p, const Layout& L, cudaStream_
 }
 
 }  // namespace
+
+namespace b200 {
+int encode_tensor_map(CUtensorMap* map, bool bf16, int rank, const void* base, const uint64_t* dims,
+                      const uint64_t* strides, const uint32_t* box) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return CUDA_ERROR_NOT_SUPPORTED;
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i > 0) st[i - 1] = strides[i - 1];
+  }
+  return (int)enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank,
+                  const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+}  // namespace b200
 
 extern "C" {
 
@@ -450,13 +455,12 @@ int b200_paged_attention(const B200PagedAttentionParams* p, void* stream_ptr) {
     b200::DecodePlan plan{};
     b200::DecodeMaps maps;
     if (L.fast_decode) {
-      plan.n_units = reinterpret_cast<int*>(ws + L.n_units);
-      plan.units = reinterpret_cast<int2*>(ws + L.units);
-      plan.seq_nsplit = reinterpret_cast<int*>(ws + L.seq_nsplit);
-      plan.seq_part_off = reinterpret_cast<int*>(ws + L.seq_part_off);
-      plan.partials = reinterpret_cast<float*>(ws + L.partials);
-      plan.max_items = L.max_items;
-      plan.tiles_per_split = L.tiles_per_split;
+      plan.total_tiles = reinterpret_cast<int64_t*>(ws + L.total_tiles);
+      plan.seq_tile_off = reinterpret_cast<int*>(ws + L.seq_tile_off);
+      plan.done = reinterpret_cast<int*>(ws + L.done);
+      plan.part_o = reinterpret_cast<float*>(ws + L.part_o);
+      plan.part_ml = reinterpret_cast<float*>(ws + L.part_ml);
+      plan.min_tiles_per_warp = L.min_tiles_per_warp;
       if ((rc = encode_cache_map(&maps.k_map, p->key_cache, p))) return rc;
       if ((rc = encode_cache_map(&maps.v_map, p->value_cache, p))) return rc;
       // First launch of the call: clears the status word, then plans the decode units.
@@ -476,7 +480,7 @@ int b200_paged_attention(const B200PagedAttentionParams* p, void* stream_ptr) {
     if (L.fast_decode) {
       cudaError_t e = b200::launch_decode(a, plan, maps, device_sm_count(p), stream);
       if (e != cudaSuccess) return cuda_fail(e, "paged_decode_kernel");
-      count_launches(2);
+      count_launches(1);
       a.skip_decode = 1;
       if (host_meta) {
         any_generic = false;
@@ -502,6 +506,21 @@ int b200_paged_attention(const B200PagedAttentionParams* p, void* stream_ptr) {
   } catch (...) {
     return fail(B200_ERR_FAIL, "PagedAttention: unknown failure");
   }
+}
+
+int b200_selftest_tcgen05(int32_t dtype, const void* a, const void* b, const void* v, float* c_qk, float* c_pv,
+                          int32_t* device_status, void* stream) {
+  if (!a || !b || !v || !c_qk || !c_pv || !device_status)
+    return fail(B200_ERR_INVALID_ARGUMENT, "selftest: null pointer");
+  if (dtype != B200_DTYPE_FLOAT16 && dtype != B200_DTYPE_BFLOAT16)
+    return fail(B200_ERR_INVALID_ARGUMENT, "selftest: dtype must be FLOAT16 or BFLOAT16");
+  int cu = 0;
+  cudaError_t e = b200::launch_tc_selftest(dtype == B200_DTYPE_BFLOAT16, a, b, v, c_qk, c_pv, device_status,
+                                           static_cast<cudaStream_t>(stream), &cu);
+  if (cu) return fail(B200_ERR_CUDA, "selftest: cuTensorMapEncodeTiled failed (" + std::to_string(cu) + ")");
+  if (e != cudaSuccess) return cuda_fail(e, "tc_selftest_kernel");
+  count_launches(1);
+  return B200_OK;
 }
 
 int b200_read_status(const B200PagedAttentionParams* p, void* stream_ptr) {

@@ -8,13 +8,14 @@
 // paged_attention.rs:52-61).
 //
 // B200 design (one launch for the whole ragged batch, not one per sequence):
-//  * decode_plan_kernel (1 CTA) turns cum/past into a device work list of units
-//    (sequence, split) x kv-head, each covering up to `tiles_per_split` 16-token tiles;
-//  * paged_decode_kernel is persistent (grid = SMs x resident CTAs).  A unit is processed by 4
-//    warps that take the unit's tiles round-robin.  Each warp owns a private STAGES-deep ring
-//    of shared-memory stages filled by TMA (cp.async.bulk.tensor.3d, 128-byte swizzle, no
-//    multicast) from the [NB*bs, KV, d] cache view: a 16-token tile of one kv head is one
-//    box per 64 channels for K and for V, completion tracked by an mbarrier;
+//  * decode_plan_kernel (1 CTA) lays the work out as one stream of 16-token tiles:
+//    for each decode sequence, for each kv head, its tiles (prefix offsets per sequence);
+//  * paged_decode_kernel is persistent (grid = SMs x resident CTAs) and every warp owns an
+//    equal contiguous range of that stream (stream-K: exact balance for ragged lengths, no
+//    scheduling atomics).  A warp streams its tiles through a private STAGES-deep ring of
+//    shared-memory stages filled by TMA (cp.async.bulk.tensor.3d, 128-byte swizzle, no
+//    multicast) from the [NB*bs, KV, d] cache view; the lookahead runs across (sequence, kv
+//    head) boundaries, so the ring never drains;
 //  * the g = H/KV query heads of a kv head (times the unit's queries, <= 8 rows) are batched
 //    into one tensor-core tile: S^T[16 tok x 8 rows] = K_tile[16 x d] . Q^T via
 //    mma.m16n8k16 (K from ldmatrix, Q fragments in registers), so every K/V byte is read once
@@ -22,14 +23,16 @@
 //  * online softmax on the accumulator fragments (exp2 domain), P^T moved into the B operand
 //    with movmatrix.trans, O^T[d x 8 rows] += V_tile^T . P^T with ldmatrix.trans; P is carried
 //    as a hi + lo pair of 16-bit values so the PV product keeps ~16 mantissa bits;
-//  * the 4 warps merge in shared memory; a unit that covers its whole sequence writes the
-//    output, otherwise an fp32 partial (m, l, o) that decode_combine_kernel reduces.
+//  * a (sequence, kv head) segment that lies inside one warp's range is written directly;
+//    a segment cut by range boundaries leaves one fp32 partial (m, l, o) per warp, and the last
+//    warp to finish it merges them (fused split-K combine, no extra launch).  A warp writes at
+//    most two partials, so partial storage is 2 x 8 rows per warp.
 #include "b200_common.cuh"
 #include "b200_kernels.h"
 
 namespace b200 {
 
-constexpr int kDecodeWarps = 4;
+constexpr int kDecodeWarps = kDecodeWarpsPerCta;
 constexpr float kLog2e = 1.4426950408889634f;
 
 bool decode_supported(int head_size, int block_size, int act_dtype, int cache_dtype) {
@@ -38,7 +41,7 @@ bool decode_supported(int head_size, int block_size, int act_dtype, int cache_dt
 }
 
 // ---------------------------------------------------------------------------------------
-// Plan: one CTA scans the sequences (chunks of 1024) and emits the unit list.
+// Plan: one CTA scans the sequences (chunks of blockDim) and writes the tile-stream offsets.
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -66,39 +69,35 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int& 
   return before;
 }
 
+// 16-token tiles of sequence b per kv head if it is on the decode path, else 0.
+__device__ __forceinline__ int decode_tiles(const AttnArgs& a, int b) {
+  const int c0 = a.cum[b], c1 = a.cum[b + 1], nq = c1 - c0, past = a.past[b];
+  const int64_t total = (int64_t)past + nq;
+  if (c0 >= 0 && c1 <= a.num_tokens && nq >= 1 && nq * a.group <= kDecodeRows && past >= 0 &&
+      total <= (int64_t)a.max_blocks * a.block_size)
+    return (int)((total + kTile - 1) / kTile);
+  return 0;
+}
+
 __global__ void __launch_bounds__(1024) decode_plan_kernel(AttnArgs a, DecodePlan plan) {
   __shared__ int warp_sums[32];
   if (threadIdx.x == 0 && a.status) *a.status = 0;  // first kernel of every call clears status
-  int carry_items = 0, carry_rows = 0;
-  const int P = plan.tiles_per_split;
+  int carry = 0;
   for (int base = 0; base < a.batch; base += blockDim.x) {
-    int b = base + threadIdx.x;
-    int ns = 0, rows = 0;
+    const int b = base + threadIdx.x;
+    const int tiles = b < a.batch ? decode_tiles(a, b) : 0;
+    int tot;
+    const int off = block_exclusive_scan(tiles, warp_sums, tot);
     if (b < a.batch) {
-      int c0 = a.cum[b], c1 = a.cum[b + 1], nq = c1 - c0, past = a.past[b];
-      int64_t total = (int64_t)past + nq;
-      if (c0 >= 0 && c1 <= a.num_tokens && nq >= 1 && nq * a.group <= kDecodeRows && past >= 0 &&
-          total <= (int64_t)a.max_blocks * a.block_size) {
-        int tiles = (int)((total + kTile - 1) / kTile);
-        ns = (tiles + P - 1) / P;
-        rows = nq * a.group;
-      }
+      plan.seq_tile_off[b] = carry + off;
+      for (int kh = 0; kh < a.kv_heads; ++kh) plan.done[(int64_t)b * a.kv_heads + kh] = 0;
     }
-    int total_items, total_rows;
-    int item_off = block_exclusive_scan(ns, warp_sums, total_items);
-    int row_off = block_exclusive_scan(ns * rows * a.kv_heads, warp_sums, total_rows);
-    if (b < a.batch) {
-      plan.seq_nsplit[b] = ns;
-      plan.seq_part_off[b] = carry_rows + row_off;
-      for (int s = 0; s < ns; ++s) {
-        int idx = carry_items + item_off + s;
-        if (idx < plan.max_items) plan.units[idx] = make_int2(b, s);
-      }
-    }
-    carry_items += total_items;
-    carry_rows += total_rows;
+    carry += tot;
   }
-  if (threadIdx.x == 0) *plan.n_units = min(carry_items, plan.max_items);
+  if (threadIdx.x == 0) {
+    plan.seq_tile_off[a.batch] = carry;
+    *plan.total_tiles = (int64_t)carry * a.kv_heads;
+  }
 }
 
 // ---------------------------------------------------------------------------------------
@@ -119,6 +118,17 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return (uint32_t)(box * (kTile * 128) + row * 128 + ((c ^ (row & 7)) << 4));
 }
 
+// A piece of one (sequence, kv head) segment of the tile stream, as a warp sees it.
+struct Piece {
+  int valid, b, kh, t0, t1, tiles, c0, nq, past, total;
+  int64_t seg_start;  // stream index of the segment's first tile
+};
+
+// Stream layout: for each decode sequence b (in order), for each kv head, its tiles; sequence b
+// starts at seq_tile_off[b] * KV.  Warp g of W owns stream range [g*T/W, (g+1)*T/W).
+__device__ __forceinline__ int64_t range_start(int64_t g, int64_t T, int64_t W) { return g * T / W; }
+__device__ __forceinline__ int64_t warp_of(int64_t x, int64_t T, int64_t W) { return ((x + 1) * W + T - 1) / T - 1; }
+
 template <typename T, int D, int STAGES>
 __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant__ AttnArgs a,
                                                            const __grid_constant__ DecodeMaps maps,
@@ -126,47 +136,133 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
   using L = DecodeLayout<D>;
   using MMA = mma_op<T>;
   constexpr int KSTEPS = D / 16;
+  constexpr int RING = STAGES + 1;  // pieces live at once: one per in-flight tile + the newest
   extern __shared__ uint8_t dyn_smem[];
   __shared__ __align__(8) uint64_t bars[kDecodeWarps][STAGES];
+  __shared__ Piece ring[kDecodeWarps][RING];
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* wbase = smem + warp * STAGES * L::kStageBytes;
   const uint32_t wbase_u32 = smem_u32(wbase);
+  Piece* myring = ring[warp];
+
+  const int KV = a.kv_heads, g = a.group, H = a.num_heads;
+  const int64_t Ttot = *plan.total_tiles;
+  const int64_t Wmax = (int64_t)gridDim.x * kDecodeWarps;
+  const int64_t W = max((int64_t)1, min(Wmax, (Ttot + plan.min_tiles_per_warp - 1) / plan.min_tiles_per_warp));
+  const int64_t gw = (int64_t)blockIdx.x * kDecodeWarps + warp;
+  if (Ttot == 0 || gw >= W) return;
+  const int64_t r0 = range_start(gw, Ttot, W), r1 = range_start(gw + 1, Ttot, W);
+  if (r0 >= r1) return;
 
   if (lane == 0) {
     for (int s = 0; s < STAGES; ++s) mbar_init(&bars[warp][s], 1);
     fence_mbar_init();
   }
   __syncwarp();
-  uint32_t phase = 0;    // bit s: parity of the next completion of stage s
-  uint32_t pending = 0;  // bit s: a load into stage s has been issued and not yet waited on
-  bool failed = false;
-
-  const int KV = a.kv_heads, g = a.group, H = a.num_heads;
-  const int P = plan.tiles_per_split;
-  const int n_units = *plan.n_units * KV;
   const float qk_scale = a.softcap > 0.f ? a.scale : a.scale * kLog2e;
 
-  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-    const int2 it = plan.units[u / KV];
-    const int kh = u % KV;
-    const int b = it.x, split = it.y;
-    const int c0 = a.cum[b], nq = a.cum[b + 1] - c0, past = a.past[b];
-    const int total = past + nq;
-    const int tiles = (total + kTile - 1) / kTile;
-    const int t0 = split * P, t1 = min(t0 + P, tiles);
-    const int rows = nq * g;
-    const int32_t* bt = a.block_table + (int64_t)b * a.max_blocks;
-    const int n_my = t1 - t0 > warp ? (t1 - t0 - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
+  // Piece of the stream starting at position x (< r1) into ring slot `slot` (all lanes).
+  auto locate = [&](int slot, int64_t x) {
+    Piece p{};
+    if (x < r1) {
+      int lo = 0, hi = a.batch - 1;  // largest b with seq_tile_off[b] * KV <= x
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if ((int64_t)plan.seq_tile_off[mid] * KV <= x) lo = mid; else hi = mid - 1;
+      }
+      const int b = lo;
+      const int64_t sb = (int64_t)plan.seq_tile_off[b] * KV;
+      const int tb = plan.seq_tile_off[b + 1] - plan.seq_tile_off[b];
+      if (tb > 0) {
+        const int64_t rel = x - sb;
+        p.valid = 1;
+        p.b = b;
+        p.kh = (int)(rel / tb);
+        p.tiles = tb;
+        p.t0 = (int)(rel % tb);
+        p.t1 = (int)min((int64_t)tb, p.t0 + (r1 - x));
+        p.seg_start = sb + (int64_t)p.kh * tb;
+        p.c0 = a.cum[b];
+        p.nq = a.cum[b + 1] - p.c0;
+        p.past = a.past[b];
+        p.total = p.past + p.nq;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) myring[slot] = p;
+    __syncwarp();
+  };
 
-    // Q^T B-fragments: column n = lane/4 is q row r = (query i, head-in-group); k pairs.
+  // Issue the TMA loads of tile t of the piece in ring slot `slot` into stage s (lane 0).
+  auto issue = [&](int s, int slot, int t) {
+    if (lane != 0) return;
+    const Piece& u = myring[slot];
+    const int pos0 = t * kTile;
+    const int32_t blk = a.block_table[(int64_t)u.b * a.max_blocks + pos0 / a.block_size];
+    uint64_t* bar = &bars[warp][s];
+    if (blk < 0 || blk >= a.num_blocks) {
+      set_status(a.status, kStatusBadBlock);
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+      return;
+    }
+    const int z = blk * a.block_size + pos0 % a.block_size;
+    uint8_t* kdst = wbase + s * L::kStageBytes;
+    uint8_t* vdst = kdst + L::kTileBytes;
+    mbar_arrive_expect_tx(bar, L::kStageBytes);
+#pragma unroll
+    for (int h = 0; h < L::kBoxes; ++h) {
+      tma_load_3d(kdst + h * L::kBoxBytes, &maps.k_map, bar, h * 64, u.kh, z);
+      tma_load_3d(vdst + h * L::kBoxBytes, &maps.v_map, bar, h * 64, u.kh, z);
+    }
+  };
+
+  // Producer: ring slot ps, next tile pt of that piece.  The lookahead runs across pieces.
+  int ps = 0, pt = 0;
+  locate(0, r0);
+  bool producing = myring[0].valid != 0;
+  if (producing) pt = myring[0].t0;
+  uint32_t phase = 0, pending = 0;
+  int issued = 0, consumed = 0;
+  bool failed = false;
+
+  auto produce = [&]() {
+    while (producing && pt >= myring[ps].t1) {
+      const int64_t next = myring[ps].seg_start + myring[ps].t1;
+      ps = (ps + 1) % RING;
+      locate(ps, next);
+      producing = myring[ps].valid != 0;
+      if (producing) pt = myring[ps].t0;
+    }
+    if (!producing) return;
+    const int s = issued % STAGES;
+    issue(s, ps, pt);
+    pending |= 1u << s;
+    ++pt;
+    ++issued;
+  };
+
+  for (int i = 0; i < STAGES; ++i) produce();
+  __syncwarp();
+
+  int cs = 0;
+  int ct = myring[0].t0;
+  const int col0 = (lane & 3) * 2;  // q rows held by this lane: col0, col0 + 1
+
+  while (consumed < issued && !failed) {
+    const Piece u = myring[cs];
+    const int rows = u.nq * g;
+    const int qi0 = col0 / g, qi1 = (col0 + 1) / g;
+
+    // Q^T B-fragments: column n = lane/4 is q row r = (query i, head-in-group).
     uint32_t qf[KSTEPS][2];
     {
       const int r = lane >> 2, kq = (lane & 3) * 2;
       if (r < rows) {
         const int qi = r / g, hl = r % g;
-        const T* qrow = reinterpret_cast<const T*>(a.q) + (int64_t)(c0 + qi) * a.q_stride + (int64_t)(kh * g + hl) * D;
+        const T* qrow =
+            reinterpret_cast<const T*>(a.q) + (int64_t)(u.c0 + qi) * a.q_stride + (int64_t)(u.kh * g + hl) * D;
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; ++kk) {
           qf[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + kq);
@@ -178,54 +274,18 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
       }
     }
 
-    // Issue the TMA loads of my j-th tile into stage j % STAGES (lane 0 only).
-    auto issue = [&](int j) {
-      const int s = j % STAGES;
-      const int t = t0 + warp + kDecodeWarps * j;
-      const int pos0 = t * kTile;
-      const int32_t blk = bt[pos0 / a.block_size];
-      uint64_t* bar = &bars[warp][s];
-      if (blk < 0 || blk >= a.num_blocks) {
-        set_status(a.status, kStatusBadBlock);
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-        return;
-      }
-      const int z = blk * a.block_size + pos0 % a.block_size;
-      uint8_t* kdst = wbase + s * L::kStageBytes;
-      uint8_t* vdst = kdst + L::kTileBytes;
-      mbar_arrive_expect_tx(bar, L::kStageBytes);
-#pragma unroll
-      for (int h = 0; h < L::kBoxes; ++h) {
-        tma_load_3d(kdst + h * L::kBoxBytes, &maps.k_map, bar, h * 64, kh, z);
-        tma_load_3d(vdst + h * L::kBoxBytes, &maps.v_map, bar, h * 64, kh, z);
-      }
-    };
-
-    if (!failed) {
-      for (int j = 0; j < min(STAGES, n_my); ++j) {
-        if (lane == 0) issue(j);
-        pending |= 1u << (j % STAGES);
-      }
-    }
-    __syncwarp();
-
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float o[KSTEPS][4];
 #pragma unroll
     for (int mt = 0; mt < KSTEPS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
 
-    const int col0 = (lane & 3) * 2;          // q rows held by this lane: col0, col0 + 1
-    const int qi0 = col0 / g, qi1 = (col0 + 1) / g;
-
-    for (int j = 0; j < n_my && !failed; ++j) {
-      const int s = j % STAGES;
-      const int t = t0 + warp + kDecodeWarps * j;
-      const int pos0 = t * kTile;
+    for (; ct < u.t1; ++ct) {
+      const int s = consumed % STAGES;
+      const int pos0 = ct * kTile;
       if (!mbar_wait(&bars[warp][s], (phase >> s) & 1u)) {
         if (lane == 0) set_status(a.status, kStatusTimeout);
         failed = true;
-        // Give the loads still in flight into this warp's stages one more bounded wait
-        // before the shared memory is reused, then stop issuing.
+        // One more bounded wait for the loads still in flight before the warp stops.
         for (int s2 = 0; s2 < STAGES; ++s2)
           if ((pending >> s2) & 1u) mbar_wait(&bars[warp][s2], (phase >> s2) & 1u);
         pending = 0;
@@ -233,39 +293,45 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
       }
       phase ^= 1u << s;
       pending &= ~(1u << s);
-      const int32_t blk = bt[pos0 / a.block_size];
+      const int32_t blk = a.block_table[(int64_t)u.b * a.max_blocks + pos0 / a.block_size];
       const bool blk_ok = blk >= 0 && blk < a.num_blocks;
       const uint32_t kbase = wbase_u32 + s * L::kStageBytes;
       const uint32_t vbase = kbase + L::kTileBytes;
 
       // Overlay: tile rows at positions >= past hold the sequence's own new K/V rows.
-      const bool overlay = pos0 + kTile > past;
+      const bool overlay = pos0 + kTile > u.past;
       if (overlay) {
         constexpr int CH = D / 8;  // 16-byte chunks per row
         for (int idx = lane; idx < kTile * CH; idx += 32) {
           const int row = idx / CH, chunk = idx % CH;
           const int pos = pos0 + row;
-          if (pos < past || pos >= total) continue;
-          const int64_t tok = c0 + (pos - past);
-          const uint4 kv = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) + tok * a.k_stride + (int64_t)kh * D + chunk * 8);
-          const uint4 vv = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) + tok * a.v_stride + (int64_t)kh * D + chunk * 8);
+          if (pos < u.past || pos >= u.total) continue;
+          const int64_t tok = u.c0 + (pos - u.past);
+          const uint4 kv = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) + tok * a.k_stride +
+                                                           (int64_t)u.kh * D + chunk * 8);
+          const uint4 vv = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) + tok * a.v_stride +
+                                                           (int64_t)u.kh * D + chunk * 8);
           *reinterpret_cast<uint4*>(wbase + (kbase - wbase_u32) + swz(row, chunk)) = kv;
           *reinterpret_cast<uint4*>(wbase + (vbase - wbase_u32) + swz(row, chunk)) = vv;
         }
         __syncwarp();
       }
 
-      // S^T = K_tile . Q^T
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      // S^T = K_tile . Q^T (two accumulators halve the dependent MMA chain)
+      float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
       {
         const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
         const int half = lane >> 4;
 #pragma unroll
-        for (int kk = 0; kk < KSTEPS; ++kk) {
-          uint32_t af[4];
+        for (int kk = 0; kk < KSTEPS; kk += 2) {
+          uint32_t af[4], bf[4];
           ldsm_x4(kbase + swz(row, kk * 2 + half), af[0], af[1], af[2], af[3]);
+          ldsm_x4(kbase + swz(row, kk * 2 + 2 + half), bf[0], bf[1], bf[2], bf[3]);
           MMA::run(c, af, qf[kk][0], qf[kk][1]);
+          MMA::run(c2, bf, qf[kk + 1][0], qf[kk + 1][1]);
         }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) c[e] += c2[e];
       }
 
       // Masks, scale (log2 domain), online softmax per q-row column.
@@ -276,9 +342,9 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
         const int col = col0 + (e & 1);
         const int qi = (e & 1) ? qi1 : qi0;
         const int pos = pos0 + tok;
-        bool vis = blk_ok && col < rows && pos < total;
-        if (a.is_causal) vis = vis && pos <= past + qi;
-        if (a.window > 0) vis = vis && pos >= past + qi - a.window + 1;
+        bool vis = blk_ok && col < rows && pos < u.total;
+        if (a.is_causal) vis = vis && pos <= u.past + qi;
+        if (a.window > 0) vis = vis && pos >= u.past + qi - a.window + 1;
         float x = c[e] * qk_scale;
         if (a.softcap > 0.f) x = a.softcap * tanhf(x / a.softcap) * kLog2e;
         sc[e] = vis ? x : -INFINITY;
@@ -325,107 +391,120 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
       }
       __syncwarp();
       if (overlay) fence_proxy_async_smem();
-      if (j + STAGES < n_my) {
-        if (lane == 0) issue(j + STAGES);
-        pending |= 1u << s;
-      }
+      ++consumed;
+      produce();  // refill the stage just freed (possibly with the next piece's first tile)
       __syncwarp();
     }
+    if (failed) break;
 
-    // Column sums of l across the 8 lanes that share a column.
+    // ---- finish the piece: column sums of l, then output or partial (+ fused combine)
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
       l0 += __shfl_xor_sync(0xffffffffu, l0, off);
       l1 += __shfl_xor_sync(0xffffffffu, l1, off);
     }
-
-    // Merge the 4 warps through shared memory (stage buffers are idle now).
-    __syncthreads();
-    float* mo = reinterpret_cast<float*>(smem);                  // [4][8][D]
-    float* mm = mo + kDecodeWarps * kDecodeRows * D;             // [4][8]
-    float* ml = mm + kDecodeWarps * kDecodeRows;                 // [4][8]
-    if (lane < 4) {
-      mm[warp * kDecodeRows + col0] = m0; mm[warp * kDecodeRows + col0 + 1] = m1;
-      ml[warp * kDecodeRows + col0] = l0; ml[warp * kDecodeRows + col0 + 1] = l1;
-    }
-    {
-      float* ow = mo + warp * kDecodeRows * D;
-      const int dr = lane >> 2;
+    const int dr = lane >> 2;
+    if (u.t0 == 0 && u.t1 == u.tiles) {
+      // Whole segment in this warp: normalise and write the output rows.
 #pragma unroll
-      for (int mt = 0; mt < KSTEPS; ++mt) {
-        ow[col0 * D + mt * 16 + dr] = o[mt][0];
-        ow[(col0 + 1) * D + mt * 16 + dr] = o[mt][1];
-        ow[col0 * D + mt * 16 + dr + 8] = o[mt][2];
-        ow[(col0 + 1) * D + mt * 16 + dr + 8] = o[mt][3];
-      }
-    }
-    __syncthreads();
-    const int nsplit = plan.seq_nsplit[b];
-    for (int idx = threadIdx.x; idx < rows * D; idx += blockDim.x) {
-      const int r = idx / D, d = idx % D;
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < kDecodeWarps; ++w) M = fmaxf(M, mm[w * kDecodeRows + r]);
-      float Lsum = 0.f, Osum = 0.f;
-#pragma unroll
-      for (int w = 0; w < kDecodeWarps; ++w) {
-        const float mw = mm[w * kDecodeRows + r];
-        const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
-        Lsum += ml[w * kDecodeRows + r] * f;
-        Osum += mo[(w * kDecodeRows + r) * D + d] * f;
-      }
-      const int qi = r / g, hl = r % g;
-      if (nsplit == 1) {
+      for (int e = 0; e < 2; ++e) {
+        const int r = col0 + e;
+        if (r >= rows) continue;
+        float M = e ? m1 : m0, Ls = e ? l1 : l0, f = 1.f;
+        const int qi = r / g, hl = r % g;
         if (a.head_sink) {
-          const float sink = load_act(a.head_sink, kh * g + hl, a.act_dtype) * kLog2e;
+          const float sink = load_act(a.head_sink, u.kh * g + hl, a.act_dtype) * kLog2e;
           const float M2 = fmaxf(M, sink);
-          const float f = M == -INFINITY ? 0.f : exp2f(M - M2);
-          Lsum = Lsum * f + exp2f(sink - M2);
-          Osum *= f;
+          f = M == -INFINITY ? 0.f : exp2f(M - M2);
+          Ls = Ls * f + exp2f(sink - M2);
         }
-        const float y = Lsum > 0.f ? Osum / Lsum : 0.f;
-        store_act(a.out, (int64_t)(c0 + qi) * H * D + (int64_t)(kh * g + hl) * D + d, y, a.act_dtype);
-      } else {
-        const int64_t pr = plan.seq_part_off[b] + ((int64_t)split * KV + kh) * rows + r;
-        float* part = plan.partials + pr * (D + 2);
-        part[2 + d] = Osum;
-        if (d == 0) { part[0] = M; part[1] = Lsum; }
+        const float inv = Ls > 0.f ? f / Ls : 0.f;
+        T* orow = reinterpret_cast<T*>(a.out) + (int64_t)(u.c0 + qi) * H * D + (int64_t)(u.kh * g + hl) * D;
+#pragma unroll
+        for (int mt = 0; mt < KSTEPS; ++mt) {
+          store_act(orow, mt * 16 + dr, o[mt][e] * inv, a.act_dtype);
+          store_act(orow, mt * 16 + dr + 8, o[mt][e + 2] * inv, a.act_dtype);
+        }
+      }
+    } else {
+      // Partial: slot 0 holds the warp's first piece, slot 1 its last (split) piece.
+      const int64_t piece_start = u.seg_start + u.t0;
+      const int slot = piece_start == r0 ? 0 : 1;
+      const int64_t prow = (gw * 2 + slot) * kDecodeRows;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int r = col0 + e;
+        if (r >= rows) continue;
+        float* po = plan.part_o + (prow + r) * D;
+        if (dr == 0) {
+          plan.part_ml[(prow + r) * 2] = e ? m1 : m0;
+          plan.part_ml[(prow + r) * 2 + 1] = e ? l1 : l0;
+        }
+#pragma unroll
+        for (int mt = 0; mt < KSTEPS; ++mt) {
+          po[mt * 16 + dr] = o[mt][e];
+          po[mt * 16 + dr + 8] = o[mt][e + 2];
+        }
+      }
+      __threadfence();
+      __syncwarp();
+      const int64_t seg_end = u.seg_start + u.tiles;
+      const int64_t w_first = warp_of(u.seg_start, Ttot, W);
+      const int pieces = (int)(warp_of(seg_end - 1, Ttot, W) - w_first + 1);
+      int prior = 0;
+      if (lane == 0) prior = atomicAdd(&plan.done[(int64_t)u.b * KV + u.kh], 1);
+      prior = __shfl_sync(0xffffffffu, prior, 0);
+      if (prior == pieces - 1) {
+        // Last piece of this (sequence, kv head) to finish: merge all pieces.
+        __threadfence();
+        const bool first_is_last_slot = u.seg_start > range_start(w_first, Ttot, W);
+        for (int r = 0; r < rows; ++r) {
+          float mloc = -INFINITY;
+          for (int pc = lane; pc < pieces; pc += 32) {
+            const int64_t row = ((w_first + pc) * 2 + (pc == 0 && first_is_last_slot ? 1 : 0)) * kDecodeRows + r;
+            mloc = fmaxf(mloc, __ldcg(plan.part_ml + row * 2));
+          }
+#pragma unroll
+          for (int off = 16; off; off >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, off));
+          const float M = mloc;
+          float lloc = 0.f;
+          for (int pc = lane; pc < pieces; pc += 32) {
+            const int64_t row = ((w_first + pc) * 2 + (pc == 0 && first_is_last_slot ? 1 : 0)) * kDecodeRows + r;
+            const float mp = __ldcg(plan.part_ml + row * 2);
+            lloc += mp == -INFINITY ? 0.f : __ldcg(plan.part_ml + row * 2 + 1) * exp2f(mp - M);
+          }
+#pragma unroll
+          for (int off = 16; off; off >>= 1) lloc += __shfl_xor_sync(0xffffffffu, lloc, off);
+          float Lsum = lloc, fo = 1.f;
+          const int qi = r / g, hl = r % g;
+          if (a.head_sink) {
+            const float sink = load_act(a.head_sink, u.kh * g + hl, a.act_dtype) * kLog2e;
+            const float M2 = fmaxf(M, sink);
+            fo = M == -INFINITY ? 0.f : exp2f(M - M2);
+            Lsum = Lsum * fo + exp2f(sink - M2);
+          }
+          const float inv = Lsum > 0.f ? fo / Lsum : 0.f;
+          T* orow = reinterpret_cast<T*>(a.out) + (int64_t)(u.c0 + qi) * H * D + (int64_t)(u.kh * g + hl) * D;
+          for (int d4 = lane; d4 < D / 4; d4 += 32) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int pc = 0; pc < pieces; ++pc) {
+              const int64_t row = ((w_first + pc) * 2 + (pc == 0 && first_is_last_slot ? 1 : 0)) * kDecodeRows + r;
+              const float mp = __ldcg(plan.part_ml + row * 2);
+              const float f = mp == -INFINITY ? 0.f : exp2f(mp - M);
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(plan.part_o + row * D) + d4);
+              acc.x += f * v.x; acc.y += f * v.y; acc.z += f * v.z; acc.w += f * v.w;
+            }
+            store_act(orow, d4 * 4 + 0, acc.x * inv, a.act_dtype);
+            store_act(orow, d4 * 4 + 1, acc.y * inv, a.act_dtype);
+            store_act(orow, d4 * 4 + 2, acc.z * inv, a.act_dtype);
+            store_act(orow, d4 * 4 + 3, acc.w * inv, a.act_dtype);
+          }
+        }
       }
     }
-    __syncthreads();
-  }
-}
-
-// Reduce the split partials of every (sequence, kv head) with more than one split.
-__global__ void __launch_bounds__(128) decode_combine_kernel(AttnArgs a, DecodePlan plan) {
-  const int b = blockIdx.x, kh = blockIdx.y;
-  const int ns = plan.seq_nsplit[b];
-  if (ns <= 1) return;
-  const int D = a.head_size, KV = a.kv_heads, g = a.group, H = a.num_heads;
-  const int c0 = a.cum[b], nq = a.cum[b + 1] - c0;
-  const int rows = nq * g;
-  const int64_t base = plan.seq_part_off[b];
-  for (int idx = threadIdx.x; idx < rows * D; idx += blockDim.x) {
-    const int r = idx / D, d = idx % D;
-    float M = -INFINITY;
-    for (int s = 0; s < ns; ++s) M = fmaxf(M, plan.partials[(base + ((int64_t)s * KV + kh) * rows + r) * (D + 2)]);
-    float Lsum = 0.f, Osum = 0.f;
-    for (int s = 0; s < ns; ++s) {
-      const float* part = plan.partials + (base + ((int64_t)s * KV + kh) * rows + r) * (D + 2);
-      const float f = part[0] == -INFINITY ? 0.f : exp2f(part[0] - M);
-      Lsum += part[1] * f;
-      Osum += part[2 + d] * f;
-    }
-    const int qi = r / g, hl = r % g;
-    if (a.head_sink) {
-      const float sink = load_act(a.head_sink, kh * g + hl, a.act_dtype) * kLog2e;
-      const float M2 = fmaxf(M, sink);
-      const float f = M == -INFINITY ? 0.f : exp2f(M - M2);
-      Lsum = Lsum * f + exp2f(sink - M2);
-      Osum *= f;
-    }
-    const float y = Lsum > 0.f ? Osum / Lsum : 0.f;
-    store_act(a.out, (int64_t)(c0 + qi) * H * D + (int64_t)(kh * g + hl) * D + d, y, a.act_dtype);
+    // next consumer piece
+    cs = (cs + 1) % RING;
+    ct = myring[cs].t0;
   }
 }
 
@@ -436,9 +515,7 @@ template <typename T, int D, int STAGES>
 static cudaError_t launch_decode_t(const AttnArgs& a, const DecodePlan& plan, const DecodeMaps& maps, int num_sms,
                                    cudaStream_t stream) {
   using L = DecodeLayout<D>;
-  constexpr size_t stage_smem = (size_t)kDecodeWarps * STAGES * L::kStageBytes;
-  constexpr size_t merge_smem = sizeof(float) * (size_t)kDecodeWarps * kDecodeRows * (D + 2);
-  constexpr size_t smem = (stage_smem > merge_smem ? stage_smem : merge_smem) + 1024;
+  constexpr size_t smem = (size_t)kDecodeWarps * STAGES * L::kStageBytes + 1024;
   static int occupancy[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -450,10 +527,9 @@ static cudaError_t launch_decode_t(const AttnArgs& a, const DecodePlan& plan, co
     int occ = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, paged_decode_kernel<T, D, STAGES>, 128, smem);
     if (e != cudaSuccess) return e;
-    occupancy[dev] = occ > 0 ? occ : 1;
+    occupancy[dev] = occ < 1 ? 1 : (occ > kDecodeMaxCtasPerSm ? kDecodeMaxCtasPerSm : occ);
   }
   paged_decode_kernel<T, D, STAGES><<<num_sms * occupancy[dev], 128, smem, stream>>>(a, maps, plan);
-  decode_combine_kernel<<<dim3(a.batch, a.kv_heads), 128, 0, stream>>>(a, plan);
   return cudaGetLastError();
 }
 

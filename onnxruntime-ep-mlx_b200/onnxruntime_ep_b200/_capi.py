@@ -52,7 +52,7 @@ class PagedAttentionParams(ctypes.Structure):
         ("host_cumulative_sequence_length", _vp), ("host_past_seqlens", _vp),
         ("host_block_table", _vp), ("host_slot_mapping", _vp),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t), ("device_status", _vp),
-        ("decode_tiles_per_split", _i32), ("force_generic", _i32), ("num_sms", _i32),
+        ("decode_min_tiles_per_warp", _i32), ("force_generic", _i32), ("num_sms", _i32),
         ("attention_event_begin", _vp), ("attention_event_end", _vp),
     ]
 
@@ -93,6 +93,7 @@ SIGNATURES = {
     "b200_paged_attention": (ctypes.c_int, [ctypes.POINTER(PagedAttentionParams), _vp]),
     "b200_kv_append": (ctypes.c_int, [ctypes.POINTER(PagedAttentionParams), _vp]),
     "b200_read_status": (ctypes.c_int, [ctypes.POINTER(PagedAttentionParams), _vp]),
+    "b200_selftest_tcgen05": (ctypes.c_int, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_paged_attention_claim": (
         ctypes.c_int, [ctypes.POINTER(NodeInfo), ctypes.c_char_p, ctypes.c_size_t]),
 }

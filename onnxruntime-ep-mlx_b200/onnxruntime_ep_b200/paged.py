@@ -63,7 +63,7 @@ def build_params(query, key, value, key_cache, value_cache, cum, past, block_tab
                  q_norm_weight=None, k_norm_weight=None, k_scale=None, v_scale=None, scale=0.0,
                  is_causal=1, local_window_size=-1, softcap=0.0, do_rotary=0, rotary_interleaved=0,
                  rotary_offset=0, qk_norm_epsilon=1e-6, k_quant_type="NONE", v_quant_type="NONE",
-                 output=None, host_metadata=None, tiles_per_split=0, force_generic=False,
+                 output=None, host_metadata=None, min_tiles_per_warp=0, force_generic=False,
                  kv_only=False):
     """Fill a ``B200PagedAttentionParams``.  Returns ``(params, keepalive, output)``."""
     device = key_cache.device
@@ -156,7 +156,7 @@ def build_params(query, key, value, key_cache, value_cache, cum, past, block_tab
         if output is None:
             output = torch.empty((nt, H * d), dtype=query.dtype, device=device)
         p.output = _ptr(output)
-    p.decode_tiles_per_split = int(tiles_per_split)
+    p.decode_min_tiles_per_warp = int(min_tiles_per_warp)
     p.force_generic = int(bool(force_generic))
     nbytes = ctypes.c_size_t(0)
     check(LIB.b200_paged_attention_workspace_size(ctypes.byref(p), ctypes.byref(nbytes)))

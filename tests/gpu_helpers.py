@@ -24,7 +24,7 @@ def to_np(t):
     return t.cpu().numpy()
 
 
-def run_float_case(feeds, H, KV, *, metadata="host", force_generic=False, tiles_per_split=0,
+def run_float_case(feeds, H, KV, *, metadata="host", force_generic=False, min_tiles_per_warp=0,
                    attrs=None, check_status=True):
     """Run one golden float case through ``paged_attention``.  Returns numpy
     ``(output fp32, key_cache, value_cache)``."""
@@ -49,7 +49,7 @@ def run_float_case(feeds, H, KV, *, metadata="host", force_generic=False, tiles_
     out, kc2, vc2 = paged_attention(
         q, k, v, kc, vc, meta["cumulative_sequence_length"], meta["past_seqlens"],
         meta["block_table"], slot_mapping=meta.get("slot_mapping"), num_heads=H,
-        kv_num_heads=KV, force_generic=force_generic, tiles_per_split=tiles_per_split,
+        kv_num_heads=KV, force_generic=force_generic, min_tiles_per_warp=min_tiles_per_warp,
         check_status=check_status, **kw, **attrs)
     torch.cuda.synchronize()
     return out.float().cpu().numpy(), to_np(kc2), to_np(vc2)

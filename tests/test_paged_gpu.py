@@ -174,7 +174,7 @@ def test_bf16_decode_matches_oracle(nq, H, KV, metadata):
 @pytest.mark.parametrize("tiles", [1, 3, 8, 64])
 def test_split_count_does_not_change_results_beyond_rounding(tiles):
     feeds = decode_feeds(99, B=6, H=32, KV=8, D=128, bs=16, lo=1, hi=3000, nb=1400)
-    out, _, _ = run_float_case(feeds, 32, 8, tiles_per_split=tiles)
+    out, _, _ = run_float_case(feeds, 32, 8, min_tiles_per_warp=tiles)
     want, _, _ = oracle_float(feeds, 32, 8)
     assert np.abs(out - want).max() <= 2e-3
 
