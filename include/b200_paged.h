@@ -155,6 +155,19 @@ B200_API int b200_paged_attention(const B200PagedAttentionParams* p, void* strea
  * in-place write-back of engine.rs:1212-1364, without attention.  Uses the same params. */
 B200_API int b200_kv_append(const B200PagedAttentionParams* p, void* stream);
 
+/* PagedAttention with library-owned scratch, for callers that cannot allocate device memory
+ * (a host runtime that passes only the tensors it already owns, a serving loop that forbids
+ * device allocations after start-up, a cgo/JNI binding without a CUDA allocator).  No
+ * counterpart in the reference.  Same inputs, outputs and semantics as b200_paged_attention,
+ * but `workspace` / `workspace_bytes` are ignored: scratch comes from a 32 MiB static device
+ * array that every GPU loading the library keeps until exit.  Calls needing more scratch than
+ * 32 MiB (see b200_paged_attention_workspace_size) fail with B200_ERR_WORKSPACE.  All calls on
+ * a device share the array (each call re-initialises what must start at zero), so calls that
+ * overlap on the GPU race and must be serialised by the caller.  The first call on a device
+ * resolves the array's address (cudaGetSymbolAddress) and should come before any stream
+ * capture.  The call allocates nothing. */
+B200_API int b200_paged_attention_static_scratch(const B200PagedAttentionParams* p, void* stream);
+
 /* Synchronise `stream`, read and clear the device status word of the last call with these
  * params, and turn set bits into B200_ERR_FAIL / B200_ERR_DEVICE with the reference's
  * messages. */

@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace b200 {
 
 // Device status word.  Bit flags, OR-ed by any thread that detects a problem; the host maps
@@ -21,6 +23,9 @@ enum StatusBits : int {
   kStatusBadPosition = 1 << 6,     // RoPE position outside the cos/sin cache
 };
 
+
+// Record `msg` as this thread's b200_last_error() and return `code` (capi.cu).
+int set_error(int code, const std::string& msg);
 
 // KV append / Q-K preprocessing (kv_append.cu).
 struct PrologueArgs {

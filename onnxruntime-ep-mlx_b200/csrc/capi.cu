@@ -334,6 +334,8 @@ int run_prologue(const B200PagedAttentionParams* p, const Layout& L, cudaStream_
 }  // namespace
 
 namespace b200 {
+int set_error(int code, const std::string& msg) { return fail(code, msg); }
+
 int encode_tensor_map(CUtensorMap* map, bool bf16, int rank, const void* base, const uint64_t* dims,
                       const uint64_t* strides, const uint32_t* box) {
   auto enc = tensor_map_encoder();
