@@ -241,7 +241,7 @@ def run_b200(args):
     if KV % n:
         raise SystemExit(f"--gpus {n} must divide the 8 kv heads")
 
-    from onnxruntime_ep_b200 import _capi, paged
+    from onnxruntime_ep_b200 import _capi, paged, sharding
 
     meta = make_metadata(n, args.seqs, args.pool_blocks)
     kvh = KV // n
@@ -272,9 +272,9 @@ def run_b200(args):
     def step():
         _capi.check(_capi.LIB.b200_paged_attention(pp, sp))
         if n > 1:
+            # one NCCL all-gather of the head-sharded outputs, then the head permute
             dist.all_gather_into_tensor(gathered, out)
-            # [N, B, qh*D] -> [B, H*D]: rank r's heads are q heads [r*qh, (r+1)*qh)
-            return gathered.permute(1, 0, 2).reshape(B, H * D)
+            return sharding.reassemble(gathered)
         return out
 
     for _ in range(args.warmup):
