@@ -53,6 +53,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--seqs", type=int, default=B_PER_GPU, help="sequences per GPU (profiling runs use fewer)")
     ap.add_argument("--pool-blocks", type=int, default=NB_PER_GPU, help="KV pool blocks per GPU")
+    ap.add_argument("--mixed-chunks", type=int, default=8, help="mixed workload: prefill chunks")
+    ap.add_argument("--mixed-decode", type=int, default=120, help="mixed workload: decode rows")
+    ap.add_argument("--workload", default="decode", choices=["decode", "mixed"],
+                    help="decode = BASELINE config 3 (the metric); mixed = config 4 (8 x 2048-token "
+                         "prefill chunks + 120 decode rows, 64q/8kv)")
     return ap.parse_args()
 
 
@@ -404,8 +409,95 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def run_mixed(args):
+    """one PagedAttention call over 8 prefill chunks of 2048 tokens (past 0,
+    causal) and 120 decode rows with contexts U[1024, 16384]; 64 q / 8 kv heads, d128, bf16."""
+    import ctypes
+
+    import torch
+
+    from onnxruntime_ep_b200 import _capi, paged
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    Hm, KVm = 64, 8
+    rng = np.random.default_rng(4)
+    n_pre, s_pre, n_dec = args.mixed_chunks, 2048, args.mixed_decode
+    Ldec = rng.integers(1024, 16384, size=n_dec, endpoint=True)
+    nq = np.array([s_pre] * n_pre + [1] * n_dec)
+    past = np.concatenate([np.zeros(n_pre, np.int64), Ldec - 1])
+    total = nq + past
+    need = -(-total // BS)
+    NB = max(min(args.pool_blocks, 131072), int(need.sum()))
+    perm = rng.permutation(NB).astype(np.int32)
+    maxb = int(need.max())
+    bt = np.zeros((len(nq), maxb), np.int32)
+    off = 0
+    for b in range(len(nq)):
+        bt[b, :need[b]] = perm[off:off + need[b]]
+        off += int(need[b])
+    cum = np.concatenate([[0], np.cumsum(nq)]).astype(np.int32)
+    nt = int(cum[-1])
+    g = torch.Generator(device=dev)
+    g.manual_seed(4)
+    kc = torch.empty((NB, BS, KVm, D), dtype=torch.bfloat16, device=dev)
+    vc = torch.empty_like(kc)
+    kc.normal_(0.0, 1.0, generator=g)
+    vc.normal_(0.0, 1.0, generator=g)
+    q = torch.randn((nt, Hm * D), generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn((nt, KVm * D), generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn((nt, KVm * D), generator=g, device=dev).to(torch.bfloat16)
+    host = {"cumulative_sequence_length": cum, "past_seqlens": past.astype(np.int32), "block_table": bt}
+    p, keep, out = paged.build_params(q, k, v, kc, vc, torch.from_numpy(cum).to(dev),
+                                      torch.from_numpy(past.astype(np.int32)).to(dev),
+                                      torch.from_numpy(bt).to(dev), num_heads=Hm, kv_num_heads=KVm,
+                                      host_metadata=host)
+    stream = torch.cuda.current_stream(dev)
+    sp, pp = ctypes.c_void_p(stream.cuda_stream), ctypes.byref(p)
+    for _ in range(args.warmup):
+        _capi.check(_capi.LIB.b200_paged_attention(pp, sp))
+    _capi.check(_capi.LIB.b200_read_status(pp, sp))
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a_, b_ in ev:
+        a_.record(stream)
+        b_.record(stream)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        t0.record(stream)
+        for i in range(args.steps):
+            p.attention_event_begin = ctypes.c_void_p(ev[i][0].cuda_event)
+            p.attention_event_end = ctypes.c_void_p(ev[i][1].cuda_event)
+            _capi.check(_capi.LIB.b200_paged_attention(pp, sp))
+        t1.record(stream)
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    attn_ms = statistics.mean(a_.elapsed_time(b_) for a_, b_ in ev)
+    prefill_flop = 4.0 * D * Hm * n_pre * s_pre * (s_pre + 1) / 2
+    decode_kv = int(Ldec.sum()) * KVm * D * 2 * 2
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    line = {"metric": "mixed ragged PagedAttention call time (config 4)", "value": ms, "unit": "ms/call",
+            "higher_is_better": False, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": {"workload": "BASELINE config 4: 8 prefill chunks x 2048 tokens (causal) + 120 decode rows "
+                                   "(ctx U[1024,16384]), 64q/8kv, d128, bs16", "num_tokens": nt},
+            "attention_ms": attn_ms, "prefill_tflop": prefill_flop / 1e12, "decode_kv_gb": decode_kv / 1e9,
+            "roofline_ms": {"prefill_at_sustained_bf16": prefill_flop / (peaks.get("bf16_tflops_sustained", 1411.9) * 1e12) * 1e3,
+                            "decode_at_measured_hbm": decode_kv / (peaks.get("hbm_gbs", 6448.7) * 1e9) * 1e3},
+            "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.workload == "mixed":
+        run_mixed(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

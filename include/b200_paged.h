@@ -211,9 +211,10 @@ B200_API int b200_paged_attention_claim(const B200NodeInfo* node, char* reason, 
 
 /* Known-answer test of the tcgen05 tensor-core path: one CTA computes, for 128x128 fp16/bf16
  * row-major device matrices a, b, v, the fp32 products c_qk = a . b^T and c_pv = a . v through
- * TMA, shared-memory matrix descriptors, tcgen05.mma into tensor memory and tcgen05.ld. */
+ * TMA, shared-memory matrix descriptors, tcgen05.mma into tensor memory and tcgen05.ld, and
+ * (when c_ts is not NULL) c_ts = a . v again with a held in tensor memory. */
 B200_API int b200_selftest_tcgen05(int32_t dtype, const void* a, const void* b, const void* v, float* c_qk,
-                                   float* c_pv, int32_t* device_status, void* stream);
+                                   float* c_pv, float* c_ts, int32_t* device_status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -44,6 +44,8 @@ struct PrologueArgs {
   void* q_proc; void* k_proc;  // processed rows [nt, H*d], [nt, KV*d] in T (norm/RoPE only)
   int* owner_keys; int* owner_vals; uint32_t owner_capacity;  // duplicate-slot table or null
   int* status;
+  int* route;  // per-sequence route; a prefill sequence whose new rows do not all land in their
+               // block-table slots (slot_mapping elsewhere, -1, or overwritten) moves to generic
 };
 
 void launch_meta_check(const PrologueArgs& a, cudaStream_t stream);
@@ -66,16 +68,25 @@ struct AttnArgs {
   const void* head_sink;
   void* out;
   int* status;
-  int skip_decode;   // generic kernel: leave sequences with nq*group <= kDecodeRows to the decode kernel
+  // Per-sequence route (kRoute*), written by the plan kernel and refined by the prologue; null
+  // means every sequence runs on the generic kernel.
+  int* route;
+  int decode_on;   // decode kernel enabled for this call (shape supported)
+  int prefill_tq;  // tokens per 128-row prefill tile (128 / group) or 0 = prefill kernel off
 };
+
+enum Route : int { kRouteDecode = 0, kRoutePrefill = 1, kRouteGeneric = 2 };
 
 constexpr int kDecodeRows = 8;   // q rows (query x head-in-group) one decode unit covers
 constexpr int kTile = 16;        // tokens per decode tile (one mma M tile)
 
 cudaError_t launch_generic(const AttnArgs& a, cudaStream_t stream);
 
-// Decode plan (stream-K layout), written by decode_plan_kernel into the workspace.
+// Plan of one call, written by decode_plan_kernel into the workspace: per-sequence routes,
+// the decode tile stream (stream-K layout) and the prefill tile list.
 struct DecodePlan {
+  int64_t* pf_total;     // [1]   prefill work items: q tiles x kv heads
+  int* pf_tile_off;      // [B+1] exclusive prefix of prefill q tiles over sequences
   int64_t* total_tiles;  // [1]   tiles over all decode sequences x kv heads
   int* seq_tile_off;     // [B+1] exclusive prefix of decode tiles (per kv head) over sequences
   int* done;             // [B*KV] pieces finished per (sequence, kv head), for the fused combine
@@ -101,8 +112,17 @@ int encode_tensor_map(CUtensorMap* map, bool bf16, int rank, const void* base, c
 
 cudaError_t launch_decode(const AttnArgs& a, const DecodePlan& plan, const DecodeMaps& maps, int num_sms,
                           cudaStream_t stream);
+struct PrefillMaps {
+  CUtensorMap k_map;  // cache views, as DecodeMaps
+  CUtensorMap v_map;
+  CUtensorMap q_map;  // [nt, H, d] view of the (processed) queries: box {64, group, 128/group}
+};
+bool prefill_supported(int head_size, int block_size, int group, int act_dtype, int cache_dtype);
+cudaError_t launch_prefill(const AttnArgs& a, const DecodePlan& plan, const PrefillMaps& maps, int num_sms,
+                           cudaStream_t stream);
+
 cudaError_t launch_tc_selftest(bool bf16, const void* a, const void* b, const void* v, float* c_qk, float* c_pv,
-                               int* status, cudaStream_t stream, int* cu_result);
+                               float* c_ts, int* status, cudaStream_t stream, int* cu_result);
 bool decode_supported(int head_size, int block_size, int act_dtype, int cache_dtype);
 
 }  // namespace b200

@@ -61,14 +61,22 @@ struct Layout {
   uint32_t owner_cap = 0;
   size_t q_proc = 0, k_proc = 0;
   size_t total_tiles = 0, seq_tile_off = 0, done = 0, part_o = 0, part_ml = 0;
+  size_t route = 0, pf_tile_off = 0, pf_total = 0;
   int min_tiles_per_warp = 0;
   bool fast_decode = false;
+  bool fast_prefill = false;
   bool process = false;
   size_t total = 0;
 };
 
 bool fast_decode_enabled(const B200PagedAttentionParams* p) {
   return !p->force_generic && b200::decode_supported(p->head_size, p->block_size, p->act_dtype, p->cache_dtype);
+}
+
+bool fast_prefill_enabled(const B200PagedAttentionParams* p) {
+  return !p->force_generic && p->kv_num_heads > 0 &&
+         b200::prefill_supported(p->head_size, p->block_size, p->num_heads / p->kv_num_heads, p->act_dtype,
+                                 p->cache_dtype);
 }
 
 Layout make_layout(const B200PagedAttentionParams* p) {
@@ -93,7 +101,13 @@ Layout make_layout(const B200PagedAttentionParams* p) {
     L.k_proc = take(2 * nt * p->kv_num_heads * d);
   }
   L.fast_decode = fast_decode_enabled(p);
-  if (L.fast_decode) {
+  L.fast_prefill = fast_prefill_enabled(p);
+  if (L.fast_decode || L.fast_prefill) {
+    L.route = take(sizeof(int) * (size_t)p->batch);
+    L.pf_tile_off = take(sizeof(int) * ((size_t)p->batch + 1));
+    L.pf_total = take(sizeof(int64_t));
+  }
+  if (L.fast_decode || L.fast_prefill) {
     // Stream-K decode: at most 2 partial slots of 8 rows per warp of the persistent grid.
     const size_t max_warps = (size_t)device_sm_count(p) * b200::kDecodeMaxCtasPerSm * b200::kDecodeWarpsPerCta;
     const size_t part_rows = max_warps * 2 * b200::kDecodeRows;
@@ -244,7 +258,7 @@ int encode_cache_map(CUtensorMap* map, const void* base, const B200PagedAttentio
 }
 
 b200::PrologueArgs prologue_args(const B200PagedAttentionParams* p, const Layout& L, char* ws, int* status,
-                                 bool dedup, bool kv_only) {
+                                 bool dedup, bool kv_only, int* route) {
   b200::PrologueArgs a{};
   a.num_heads = p->num_heads;
   a.kv_heads = p->kv_num_heads;
@@ -294,12 +308,13 @@ b200::PrologueArgs prologue_args(const B200PagedAttentionParams* p, const Layout
     a.owner_capacity = L.owner_cap;
   }
   a.status = status;
+  a.route = route;
   return a;
 }
 
 // Shared front half of append and attention: checks, status, dedup table, prologue kernel.
 int run_prologue(const B200PagedAttentionParams* p, const Layout& L, cudaStream_t stream, bool kv_only,
-                 bool status_cleared, b200::PrologueArgs* out_args) {
+                 bool status_cleared, int* route, bool* duplicates_out) {
   char* ws = static_cast<char*>(p->workspace);
   int* status = p->device_status ? p->device_status : reinterpret_cast<int*>(ws + L.status);
   const bool host_meta = p->host_cumulative_sequence_length && p->host_past_seqlens && p->host_block_table;
@@ -314,7 +329,8 @@ int run_prologue(const B200PagedAttentionParams* p, const Layout& L, cudaStream_
     if (e != cudaSuccess) return cuda_fail(e, "status reset");
     count_launches(1);
   }
-  b200::PrologueArgs a = prologue_args(p, L, ws, status, dedup, kv_only);
+  if (duplicates_out) *duplicates_out = dedup;
+  b200::PrologueArgs a = prologue_args(p, L, ws, status, dedup, kv_only, route);
   if (dedup) {
     e = cudaMemsetAsync(ws + L.owner_keys, 0xff, sizeof(int) * 2 * (size_t)L.owner_cap, stream);
     if (e != cudaSuccess) return cuda_fail(e, "slot table reset");
@@ -327,7 +343,6 @@ int run_prologue(const B200PagedAttentionParams* p, const Layout& L, cudaStream_
   e = b200::launch_prologue(a, stream);
   if (e != cudaSuccess) return cuda_fail(e, "kv_prologue_kernel");
   count_launches(1);
-  if (out_args) *out_args = a;
   return B200_OK;
 }
 
@@ -388,7 +403,7 @@ int b200_kv_append(const B200PagedAttentionParams* p, void* stream_ptr) {
     Layout L = make_layout(p);
     if (!p->workspace || p->workspace_bytes < L.total)
       return fail(B200_ERR_WORKSPACE, "PagedAttention: workspace missing or smaller than b200_paged_attention_workspace_size()");
-    return run_prologue(p, L, static_cast<cudaStream_t>(stream_ptr), true, false, nullptr);
+    return run_prologue(p, L, static_cast<cudaStream_t>(stream_ptr), true, false, nullptr, nullptr);
   } catch (const std::exception& ex) {
     return fail(B200_ERR_FAIL, std::string("PagedAttention: ") + ex.what());
   } catch (...) {
@@ -456,42 +471,72 @@ int b200_paged_attention(const B200PagedAttentionParams* p, void* stream_ptr) {
 
     b200::DecodePlan plan{};
     b200::DecodeMaps maps;
-    if (L.fast_decode) {
+    b200::PrefillMaps pmaps;
+    const bool planned = L.fast_decode || L.fast_prefill;
+    const int group = p->num_heads / p->kv_num_heads;
+    if (planned) {
       plan.total_tiles = reinterpret_cast<int64_t*>(ws + L.total_tiles);
       plan.seq_tile_off = reinterpret_cast<int*>(ws + L.seq_tile_off);
       plan.done = reinterpret_cast<int*>(ws + L.done);
       plan.part_o = reinterpret_cast<float*>(ws + L.part_o);
       plan.part_ml = reinterpret_cast<float*>(ws + L.part_ml);
       plan.min_tiles_per_warp = L.min_tiles_per_warp;
+      plan.pf_tile_off = reinterpret_cast<int*>(ws + L.pf_tile_off);
+      plan.pf_total = reinterpret_cast<int64_t*>(ws + L.pf_total);
+      a.route = reinterpret_cast<int*>(ws + L.route);
+      a.decode_on = L.fast_decode;
+      a.prefill_tq = L.fast_prefill ? 128 / group : 0;
       if ((rc = encode_cache_map(&maps.k_map, p->key_cache, p))) return rc;
       if ((rc = encode_cache_map(&maps.v_map, p->value_cache, p))) return rc;
-      // First launch of the call: clears the status word, then plans the decode units.
+      if (L.fast_prefill) {
+        pmaps.k_map = maps.k_map;
+        pmaps.v_map = maps.v_map;
+        // [nt, H, d] view of the (processed) queries: box {64 channels, g heads, 128/g tokens}
+        const uint64_t dims[3] = {(uint64_t)p->head_size, (uint64_t)p->num_heads, (uint64_t)p->num_tokens};
+        const uint64_t strides[2] = {(uint64_t)p->head_size * 2, (uint64_t)a.q_stride * 2};
+        const uint32_t box[3] = {64, (uint32_t)group, (uint32_t)(128 / group)};
+        int r = b200::encode_tensor_map(&pmaps.q_map, p->act_dtype == B200_DTYPE_BFLOAT16, 3, a.q, dims, strides, box);
+        if (r) return fail(B200_ERR_CUDA, "PagedAttention: cuTensorMapEncodeTiled (queries) failed (" + std::to_string(r) + ")");
+      }
+      // First launch of the call: clears the status word, routes sequences, plans the work.
       cudaError_t e = b200::launch_decode_plan(a, plan, stream);
       if (e != cudaSuccess) return cuda_fail(e, "decode_plan_kernel");
       count_launches(1);
     }
-    rc = run_prologue(p, L, stream, false, L.fast_decode, nullptr);
+    bool duplicates = true;
+    rc = run_prologue(p, L, stream, false, planned, a.route, &duplicates);
     if (rc) return rc;
 
-    bool any_generic = true;
+    // Which kernels can have work.  With host metadata the host knows the routes (a prefill
+    // sequence may still move to the generic kernel when slots are remapped or duplicated);
+    // without it every enabled kernel is launched and each skips what is not its own.
     const bool host_meta = p->host_cumulative_sequence_length && p->host_past_seqlens;
+    bool any_decode = L.fast_decode, any_prefill = L.fast_prefill, any_generic = true;
+    if (host_meta) {
+      const int32_t* cum = p->host_cumulative_sequence_length;
+      any_decode = any_prefill = any_generic = false;
+      for (int b = 0; b < p->batch; ++b) {
+        const int nq = cum[b + 1] - cum[b];
+        if (nq <= 0) continue;
+        if (L.fast_decode && nq * group <= b200::kDecodeRows) any_decode = true;
+        else if (L.fast_prefill) any_prefill = true;
+        else any_generic = true;
+      }
+      if (any_prefill && (p->host_slot_mapping || p->slot_mapping || duplicates)) any_generic = true;
+    }
     if (p->attention_event_begin) {
       cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(p->attention_event_begin), stream);
       if (e != cudaSuccess) return cuda_fail(e, "event record");
     }
-    if (L.fast_decode) {
+    if (any_decode) {
       cudaError_t e = b200::launch_decode(a, plan, maps, device_sm_count(p), stream);
       if (e != cudaSuccess) return cuda_fail(e, "paged_decode_kernel");
       count_launches(1);
-      a.skip_decode = 1;
-      if (host_meta) {
-        any_generic = false;
-        const int32_t* cum = p->host_cumulative_sequence_length;
-        for (int b = 0; b < p->batch && !any_generic; ++b) {
-          int nq = cum[b + 1] - cum[b];
-          any_generic = nq * a.group > b200::kDecodeRows;
-        }
-      }
+    }
+    if (any_prefill) {
+      cudaError_t e = b200::launch_prefill(a, plan, pmaps, device_sm_count(p), stream);
+      if (e != cudaSuccess) return cuda_fail(e, "paged_prefill_kernel");
+      count_launches(1);
     }
     if (any_generic) {
       cudaError_t e = b200::launch_generic(a, stream);
@@ -511,13 +556,13 @@ int b200_paged_attention(const B200PagedAttentionParams* p, void* stream_ptr) {
 }
 
 int b200_selftest_tcgen05(int32_t dtype, const void* a, const void* b, const void* v, float* c_qk, float* c_pv,
-                          int32_t* device_status, void* stream) {
+                          float* c_ts, int32_t* device_status, void* stream) {
   if (!a || !b || !v || !c_qk || !c_pv || !device_status)
     return fail(B200_ERR_INVALID_ARGUMENT, "selftest: null pointer");
   if (dtype != B200_DTYPE_FLOAT16 && dtype != B200_DTYPE_BFLOAT16)
     return fail(B200_ERR_INVALID_ARGUMENT, "selftest: dtype must be FLOAT16 or BFLOAT16");
   int cu = 0;
-  cudaError_t e = b200::launch_tc_selftest(dtype == B200_DTYPE_BFLOAT16, a, b, v, c_qk, c_pv, device_status,
+  cudaError_t e = b200::launch_tc_selftest(dtype == B200_DTYPE_BFLOAT16, a, b, v, c_qk, c_pv, c_ts, device_status,
                                            static_cast<cudaStream_t>(stream), &cu);
   if (cu) return fail(B200_ERR_CUDA, "selftest: cuTensorMapEncodeTiled failed (" + std::to_string(cu) + ")");
   if (e != cudaSuccess) return cuda_fail(e, "tc_selftest_kernel");

@@ -156,6 +156,19 @@ __global__ void kv_prologue_kernel(PrologueArgs a) {
   bool valid = token_slot(a, t, b, slot);
   bool write = valid && slot >= 0 && owns_slot(a, t, slot);
   if (!valid && tid == 0) set_status(a.status, a.slot_mapping ? kStatusBadSlot : kStatusBadBlock);
+  if (a.route && tid == 0 && a.route[b] == kRoutePrefill) {
+    // The prefill kernel reads this call's new keys back from the cache; it may only do so
+    // when this token's row lands in its own block-table slot.
+    bool canonical = write;
+    if (canonical && a.slot_mapping) {
+      const int64_t logical = (int64_t)a.past[b] + (t - a.cum[b]);
+      const int64_t page = logical / a.block_size;
+      canonical = page < a.max_blocks &&
+                  slot == (int64_t)a.block_table[(int64_t)b * a.max_blocks + page] * a.block_size +
+                              logical % a.block_size;
+    }
+    if (!canonical) a.route[b] = kRouteGeneric;
+  }
   if (a.kv_only && !write) return;
 
   const bool process = a.do_norm || a.do_rotary;

@@ -8,8 +8,9 @@
 // paged_attention.rs:52-61).
 //
 // B200 design (one launch for the whole ragged batch, not one per sequence):
-//  * decode_plan_kernel (1 CTA) lays the work out as one stream of 16-token tiles:
-//    for each decode sequence, for each kv head, its tiles (prefix offsets per sequence);
+//  * decode_plan_kernel (1 CTA) routes every sequence (decode / tcgen05 prefill / generic) and
+//    lays the decode work out as one stream of 16-token tiles: for each decode sequence, for
+//    each kv head, its tiles (prefix offsets per sequence);
 //  * paged_decode_kernel is persistent (grid = SMs x resident CTAs) and every warp owns an
 //    equal contiguous range of that stream (stream-K: exact balance for ragged lengths, no
 //    scheduling atomics).  A warp streams its tiles through a private STAGES-deep ring of
@@ -69,34 +70,50 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int& 
   return before;
 }
 
-// 16-token tiles of sequence b per kv head if it is on the decode path, else 0.
-__device__ __forceinline__ int decode_tiles(const AttnArgs& a, int b) {
+// Route of sequence b, with its decode tiles (per kv head) or prefill q tiles.
+__device__ __forceinline__ int route_of(const AttnArgs& a, int b, int& dtiles, int& ptiles) {
+  dtiles = ptiles = 0;
   const int c0 = a.cum[b], c1 = a.cum[b + 1], nq = c1 - c0, past = a.past[b];
   const int64_t total = (int64_t)past + nq;
-  if (c0 >= 0 && c1 <= a.num_tokens && nq >= 1 && nq * a.group <= kDecodeRows && past >= 0 &&
-      total <= (int64_t)a.max_blocks * a.block_size)
-    return (int)((total + kTile - 1) / kTile);
-  return 0;
+  const bool valid = c0 >= 0 && c1 <= a.num_tokens && nq >= 1 && past >= 0 &&
+                     total <= (int64_t)a.max_blocks * a.block_size;
+  if (!valid) return kRouteGeneric;  // the generic kernel guards invalid metadata itself
+  if (a.decode_on && nq * a.group <= kDecodeRows) {
+    dtiles = (int)((total + kTile - 1) / kTile);
+    return kRouteDecode;
+  }
+  if (a.prefill_tq > 0) {
+    ptiles = (nq + a.prefill_tq - 1) / a.prefill_tq;
+    return kRoutePrefill;
+  }
+  return kRouteGeneric;
 }
 
 __global__ void __launch_bounds__(1024) decode_plan_kernel(AttnArgs a, DecodePlan plan) {
   __shared__ int warp_sums[32];
   if (threadIdx.x == 0 && a.status) *a.status = 0;  // first kernel of every call clears status
-  int carry = 0;
+  int carry = 0, pcarry = 0;
   for (int base = 0; base < a.batch; base += blockDim.x) {
     const int b = base + threadIdx.x;
-    const int tiles = b < a.batch ? decode_tiles(a, b) : 0;
-    int tot;
-    const int off = block_exclusive_scan(tiles, warp_sums, tot);
+    int dtiles = 0, ptiles = 0, route = kRouteGeneric;
+    if (b < a.batch) route = route_of(a, b, dtiles, ptiles);
+    int tot, ptot;
+    const int off = block_exclusive_scan(dtiles, warp_sums, tot);
+    const int poff = block_exclusive_scan(ptiles, warp_sums, ptot);
     if (b < a.batch) {
+      a.route[b] = route;
       plan.seq_tile_off[b] = carry + off;
+      plan.pf_tile_off[b] = pcarry + poff;
       for (int kh = 0; kh < a.kv_heads; ++kh) plan.done[(int64_t)b * a.kv_heads + kh] = 0;
     }
     carry += tot;
+    pcarry += ptot;
   }
   if (threadIdx.x == 0) {
     plan.seq_tile_off[a.batch] = carry;
+    plan.pf_tile_off[a.batch] = pcarry;
     *plan.total_tiles = (int64_t)carry * a.kv_heads;
+    *plan.pf_total = (int64_t)pcarry * a.kv_heads;
   }
 }
 

@@ -29,7 +29,7 @@ __global__ void __launch_bounds__(128) generic_attention_kernel(AttnArgs a) {
   const int b = seq_of_token(a.cum, a.batch, t);
   const int c0 = a.cum[b];
   const int nq = a.cum[b + 1] - c0;
-  if (a.skip_decode && nq * a.group <= kDecodeRows) return;
+  if (a.route && a.route[b] != kRouteGeneric) return;  // another kernel owns this sequence
   const int D = a.head_size;
   const int i = t - c0;
   const int past = a.past[b];
