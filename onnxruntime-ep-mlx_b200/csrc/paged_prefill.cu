@@ -259,29 +259,52 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
         // Masks only where a key can be invisible to this row (diagonal tile, sequence end, window).
         const bool full = row_ok && kbase + kBN <= m.total && (!a.is_causal || kbase + kBN - 1 <= qpos) &&
                           (a.window <= 0 || kbase >= qpos - a.window + 1) && a.softcap <= 0.f;
-        float m_tile = -INFINITY;
-        if (full) {
+        // In the unmasked case the scores stay raw and scale folds into the exponent's FMA
+        // (qk_scale > 0); masked tiles are rewritten to scaled log2 values (-inf = masked).
+        const bool raw = full && qk_scale > 0.f;
+        float m_tile;
+        if (raw) {
+          float mx[8];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) mx[r] = -INFINITY;
 #pragma unroll
           for (int c = 0; c < kBN / 32; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              sv[c][i] *= qk_scale;
-              m_tile = fmaxf(m_tile, sv[c][i]);
-            }
+            for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], sv[c][i]);
+          m_tile = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+          m_tile *= qk_scale;
         } else {
+          // Keys this row sees, as a column range [vlo, vhi] of the tile (empty for padding rows).
+          const int vhi = row_ok ? min(m.total - 1, a.is_causal ? qpos : m.total - 1) - kbase : -1;
+          const int vlo = (a.window > 0 ? qpos - a.window + 1 : 0) - kbase;
+          if (a.softcap > 0.f) {
+            // cap * tanh(y / cap) in the log2 domain, tanh(u) = 1 - 2 / (1 + e^(2u)).
+            const float two_log2e_over_cap = 2.f * kLog2eP / a.softcap, cap_log2e = a.softcap * kLog2eP;
+#pragma unroll
+            for (int c = 0; c < kBN / 32; ++c)
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const float e = tc::ex2(fminf(sv[c][i] * qk_scale * two_log2e_over_cap, 126.f));
+                sv[c][i] = cap_log2e * (1.f - __fdividef(2.f, 1.f + e));
+              }
+          } else {
+#pragma unroll
+            for (int c = 0; c < kBN / 32; ++c)
+#pragma unroll
+              for (int i = 0; i < 32; ++i) sv[c][i] *= qk_scale;
+          }
+          float mx[8];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) mx[r] = -INFINITY;
 #pragma unroll
           for (int c = 0; c < kBN / 32; ++c)
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const int kp = kbase + c * 32 + i;
-              bool vis = row_ok && kp < m.total;
-              if (a.is_causal) vis = vis && kp <= qpos;
-              if (a.window > 0) vis = vis && kp >= qpos - a.window + 1;
-              float y = sv[c][i] * qk_scale;
-              if (a.softcap > 0.f) y = a.softcap * tanhf(y / a.softcap) * kLog2eP;
-              sv[c][i] = vis ? y : -INFINITY;
-              m_tile = fmaxf(m_tile, sv[c][i]);
+              const int col = c * 32 + i;
+              sv[c][i] = (col >= vlo && col <= vhi) ? sv[c][i] : -INFINITY;
+              mx[i & 7] = fmaxf(mx[i & 7], sv[c][i]);
             }
+          m_tile = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
         }
         // Lazy rescale: the reference max moves only when the row max grows by more than 2^8.
         const float m_new = fmaxf(m_run, m_tile);
@@ -308,15 +331,16 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
         }
         // P = 2^(s - m_run) as hi + lo 16-bit halves over the S columns: hi in [0,64), lo in [64,128)
         const float mu = m_run == -INFINITY ? 0.f : m_run;
-        float lsum = 0.f;
+        const float kscale = raw ? qk_scale : 1.0f;  // p = 2^(s * kscale - mu)
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < kBN / 32; ++c) {
           uint32_t hi[16], lo[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float p0 = tc::ex2(sv[c][2 * i] - mu);
-            const float p1 = tc::ex2(sv[c][2 * i + 1] - mu);
-            lsum += p0 + p1;
+            const float p0 = tc::ex2(fmaf(sv[c][2 * i], kscale, -mu));
+            const float p1 = tc::ex2(fmaf(sv[c][2 * i + 1], kscale, -mu));
+            ls[i & 3] += p0 + p1;
             hi[i] = MMA::pack(p0, p1);
             const float2 h = MMA::unpack(hi[i]);
             lo[i] = MMA::pack(p0 - h.x, p1 - h.y);
@@ -324,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           tc::st16u(sbuf + c * 16, hi);
           tc::st16u(sbuf + 64 + c * 16, lo);
         }
+        const float lsum = (ls[0] + ls[1]) + (ls[2] + ls[3]);
         l_run += lsum;
         tc::wait_st();
         tc::fence_before_sync();
