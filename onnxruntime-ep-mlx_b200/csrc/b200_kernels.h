@@ -72,7 +72,7 @@ struct AttnArgs {
   // means every sequence runs on the generic kernel.
   int* route;
   int decode_on;   // decode kernel enabled for this call (shape supported)
-  int prefill_tq;  // tokens per 128-row prefill tile (128 / group) or 0 = prefill kernel off
+  int prefill_tq;  // query tokens per prefill work item (2 x 128 rows / group) or 0 = prefill kernel off
 };
 
 enum Route : int { kRouteDecode = 0, kRoutePrefill = 1, kRouteGeneric = 2 };
@@ -118,6 +118,8 @@ struct PrefillMaps {
   CUtensorMap q_map;  // [nt, H, d] view of the (processed) queries: box {64, group, 128/group}
 };
 bool prefill_supported(int head_size, int block_size, int group, int act_dtype, int cache_dtype);
+// Query tokens of one prefill work item (a pair of 128-row q tiles) for query-head group `group`.
+int prefill_tokens_per_item(int group);
 cudaError_t launch_prefill(const AttnArgs& a, const DecodePlan& plan, const PrefillMaps& maps, int num_sms,
                            cudaStream_t stream);
 

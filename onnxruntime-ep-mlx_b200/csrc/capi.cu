@@ -485,7 +485,7 @@ int b200_paged_attention(const B200PagedAttentionParams* p, void* stream_ptr) {
       plan.pf_total = reinterpret_cast<int64_t*>(ws + L.pf_total);
       a.route = reinterpret_cast<int*>(ws + L.route);
       a.decode_on = L.fast_decode;
-      a.prefill_tq = L.fast_prefill ? 128 / group : 0;
+      a.prefill_tq = L.fast_prefill ? b200::prefill_tokens_per_item(group) : 0;
       if ((rc = encode_cache_map(&maps.k_map, p->key_cache, p))) return rc;
       if ((rc = encode_cache_map(&maps.v_map, p->value_cache, p))) return rc;
       if (L.fast_prefill) {

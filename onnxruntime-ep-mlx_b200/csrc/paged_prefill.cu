@@ -6,25 +6,34 @@
 // fp32 softmax with optional sink, fp32 accumulation).
 //
 // B200 design:
-//  * work item = (sequence, kv head, q tile).  A q tile is 128 rows = 128/g query tokens x the
-//    g query heads of the kv head, so each K/V tile serves the whole head group (native GQA);
-//  * persistent CTAs (one per SM: 225 KB of shared memory and all 512 tensor-memory columns)
-//    take items round-robin, longest (latest q tile) first;
+//  * work item = (sequence, kv head, pair of q tiles).  A q tile is 128 rows = 128/g query
+//    tokens x the g query heads of the kv head, so each K/V tile serves the whole head group
+//    (native GQA), and the two q tiles of an item share every K/V tile they load;
+//  * persistent CTAs (one per SM: 224 KB of shared memory and all 512 tensor-memory columns)
+//    take items round-robin, longest (latest q tiles) first;
 //  * warp-specialised, the roles synchronised only through mbarriers:
-//      - warp 4 (TMA producer): Q tile [128 x 128] by a 3-D box pair from the [nt, H, d] query
-//        view; K/V tiles of 128 keys = 8 pages of 16 slots, one 64-channel box per lane (32
-//        boxes per tile issued in parallel), 3 stages; pages past the sequence end load from an
-//        out-of-range coordinate (TMA zero fill);
-//      - warp 5 (MMA issuer): S = Q K^T (8 x tcgen05.mma kind::f16, M=128, N=128, K=16) into one
-//        of two tensor-memory S buffers, then O += P V with P read from tensor memory and V as
-//        the MN-major operand (the cache's [key][channel] layout); QK of tile j+1 runs while the
-//        softmax works on tile j;
-//      - warps 0-3 (softmax, one q row per thread = tensor-memory lane): exp2-domain softmax
-//        with a lazily rescaled running max (O is rescaled in tensor memory only when the max
-//        grows by more than 2^8); P goes back over the S columns as a hi + lo pair of 16-bit
-//        values (~16 mantissa bits); epilogue normalises (sink) and stores the rows.
-//  * every mbarrier wait is bounded (%globaltimer); a timeout sets the status word and the CTA
-//    drains and stops instead of hanging.
+//      - warp 8 (TMA producer): Q tiles [128 x 128] by a 3-D box pair from the [nt, H, d]
+//        query view, one buffer per q tile; K tiles (2 stages) and V tiles (3 stages) of 128
+//        keys = 8 pages of 16 slots, one 64-channel box per lane; pages past the sequence end
+//        load from an out-of-range coordinate (TMA zero fill);
+//      - warp 9 (MMA issuer, one thread): per K/V tile j, in order
+//          PV0(j-1), S0(j), PV1(j-1), S1(j)
+//        with S = Q K^T (tcgen05.mma kind::f16, M=N=128, K=16 steps, both operands in shared
+//        memory) and O += P V (P from tensor memory, V as the MN-major operand in the cache's
+//        [key][channel] layout).  While warpgroup 0 turns S0 into P0 the tensor core runs
+//        PV1/S1, and the other way round (ping-pong);
+//      - warpgroups 0 and 1 (softmax and epilogue of q tile 0 / 1, one row per thread =
+//        tensor-memory lane): exp2-domain softmax with a lazily rescaled running max (O is
+//        rescaled in tensor memory only when the max grows by more than 2^8); P goes back over
+//        the S columns as a hi + lo pair of 16-bit values (~16 mantissa bits); the epilogue
+//        normalises (sink) and stores the rows;
+//  * tensor memory: S0/P0 columns [0,128), S1/P1 [128,256), O0 [256,384), O1 [384,512);
+//  * registers: warpgroups 0-1 grow to 200 per thread and warpgroup 2 shrinks to 96
+//    (setmaxnreg); together they stay within the 384 x 168 the block is launched with, which
+//    the launcher checks before the first launch (a split above it would never complete);
+//  * every mbarrier wait is bounded (%globaltimer); a timeout sets the status word, the CTA
+//    waits (bounded) for its own copies and MMAs in flight, frees tensor memory and returns.
+#include <atomic>
 #include <type_traits>
 
 #include "b200_common.cuh"
@@ -38,40 +47,49 @@ namespace {
 constexpr int kBM = 128;             // q rows per tile
 constexpr int kBN = 128;             // keys per tile
 constexpr int kD = 128;              // head size of this kernel
-constexpr int kStages = 3;           // K/V pipeline depth
+constexpr int kQTiles = 2;           // q tiles per work item
+constexpr int kKStages = 2;          // K pipeline depth
+constexpr int kVStages = 3;          // V pipeline depth
 constexpr int kBoxBytes = 128 * 128; // one [128 rows][64 channels] 16-bit box: 16 KB
 constexpr int kTileBytes = 2 * kBoxBytes;  // [128][128] 16-bit tile: 32 KB
 constexpr float kLog2eP = 1.4426950408889634f;
 
 // shared-memory map (offsets from the 1024-aligned base)
-constexpr int kSmemQ = 0;
-constexpr int kSmemK = kSmemQ + kTileBytes;              // kStages K tiles
-constexpr int kSmemV = kSmemK + kStages * kTileBytes;    // kStages V tiles
-constexpr int kSmemBytes = kSmemV + kStages * kTileBytes;  // 224 KB
+constexpr int kSmemQ = 0;                                   // kQTiles Q tiles
+constexpr int kSmemK = kSmemQ + kQTiles * kTileBytes;       // kKStages K tiles
+constexpr int kSmemV = kSmemK + kKStages * kTileBytes;      // kVStages V tiles
+constexpr int kSmemBytes = kSmemV + kVStages * kTileBytes;  // 224 KB
 
-// Roles: warps 0-3 softmax / epilogue (one q row per thread), warp 4 TMA producer, warp 5 MMA.
-constexpr int kSoftmaxThreads = 128;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kThreads = 192;
+// Roles: warpgroups 0-1 softmax / epilogue of q tile 0 / 1; warpgroup 2 = warp 8 TMA producer,
+// warp 9 MMA issuer, warps 10-11 idle.
+constexpr int kThreads = 384;
+constexpr int kWgThreads = 128;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kSoftmaxRegs = 200;  // setmaxnreg split: 2 x 128 x 200 + 128 x 96 = 63488
+constexpr int kControlRegs = 96;
+constexpr int kSplitRegs = 2 * kWgThreads * kSoftmaxRegs + kWgThreads * kControlRegs;
+static_assert(kSplitRegs <= kThreads * 168, "register split exceeds the 384 x 168 launch allocation");
 
 struct Bars {
-  uint64_t q_full, q_empty;
-  uint64_t kv_full[kStages], kv_empty[kStages];
-  uint64_t s_full[2], p_full[2], o_done[2];
-  uint64_t o_free;
+  uint64_t q_full[kQTiles], q_empty[kQTiles];
+  uint64_t k_full[kKStages], k_empty[kKStages];
+  uint64_t v_full[kVStages], v_empty[kVStages];
+  uint64_t s_full[kQTiles], p_full[kQTiles], o_done[kQTiles];
+  uint64_t drain;
 };
 
 // One item of the prefill work list, as every role decodes it.
 struct Item {
-  int skip, b, kh, c0, nq, past, total, q0, q1, kv_lo, nkv;
+  int skip, b, kh, c0, nq, past, total, q0, kv_lo, n;
+  int nkv[kQTiles];  // K/V tiles q tile w needs (0: the tile has no rows); n = max
 };
 
 __device__ __forceinline__ Item decode_item(const AttnArgs& a, const DecodePlan& plan, int64_t it) {
   Item m{};
-  const int KV = a.kv_heads, TQ = a.prefill_tq;
-  const int64_t qtiles_total = *plan.pf_total / KV;
-  const int64_t qt_global = qtiles_total - 1 - it / KV;  // latest q tiles (most keys) first
+  const int KV = a.kv_heads, TQ = a.prefill_tq / kQTiles;
+  const int64_t items_total = *plan.pf_total / KV;
+  const int64_t qt_global = items_total - 1 - it / KV;  // latest q tiles (most keys) first
   m.kh = (int)(it % KV);
   int lo = 0, hi = a.batch - 1;  // sequence: largest b with pf_tile_off[b] <= qt_global
   while (lo < hi) {
@@ -86,12 +104,17 @@ __device__ __forceinline__ Item decode_item(const AttnArgs& a, const DecodePlan&
   m.nq = a.cum[m.b + 1] - m.c0;
   m.past = a.past[m.b];
   m.total = m.past + m.nq;
-  m.q0 = qt * TQ;
-  m.q1 = min(m.q0 + TQ, m.nq);
-  const int kv_hi = a.is_causal ? m.past + m.q1 : m.total;
+  m.q0 = qt * a.prefill_tq;
   m.kv_lo = a.window > 0 ? max(0, m.past + m.q0 - a.window + 1) : 0;
   m.kv_lo &= ~(kTile - 1);
-  m.nkv = (kv_hi - m.kv_lo + kBN - 1) / kBN;
+  m.n = 0;
+#pragma unroll
+  for (int w = 0; w < kQTiles; ++w) {
+    const int t0 = m.q0 + w * TQ, t1 = min(t0 + TQ, m.nq);
+    const int kv_hi = a.is_causal ? m.past + t1 : m.total;
+    m.nkv[w] = t0 < m.nq ? (kv_hi - m.kv_lo + kBN - 1) / kBN : 0;
+    m.n = max(m.n, m.nkv[w]);
+  }
   return m;
 }
 
@@ -102,6 +125,8 @@ bool prefill_supported(int head_size, int block_size, int group, int act_dtype, 
          (act_dtype == B200_DTYPE_FLOAT16 || act_dtype == B200_DTYPE_BFLOAT16) &&
          (group == 1 || group == 2 || group == 4 || group == 8 || group == 16);
 }
+
+int prefill_tokens_per_item(int group) { return kQTiles * kBM / group; }
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid_constant__ AttnArgs a,
@@ -120,24 +145,28 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = a.group, H = a.num_heads;
+  const int g = a.group, H = a.num_heads, TQ = a.prefill_tq / kQTiles;
   const int64_t n_items = *plan.pf_total;
   if (n_items == 0) return;
 
   if (warp == kMmaWarp) tc::alloc(&tmem_slot, 512);
   if (tid == 0) {
-    mbar_init(&bars.q_full, 1);
-    mbar_init(&bars.q_empty, 1);
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&bars.kv_full[i], 1);
-      mbar_init(&bars.kv_empty[i], 1);
+    for (int w = 0; w < kQTiles; ++w) {
+      mbar_init(&bars.q_full[w], 1);
+      mbar_init(&bars.q_empty[w], 1);
+      mbar_init(&bars.s_full[w], 1);
+      mbar_init(&bars.p_full[w], kWgThreads);
+      mbar_init(&bars.o_done[w], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars.s_full[i], 1);
-      mbar_init(&bars.p_full[i], kSoftmaxThreads);
-      mbar_init(&bars.o_done[i], 1);
+    for (int i = 0; i < kKStages; ++i) {
+      mbar_init(&bars.k_full[i], 1);
+      mbar_init(&bars.k_empty[i], 1);
     }
-    mbar_init(&bars.o_free, kSoftmaxThreads);
+    for (int i = 0; i < kVStages; ++i) {
+      mbar_init(&bars.v_full[i], 1);
+      mbar_init(&bars.v_empty[i], 1);
+    }
+    mbar_init(&bars.drain, 1);
     fence_mbar_init();
     s_failed = 0;
   }
@@ -145,7 +174,6 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
-  const uint32_t tO = tmem + 256;  // S/P buffers at columns [0,128) and [128,256)
 
   // Bounded wait on completion `index` of an mbarrier (parity = index & 1).
   auto wait_idx = [&](uint64_t* bar, uint32_t index) -> bool {
@@ -155,102 +183,164 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
     s_failed = 1;
     return false;
   };
+  // After a failure: bounded wait for a copy or commit this CTA issued, without the early exit.
+  auto drain_idx = [&](uint64_t* bar, uint32_t index) { mbar_wait(bar, index & 1u); };
 
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------------ TMA producer
-    uint32_t tile = 0, items = 0;
-    const int64_t oob_z = (int64_t)a.num_blocks * a.block_size;  // past the cache: zero fill
-    for (int64_t it = blockIdx.x; it < n_items && !s_failed; it += gridDim.x) {
-      const Item m = decode_item(a, plan, it);
-      if (m.skip) continue;
-      if (items > 0 && !wait_idx(&bars.q_empty, items - 1)) break;
-      if (lane == 0) mbar_arrive_expect_tx(&bars.q_full, kTileBytes);
-      __syncwarp();
-      if (lane < 2)
-        tma_load_3d(smem + kSmemQ + lane * kBoxBytes, &maps.q_map, &bars.q_full, lane * 64, m.kh * g, m.c0 + m.q0);
-      const int32_t* bt = a.block_table + (int64_t)m.b * a.max_blocks;
-      for (int j = 0; j < m.nkv; ++j, ++tile) {
-        const int st = tile % kStages;
-        const uint32_t use = tile / kStages;
-        if (use > 0 && !wait_idx(&bars.kv_empty[st], use - 1)) break;
-        // lane l: page l/4, channel half (l/2)%2, K (even l) or V (odd l)
-        const int page = lane >> 2, half = (lane >> 1) & 1, is_v = lane & 1;
-        const int pos0 = m.kv_lo + j * kBN + page * kTile;
-        const int32_t blk = pos0 < m.total ? __ldg(bt + pos0 / a.block_size) : -1;
-        const bool blk_ok = blk >= 0 && blk < a.num_blocks;
-        if (pos0 < m.total && !blk_ok) set_status(a.status, kStatusBadBlock);
-        const int z = blk_ok ? blk * a.block_size + pos0 % a.block_size : (int)oob_z;
-        if (lane == 0) mbar_arrive_expect_tx(&bars.kv_full[st], 2 * kTileBytes);
-        __syncwarp();
-        uint8_t* dst = smem + (is_v ? kSmemV : kSmemK) + st * kTileBytes + half * kBoxBytes + page * (kTile * 128);
-        tma_load_3d(dst, is_v ? &maps.v_map : &maps.k_map, &bars.kv_full[st], half * 64, m.kh, z);
-      }
-      ++items;
-    }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      uint32_t tile = 0, items = 0;
-      for (int64_t it = blockIdx.x; it < n_items && !s_failed; it += gridDim.x) {
+  if (warp >= 2 * (kWgThreads / 32)) {
+    // warpgroup 2: producer, MMA issuer and two idle warps give registers to the softmax
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));
+    if (warp == kProducerWarp) {
+      // ------------------------------------------------------------------ TMA producer
+      uint32_t qc0 = 0, qc1 = 0, kc = 0, vc = 0;  // loads issued per ring (scalars: no local memory)
+      const int64_t oob_z = (int64_t)a.num_blocks * a.block_size;  // past the cache: zero fill
+      // lane l loads box (page (l & 15) / 2, channel half l & 1) of K (l < 16) or V (l >= 16)
+      const int page = (lane & 15) >> 1, half = lane & 1, is_v = lane >> 4;
+      bool ok = true;
+      for (int64_t it = blockIdx.x; it < n_items && ok && !s_failed; it += gridDim.x) {
         const Item m = decode_item(a, plan, it);
         if (m.skip) continue;
-        if (!wait_idx(&bars.q_full, items)) break;
-        tc::fence_after_sync();
-        bool first_pv = true;
-        auto issue_pv = [&](uint32_t t) -> bool {  // O (+)= P_t . V_t, then release stage and buffer
-          if (!wait_idx(&bars.p_full[t & 1], t >> 1)) return false;
-          if (first_pv && items > 0 && !wait_idx(&bars.o_free, items - 1)) return false;
-          tc::fence_after_sync();
-          const uint32_t pbuf = tmem + (t & 1) * 128;
-          const uint32_t vbase = sbase + kSmemV + (t % kStages) * kTileBytes;
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            const uint64_t vdesc = tc::smem_desc(vbase + kk * 2048, kBoxBytes, 1024);
-            tc::mma_ts(tO, pbuf + kk * 8, vdesc, kIdPV, (first_pv && kk == 0) ? 0u : 1u);
-            tc::mma_ts(tO, pbuf + 64 + kk * 8, vdesc, kIdPV, 1u);
-          }
-          tc::commit(&bars.o_done[t & 1]);
-          tc::commit(&bars.kv_empty[t % kStages]);
-          first_pv = false;
-          return true;
-        };
-        bool ok = true;
-        for (int j = 0; j < m.nkv && ok; ++j, ++tile) {
-          const int st = tile % kStages;
-          if (!(ok = wait_idx(&bars.kv_full[st], tile / kStages))) break;
-          tc::fence_after_sync();
-          const uint32_t sbuf = tmem + (tile & 1) * 128;
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-            tc::mma_ss(sbuf, tc::smem_desc(sbase + kSmemQ + off, 16, 1024),
-                       tc::smem_desc(sbase + kSmemK + st * kTileBytes + off, 16, 1024), kIdQK, kk > 0);
-          }
-          tc::commit(&bars.s_full[tile & 1]);
-          if (j > 0) ok = issue_pv(tile - 1);
+        for (int w = 0; w < kQTiles && ok; ++w) {
+          if (m.nkv[w] == 0) continue;
+          uint32_t& qc = w ? qc1 : qc0;
+          if (qc > 0 && !(ok = wait_idx(&bars.q_empty[w], qc - 1))) break;
+          if (lane == 0) mbar_arrive_expect_tx(&bars.q_full[w], kTileBytes);
+          __syncwarp();
+          if (lane < 2)
+            tma_load_3d(smem + kSmemQ + w * kTileBytes + lane * kBoxBytes, &maps.q_map, &bars.q_full[w], lane * 64,
+                        m.kh * g, m.c0 + m.q0 + w * TQ);
+          ++qc;
         }
-        if (ok) ok = issue_pv(tile - 1);
-        tc::commit(&bars.q_empty);
-        if (!ok) break;
-        ++items;
+        const int32_t* bt = a.block_table + (int64_t)m.b * a.max_blocks;
+        for (int j = 0; j < m.n && ok; ++j) {
+          const int pos0 = m.kv_lo + j * kBN + page * kTile;
+          const int32_t blk = pos0 < m.total ? __ldg(bt + pos0 / a.block_size) : -1;
+          const bool blk_ok = blk >= 0 && blk < a.num_blocks;
+          if (!is_v && pos0 < m.total && !blk_ok) set_status(a.status, kStatusBadBlock);
+          const int z = blk_ok ? blk * a.block_size + pos0 % a.block_size : (int)oob_z;
+          const int off = half * kBoxBytes + page * (kTile * 128);
+          // K tile j
+          const int ks = kc % kKStages;
+          if (kc >= kKStages && !(ok = wait_idx(&bars.k_empty[ks], kc / kKStages - 1))) break;
+          if (lane == 0) mbar_arrive_expect_tx(&bars.k_full[ks], kTileBytes);
+          __syncwarp();
+          if (!is_v) tma_load_3d(smem + kSmemK + ks * kTileBytes + off, &maps.k_map, &bars.k_full[ks], half * 64, m.kh, z);
+          ++kc;
+          // V tile j
+          const int vs = vc % kVStages;
+          if (vc >= kVStages && !(ok = wait_idx(&bars.v_empty[vs], vc / kVStages - 1))) break;
+          if (lane == 0) mbar_arrive_expect_tx(&bars.v_full[vs], kTileBytes);
+          __syncwarp();
+          if (is_v) tma_load_3d(smem + kSmemV + vs * kTileBytes + off, &maps.v_map, &bars.v_full[vs], half * 64, m.kh, z);
+          ++vc;
+        }
       }
+      // Every issued copy lands before the CTA can exit (immediate on the normal path).
+      if (qc0 > 0) drain_idx(&bars.q_full[0], qc0 - 1);
+      if (qc1 > 0) drain_idx(&bars.q_full[1], qc1 - 1);
+      for (uint32_t i = (kc > kKStages ? kc - kKStages : 0); i < kc; ++i) drain_idx(&bars.k_full[i % kKStages], i / kKStages);
+      for (uint32_t i = (vc > kVStages ? vc - kVStages : 0); i < vc; ++i) drain_idx(&bars.v_full[i % kVStages], i / kVStages);
+    } else if (warp == kMmaWarp) {
+      // ------------------------------------------------------------------ MMA issuer
+      if (lane == 0) {
+        uint32_t qc0 = 0, qc1 = 0, pc0 = 0, pc1 = 0, kvc = 0;
+        bool issued = false;
+        for (int64_t it = blockIdx.x; it < n_items && !s_failed; it += gridDim.x) {
+          const Item m = decode_item(a, plan, it);
+          if (m.skip) continue;
+          // S_w(j) = Q_w . K_j^T into the S_w columns
+          auto issue_s = [&](int w, int j) -> bool {
+            if (j == 0) {
+              if (!wait_idx(&bars.q_full[w], w ? qc1 : qc0)) return false;
+              tc::fence_after_sync();
+            }
+            const uint32_t kb = sbase + kSmemK + ((kvc + j) % kKStages) * kTileBytes;
+            const uint32_t qb = sbase + kSmemQ + w * kTileBytes;
+            for (int kk = 0; kk < kD / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+              tc::mma_ss(tmem + w * 128, tc::smem_desc(qb + off, 16, 1024), tc::smem_desc(kb + off, 16, 1024), kIdQK,
+                         kk > 0);
+            }
+            tc::commit(&bars.s_full[w]);
+            if (j == m.nkv[w] - 1) {  // last use of Q_w in this item
+              tc::commit(&bars.q_empty[w]);
+              ++(w ? qc1 : qc0);
+            }
+            issued = true;
+            return true;
+          };
+          // O_w (+)= P_w(j) . V_j once the softmax has written P_w(j)
+          auto issue_pv = [&](int w, int j) -> bool {
+            if (!wait_idx(&bars.p_full[w], w ? pc1 : pc0)) return false;
+            tc::fence_after_sync();
+            const uint32_t pbuf = tmem + w * 128, obuf = tmem + 256 + w * 128;
+            const uint32_t vb = sbase + kSmemV + ((kvc + j) % kVStages) * kTileBytes;
+            for (int kk = 0; kk < kBN / 16; ++kk) {
+              const uint64_t vdesc = tc::smem_desc(vb + kk * 2048, kBoxBytes, 1024);
+              tc::mma_ts(obuf, pbuf + kk * 8, vdesc, kIdPV, (j > 0 || kk > 0) ? 1u : 0u);
+              tc::mma_ts(obuf, pbuf + 64 + kk * 8, vdesc, kIdPV, 1u);
+            }
+            tc::commit(&bars.o_done[w]);
+            ++(w ? pc1 : pc0);
+            return true;
+          };
+          auto wait_v = [&](int j) -> bool {  // V_j resident
+            if (!wait_idx(&bars.v_full[(kvc + j) % kVStages], (kvc + j) / kVStages)) return false;
+            tc::fence_after_sync();
+            return true;
+          };
+          // Per K/V tile j: PV0(j-1), S0(j), PV1(j-1), S1(j); a late K_j never holds back PV0(j-1).
+          bool ok = true;
+          for (int j = 0; j < m.n && ok; ++j) {
+            const uint32_t ki = kvc + j;
+            if (j > 0 && !(ok = wait_v(j - 1))) break;
+            if (j > 0 && j - 1 < m.nkv[0] && !(ok = issue_pv(0, j - 1))) break;
+            if (!(ok = wait_idx(&bars.k_full[ki % kKStages], ki / kKStages))) break;
+            tc::fence_after_sync();
+            if (j < m.nkv[0] && !(ok = issue_s(0, j))) break;
+            if (j > 0 && j - 1 < m.nkv[1] && !(ok = issue_pv(1, j - 1))) break;
+            if (j > 0) tc::commit(&bars.v_empty[(ki - 1) % kVStages]);
+            if (j < m.nkv[1] && !(ok = issue_s(1, j))) break;
+            tc::commit(&bars.k_empty[ki % kKStages]);
+          }
+          if (ok) {
+            const int j = m.n - 1;
+            ok = wait_v(j);
+            if (ok && j < m.nkv[0]) ok = issue_pv(0, j);
+            if (ok && j < m.nkv[1]) ok = issue_pv(1, j);
+            if (ok) tc::commit(&bars.v_empty[(kvc + j) % kVStages]);
+          }
+          kvc += m.n;
+          if (!ok) break;
+        }
+        // Every issued MMA completes before tensor memory is freed (immediate on the normal path).
+        if (issued) {
+          tc::commit(&bars.drain);
+          drain_idx(&bars.drain, 0);
+        }
+      }
+      __syncwarp();
     }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
     // ------------------------------------------------------------------ softmax + epilogue
-    const int row = tid;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const int w = warp >> 2;           // q tile of this warpgroup
+    const int row = tid & (kWgThreads - 1);
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t sbuf = tmem + w * 128 + lane_off, obuf = tmem + 256 + w * 128 + lane_off;
     const float qk_scale = a.softcap > 0.f ? a.scale : a.scale * kLog2eP;
-    uint32_t tile = 0;
+    uint32_t t = 0;  // tiles this warpgroup has processed
     for (int64_t it = blockIdx.x; it < n_items && !s_failed; it += gridDim.x) {
       const Item m = decode_item(a, plan, it);
-      if (m.skip) continue;
+      if (m.skip || m.nkv[w] == 0) continue;
       const int tl = row / g, hl = row % g;
-      const bool row_ok = m.q0 + tl < m.q1;
-      const int qpos = m.past + m.q0 + tl;
+      const int tok = m.q0 + w * TQ + tl;
+      const bool row_ok = tl < TQ && tok < m.nq;
+      const int qpos = m.past + tok;
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
-      for (int j = 0; j < m.nkv; ++j, ++tile) {
-        if (!(ok = wait_idx(&bars.s_full[tile & 1], tile >> 1))) break;
+      for (int j = 0; j < m.nkv[w]; ++j, ++t) {
+        if (!(ok = wait_idx(&bars.s_full[w], t))) break;
         tc::fence_after_sync();
-        const uint32_t sbuf = tmem + (tile & 1) * 128 + lane_off;
         float sv[kBN / 32][32];
 #pragma unroll
         for (int c = 0; c < kBN / 32; ++c) tc::ld32(sbuf + c * 32, sv[c]);
@@ -316,16 +406,16 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
         }
         if (j > 0 && __any_sync(0xffffffffu, grow && alpha != 1.0f)) {
           // O holds tiles < j: wait for PV of tile j-1, then scale this warp's rows in place.
-          if (!(ok = wait_idx(&bars.o_done[(tile - 1) & 1], (tile - 1) >> 1))) break;
+          if (!(ok = wait_idx(&bars.o_done[w], t - 1))) break;
           tc::fence_after_sync();
 #pragma unroll 1
           for (int c = 0; c < kD / 16; ++c) {
             float r[16];
-            tc::ld16(tO + lane_off + c * 16, r);
+            tc::ld16(obuf + c * 16, r);
             tc::wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) r[i] *= alpha;
-            tc::st16(tO + lane_off + c * 16, r);
+            tc::st16(obuf + c * 16, r);
           }
           tc::wait_st();
         }
@@ -348,15 +438,14 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           tc::st16u(sbuf + c * 16, hi);
           tc::st16u(sbuf + 64 + c * 16, lo);
         }
-        const float lsum = (ls[0] + ls[1]) + (ls[2] + ls[3]);
-        l_run += lsum;
+        l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
         tc::wait_st();
         tc::fence_before_sync();
-        mbar_arrive(&bars.p_full[tile & 1]);
+        mbar_arrive(&bars.p_full[w]);
       }
       if (!ok) break;
       // ---- epilogue: last PV done -> normalise -> store this row
-      if (!wait_idx(&bars.o_done[(tile - 1) & 1], (tile - 1) >> 1)) break;
+      if (!wait_idx(&bars.o_done[w], t - 1)) break;
       tc::fence_after_sync();
       float L = l_run;
       if (a.head_sink) {  // l is relative to the reference max m_run; fold the sink in that frame
@@ -364,22 +453,26 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
         L += tc::ex2(sink - (m_run == -INFINITY ? 0.f : m_run));
       }
       const float inv = L > 0.f ? 1.f / L : 0.f;
-      T* orow = reinterpret_cast<T*>(a.out) + (int64_t)(m.c0 + m.q0 + tl) * H * kD + (int64_t)(m.kh * g + hl) * kD;
-#pragma unroll 1
-      for (int c = 0; c < kD / 16; ++c) {
-        float r[16];
-        tc::ld16(tO + lane_off + c * 16, r);
+      T* orow = reinterpret_cast<T*>(a.out) + (int64_t)(m.c0 + tok) * H * kD + (int64_t)(m.kh * g + hl) * kD;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float o[2][32];
+        tc::ld32(obuf + h * 64, o[0]);
+        tc::ld32(obuf + h * 64 + 32, o[1]);
         tc::wait_ld();
         if (row_ok) {
-          uint32_t w[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) w[i] = MMA::pack(r[2 * i] * inv, r[2 * i + 1] * inv);
-          reinterpret_cast<uint4*>(orow + c * 16)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          reinterpret_cast<uint4*>(orow + c * 16)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t v[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) v[i] = MMA::pack(o[c][q * 8 + 2 * i] * inv, o[c][q * 8 + 2 * i + 1] * inv);
+              reinterpret_cast<uint4*>(orow + h * 64 + c * 32 + q * 8)[0] = make_uint4(v[0], v[1], v[2], v[3]);
+            }
         }
       }
       tc::fence_before_sync();
-      mbar_arrive(&bars.o_free);
     }
   }
 
@@ -393,23 +486,23 @@ cudaError_t launch_prefill(const AttnArgs& a, const DecodePlan& plan, const Pref
                            cudaStream_t stream) {
   const size_t smem = kSmemBytes + 1024;
   const bool bf = a.act_dtype == B200_DTYPE_BFLOAT16;
-  static bool attr_set[2] = {false, false};
-  cudaError_t e = cudaSuccess;
-  if (bf) {
-    if (!attr_set[1]) {
-      e = cudaFuncSetAttribute(paged_prefill_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-      attr_set[1] = true;
-    }
-    paged_prefill_kernel<__nv_bfloat16><<<num_sms, kThreads, smem, stream>>>(a, maps, plan);
-  } else {
-    if (!attr_set[0]) {
-      e = cudaFuncSetAttribute(paged_prefill_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-      attr_set[0] = true;
-    }
-    paged_prefill_kernel<__half><<<num_sms, kThreads, smem, stream>>>(a, maps, plan);
+  auto kernel = bf ? paged_prefill_kernel<__nv_bfloat16> : paged_prefill_kernel<__half>;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::atomic<uint32_t> ready[2][64];  // per dtype and device: attributes set and checked
+  std::atomic<uint32_t>& flag = ready[bf ? 1 : 0][dev & 63];
+  if (!flag.load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    // setmaxnreg.inc waits until the block's launch allocation can cover the split.
+    cudaFuncAttributes attr;
+    e = cudaFuncGetAttributes(&attr, kernel);
+    if (e != cudaSuccess) return e;
+    if (attr.numRegs * kThreads < kSplitRegs) return cudaErrorInvalidConfiguration;
+    flag.store(1, std::memory_order_release);
   }
+  kernel<<<num_sms, kThreads, smem, stream>>>(a, maps, plan);
   return cudaGetLastError();
 }
 
