@@ -42,6 +42,24 @@
 
 namespace b200 {
 
+// Optional per-event timestamps of CTA 0 (build with -DB200_PREFILL_TRACE): slot = 16 x counter +
+// event, events 0/1 S0/S1 issued, 2/3 PV0/PV1 issued, 4 K resident, 5 V resident, 6/7/8 and
+// 9/10/11 warpgroup 0/1 S loaded / P written / row stored, 12/13 K/V copy issued, 14/15 P0/P1
+// seen by the MMA issuer.
+#ifdef B200_PREFILL_TRACE
+constexpr int kTraceSlots = 1 << 16;
+__device__ long long g_prefill_trace[kTraceSlots];
+#define PF_TRACE(slot)                                                  \
+  do {                                                                  \
+    const int _s = (slot);                                              \
+    if (blockIdx.x == 0 && _s >= 0 && _s < kTraceSlots) g_prefill_trace[_s] = clock64(); \
+  } while (0)
+#else
+#define PF_TRACE(slot) \
+  do {                 \
+  } while (0)
+#endif
+
 namespace {
 
 constexpr int kBM = 128;             // q rows per tile
@@ -118,6 +136,10 @@ __device__ __forceinline__ Item decode_item(const AttnArgs& a, const DecodePlan&
   return m;
 }
 
+// K/V tiles of q tile w, by select (an indexed read with a run-time w would put the Item in
+// local memory)
+__device__ __forceinline__ int nkv_of(const Item& m, int w) { return w ? m.nkv[1] : m.nkv[0]; }
+
 }  // namespace
 
 bool prefill_supported(int head_size, int block_size, int group, int act_dtype, int cache_dtype) {
@@ -183,6 +205,12 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
     s_failed = 1;
     return false;
   };
+  // Warp-uniform bounded wait: every lane waits, then the warp agrees, so warp-collective code
+  // after it (tensor-memory loads/stores, __syncwarp) never runs with part of a warp.
+  auto wait_warp = [&](uint64_t* bar, uint32_t index) -> bool {
+    return __all_sync(0xffffffffu, wait_idx(bar, index));
+  };
+  auto failed_warp = [&]() -> bool { return __any_sync(0xffffffffu, s_failed != 0); };
   // After a failure: bounded wait for a copy or commit this CTA issued, without the early exit.
   auto drain_idx = [&](uint64_t* bar, uint32_t index) { mbar_wait(bar, index & 1u); };
 
@@ -196,13 +224,13 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
       // lane l loads box (page (l & 15) / 2, channel half l & 1) of K (l < 16) or V (l >= 16)
       const int page = (lane & 15) >> 1, half = lane & 1, is_v = lane >> 4;
       bool ok = true;
-      for (int64_t it = blockIdx.x; it < n_items && ok && !s_failed; it += gridDim.x) {
+      for (int64_t it = blockIdx.x; it < n_items && ok && !failed_warp(); it += gridDim.x) {
         const Item m = decode_item(a, plan, it);
         if (m.skip) continue;
         for (int w = 0; w < kQTiles && ok; ++w) {
-          if (m.nkv[w] == 0) continue;
+          if (nkv_of(m, w) == 0) continue;
           uint32_t& qc = w ? qc1 : qc0;
-          if (qc > 0 && !(ok = wait_idx(&bars.q_empty[w], qc - 1))) break;
+          if (qc > 0 && !(ok = wait_warp(&bars.q_empty[w], qc - 1))) break;
           if (lane == 0) mbar_arrive_expect_tx(&bars.q_full[w], kTileBytes);
           __syncwarp();
           if (lane < 2)
@@ -220,17 +248,19 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           const int off = half * kBoxBytes + page * (kTile * 128);
           // K tile j
           const int ks = kc % kKStages;
-          if (kc >= kKStages && !(ok = wait_idx(&bars.k_empty[ks], kc / kKStages - 1))) break;
+          if (kc >= kKStages && !(ok = wait_warp(&bars.k_empty[ks], kc / kKStages - 1))) break;
           if (lane == 0) mbar_arrive_expect_tx(&bars.k_full[ks], kTileBytes);
           __syncwarp();
           if (!is_v) tma_load_3d(smem + kSmemK + ks * kTileBytes + off, &maps.k_map, &bars.k_full[ks], half * 64, m.kh, z);
+          if (lane == 0) PF_TRACE(kc * 16 + 12);
           ++kc;
           // V tile j
           const int vs = vc % kVStages;
-          if (vc >= kVStages && !(ok = wait_idx(&bars.v_empty[vs], vc / kVStages - 1))) break;
+          if (vc >= kVStages && !(ok = wait_warp(&bars.v_empty[vs], vc / kVStages - 1))) break;
           if (lane == 0) mbar_arrive_expect_tx(&bars.v_full[vs], kTileBytes);
           __syncwarp();
           if (is_v) tma_load_3d(smem + kSmemV + vs * kTileBytes + off, &maps.v_map, &bars.v_full[vs], half * 64, m.kh, z);
+          if (lane == 0) PF_TRACE(vc * 16 + 13);
           ++vc;
         }
       }
@@ -241,82 +271,81 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
       for (uint32_t i = (vc > kVStages ? vc - kVStages : 0); i < vc; ++i) drain_idx(&bars.v_full[i % kVStages], i / kVStages);
     } else if (warp == kMmaWarp) {
       // ------------------------------------------------------------------ MMA issuer
-      if (lane == 0) {
-        uint32_t qc0 = 0, qc1 = 0, pc0 = 0, pc1 = 0, kvc = 0;
-        bool issued = false;
-        for (int64_t it = blockIdx.x; it < n_items && !s_failed; it += gridDim.x) {
-          const Item m = decode_item(a, plan, it);
-          if (m.skip) continue;
-          // S_w(j) = Q_w . K_j^T into the S_w columns
-          auto issue_s = [&](int w, int j) -> bool {
-            if (j == 0) {
-              if (!wait_idx(&bars.q_full[w], w ? qc1 : qc0)) return false;
-              tc::fence_after_sync();
-            }
-            const uint32_t kb = sbase + kSmemK + ((kvc + j) % kKStages) * kTileBytes;
-            const uint32_t qb = sbase + kSmemQ + w * kTileBytes;
-            for (int kk = 0; kk < kD / 16; ++kk) {
-              const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-              tc::mma_ss(tmem + w * 128, tc::smem_desc(qb + off, 16, 1024), tc::smem_desc(kb + off, 16, 1024), kIdQK,
-                         kk > 0);
-            }
-            tc::commit(&bars.s_full[w]);
-            if (j == m.nkv[w] - 1) {  // last use of Q_w in this item
-              tc::commit(&bars.q_empty[w]);
-              ++(w ? qc1 : qc0);
-            }
-            issued = true;
-            return true;
-          };
-          // O_w (+)= P_w(j) . V_j once the softmax has written P_w(j)
-          auto issue_pv = [&](int w, int j) -> bool {
-            if (!wait_idx(&bars.p_full[w], w ? pc1 : pc0)) return false;
-            tc::fence_after_sync();
-            const uint32_t pbuf = tmem + w * 128, obuf = tmem + 256 + w * 128;
-            const uint32_t vb = sbase + kSmemV + ((kvc + j) % kVStages) * kTileBytes;
-            for (int kk = 0; kk < kBN / 16; ++kk) {
-              const uint64_t vdesc = tc::smem_desc(vb + kk * 2048, kBoxBytes, 1024);
-              tc::mma_ts(obuf, pbuf + kk * 8, vdesc, kIdPV, (j > 0 || kk > 0) ? 1u : 0u);
-              tc::mma_ts(obuf, pbuf + 64 + kk * 8, vdesc, kIdPV, 1u);
-            }
-            tc::commit(&bars.o_done[w]);
-            ++(w ? pc1 : pc0);
-            return true;
-          };
-          auto wait_v = [&](int j) -> bool {  // V_j resident
-            if (!wait_idx(&bars.v_full[(kvc + j) % kVStages], (kvc + j) / kVStages)) return false;
-            tc::fence_after_sync();
-            return true;
-          };
-          // Per K/V tile j: PV0(j-1), S0(j), PV1(j-1), S1(j); a late K_j never holds back PV0(j-1).
-          bool ok = true;
-          for (int j = 0; j < m.n && ok; ++j) {
-            const uint32_t ki = kvc + j;
-            if (j > 0 && !(ok = wait_v(j - 1))) break;
-            if (j > 0 && j - 1 < m.nkv[0] && !(ok = issue_pv(0, j - 1))) break;
-            if (!(ok = wait_idx(&bars.k_full[ki % kKStages], ki / kKStages))) break;
-            tc::fence_after_sync();
-            if (j < m.nkv[0] && !(ok = issue_s(0, j))) break;
-            if (j > 0 && j - 1 < m.nkv[1] && !(ok = issue_pv(1, j - 1))) break;
-            if (j > 0) tc::commit(&bars.v_empty[(ki - 1) % kVStages]);
-            if (j < m.nkv[1] && !(ok = issue_s(1, j))) break;
-            tc::commit(&bars.k_empty[ki % kKStages]);
+      // The whole warp runs the schedule (waits, counters, descriptors stay warp-uniform and in
+      // uniform registers); one elected lane issues the MMAs and their commits.
+      const bool leader = tc::elect_one();
+      uint32_t qc0 = 0, qc1 = 0, pc0 = 0, pc1 = 0, kvc = 0;
+      bool issued = false, ok = true;
+      for (int64_t it = blockIdx.x; it < n_items && ok && !failed_warp(); it += gridDim.x) {
+        const Item m = decode_item(a, plan, it);
+        if (m.skip) continue;
+        // Step j issues PV0(j-1), S0(j), PV1(j-1), S1(j) (step n: the last PVs only), each from
+        // one call site so the issuing loop stays small; a late K_j never holds back PV0(j-1).
+#pragma unroll 1
+        for (int j = 0; j <= m.n && ok; ++j) {
+          const uint32_t ki = kvc + j, vi = ki - 1;
+          if (j > 0) {
+            if (!(ok = wait_warp(&bars.v_full[vi % kVStages], vi / kVStages))) break;
+            PF_TRACE(vi * 16 + 5);
           }
-          if (ok) {
-            const int j = m.n - 1;
-            ok = wait_v(j);
-            if (ok && j < m.nkv[0]) ok = issue_pv(0, j);
-            if (ok && j < m.nkv[1]) ok = issue_pv(1, j);
-            if (ok) tc::commit(&bars.v_empty[(kvc + j) % kVStages]);
+          bool k_ready = false;
+#pragma unroll 1
+          for (int w = 0; w < kQTiles; ++w) {
+            const uint32_t pc = w ? pc1 : pc0;  // values, not references: no local memory
+            if (j > 0 && j - 1 < nkv_of(m, w)) {  // O_w (+)= P_w(j-1) . V_(j-1)
+              if (!(ok = wait_warp(&bars.p_full[w], pc))) break;
+              tc::fence_after_sync();  // P was written to tensor memory by the softmax threads
+              PF_TRACE(pc * 16 + 14 + w);
+              const uint32_t pbuf = tmem + w * 128, obuf = tmem + 256 + w * 128;
+              const uint32_t vb = sbase + kSmemV + (vi % kVStages) * kTileBytes;
+#pragma unroll
+              for (int kk = 0; kk < kBN / 16; ++kk) {
+                const uint64_t vdesc = tc::smem_desc(vb + kk * 2048, kBoxBytes, 1024);
+                // P of keys 16kk..16kk+15: hi at chunk kk/2's columns (kk%2)*8.., lo 16 columns on
+                const uint32_t pcol = pbuf + (kk >> 1) * 32 + (kk & 1) * 8;
+                if (leader) {
+                  tc::mma_ts(obuf, pcol, vdesc, kIdPV, (j > 1 || kk > 0) ? 1u : 0u);
+                  tc::mma_ts(obuf, pcol + 16, vdesc, kIdPV, 1u);
+                }
+              }
+              if (leader) tc::commit(&bars.o_done[w]);
+              PF_TRACE(pc * 16 + 2 + w);
+              if (w) pc1 = pc + 1; else pc0 = pc + 1;
+            }
+            if (j < nkv_of(m, w)) {  // S_w(j) = Q_w . K_j^T into the S_w columns
+              if (!k_ready) {  // K and Q arrive by TMA: the mbarrier wait orders them for the MMA
+                if (!(ok = wait_warp(&bars.k_full[ki % kKStages], ki / kKStages))) break;
+                PF_TRACE(ki * 16 + 4);
+                k_ready = true;
+              }
+              if (j == 0 && !(ok = wait_warp(&bars.q_full[w], w ? qc1 : qc0))) break;
+              const uint32_t kb = sbase + kSmemK + (ki % kKStages) * kTileBytes;
+              const uint32_t qb = sbase + kSmemQ + w * kTileBytes;
+#pragma unroll
+              for (int kk = 0; kk < kD / 16; ++kk) {
+                const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                const uint64_t qdesc = tc::smem_desc(qb + off, 16, 1024), kdesc = tc::smem_desc(kb + off, 16, 1024);
+                if (leader) tc::mma_ss(tmem + w * 128, qdesc, kdesc, kIdQK, kk > 0);
+              }
+              if (leader) tc::commit(&bars.s_full[w]);
+              PF_TRACE((w ? pc1 : pc0) * 16 + w);
+              if (j == nkv_of(m, w) - 1) {  // last use of Q_w in this item
+                if (leader) tc::commit(&bars.q_empty[w]);
+                if (w) ++qc1; else ++qc0;
+              }
+              issued = true;
+            }
           }
-          kvc += m.n;
           if (!ok) break;
+          if (leader && j > 0) tc::commit(&bars.v_empty[vi % kVStages]);
+          if (leader && k_ready) tc::commit(&bars.k_empty[ki % kKStages]);
         }
-        // Every issued MMA completes before tensor memory is freed (immediate on the normal path).
-        if (issued) {
-          tc::commit(&bars.drain);
-          drain_idx(&bars.drain, 0);
-        }
+        kvc += m.n;
+      }
+      // Every issued MMA completes before tensor memory is freed (immediate on the normal path).
+      if (issued) {
+        if (leader) tc::commit(&bars.drain);
+        drain_idx(&bars.drain, 0);
       }
       __syncwarp();
     }
@@ -329,73 +358,74 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
     const uint32_t sbuf = tmem + w * 128 + lane_off, obuf = tmem + 256 + w * 128 + lane_off;
     const float qk_scale = a.softcap > 0.f ? a.scale : a.scale * kLog2eP;
     uint32_t t = 0;  // tiles this warpgroup has processed
-    for (int64_t it = blockIdx.x; it < n_items && !s_failed; it += gridDim.x) {
+    for (int64_t it = blockIdx.x; it < n_items && !failed_warp(); it += gridDim.x) {
       const Item m = decode_item(a, plan, it);
-      if (m.skip || m.nkv[w] == 0) continue;
+      if (m.skip || nkv_of(m, w) == 0) continue;
       const int tl = row / g, hl = row % g;
       const int tok = m.q0 + w * TQ + tl;
       const bool row_ok = tl < TQ && tok < m.nq;
       const int qpos = m.past + tok;
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
-      for (int j = 0; j < m.nkv[w]; ++j, ++t) {
-        if (!(ok = wait_idx(&bars.s_full[w], t))) break;
+      for (int j = 0; j < nkv_of(m, w); ++j, ++t) {
+        if (!(ok = wait_warp(&bars.s_full[w], t))) break;
         tc::fence_after_sync();
-        float sv[kBN / 32][32];
-#pragma unroll
-        for (int c = 0; c < kBN / 32; ++c) tc::ld32(sbuf + c * 32, sv[c]);
-        tc::wait_ld();
+        if (row == 0) PF_TRACE(t * 16 + 6 + 3 * w);
         const int kbase = m.kv_lo + j * kBN;
         // Masks only where a key can be invisible to this row (diagonal tile, sequence end, window).
         const bool full = row_ok && kbase + kBN <= m.total && (!a.is_causal || kbase + kBN - 1 <= qpos) &&
                           (a.window <= 0 || kbase >= qpos - a.window + 1) && a.softcap <= 0.f;
         // In the unmasked case the scores stay raw and scale folds into the exponent's FMA
-        // (qk_scale > 0); masked tiles are rewritten to scaled log2 values (-inf = masked).
-        const bool raw = full && qk_scale > 0.f;
-        float m_tile;
-        if (raw) {
-          float mx[8];
+        // (qk_scale > 0); masked tiles are rewritten in place to scaled log2 values (-inf = masked).
+        // Warp-uniform: both paths use tensor-memory loads/stores, which the whole warp executes
+        // together (the masked path is also exact for rows that see the whole tile).
+        const bool raw = __all_sync(0xffffffffu, full && qk_scale > 0.f);
+        float mx[4];
 #pragma unroll
-          for (int r = 0; r < 8; ++r) mx[r] = -INFINITY;
+        for (int r = 0; r < 4; ++r) mx[r] = -INFINITY;
+        if (raw) {
+          float sv[kBN / 32][32];
+#pragma unroll
+          for (int c = 0; c < kBN / 32; ++c) tc::ld32(sbuf + c * 32, sv[c]);
+          tc::wait_ld();
 #pragma unroll
           for (int c = 0; c < kBN / 32; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], sv[c][i]);
-          m_tile = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-          m_tile *= qk_scale;
+            for (int i = 0; i < 16; ++i) mx[i & 3] = tc::max3(mx[i & 3], sv[c][2 * i], sv[c][2 * i + 1]);
         } else {
           // Keys this row sees, as a column range [vlo, vhi] of the tile (empty for padding rows).
           const int vhi = row_ok ? min(m.total - 1, a.is_causal ? qpos : m.total - 1) - kbase : -1;
           const int vlo = (a.window > 0 ? qpos - a.window + 1 : 0) - kbase;
-          if (a.softcap > 0.f) {
-            // cap * tanh(y / cap) in the log2 domain, tanh(u) = 1 - 2 / (1 + e^(2u)).
-            const float two_log2e_over_cap = 2.f * kLog2eP / a.softcap, cap_log2e = a.softcap * kLog2eP;
-#pragma unroll
-            for (int c = 0; c < kBN / 32; ++c)
+#pragma unroll 1
+          for (int c = 0; c < kBN / 32; ++c) {
+            float x[32];
+            tc::ld32(sbuf + c * 32, x);
+            tc::wait_ld();
+            if (a.softcap > 0.f) {
+              // cap * tanh(y / cap) in the log2 domain, tanh(u) = 1 - 2 / (1 + e^(2u)).
+              const float two_log2e_over_cap = 2.f * kLog2eP / a.softcap, cap_log2e = a.softcap * kLog2eP;
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
-                const float e = tc::ex2(fminf(sv[c][i] * qk_scale * two_log2e_over_cap, 126.f));
-                sv[c][i] = cap_log2e * (1.f - __fdividef(2.f, 1.f + e));
+                const float e = tc::ex2(fminf(x[i] * qk_scale * two_log2e_over_cap, 126.f));
+                x[i] = cap_log2e * (1.f - __fdividef(2.f, 1.f + e));
               }
-          } else {
+            } else {
 #pragma unroll
-            for (int c = 0; c < kBN / 32; ++c)
-#pragma unroll
-              for (int i = 0; i < 32; ++i) sv[c][i] *= qk_scale;
-          }
-          float mx[8];
-#pragma unroll
-          for (int r = 0; r < 8; ++r) mx[r] = -INFINITY;
-#pragma unroll
-          for (int c = 0; c < kBN / 32; ++c)
+              for (int i = 0; i < 32; ++i) x[i] *= qk_scale;
+            }
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               const int col = c * 32 + i;
-              sv[c][i] = (col >= vlo && col <= vhi) ? sv[c][i] : -INFINITY;
-              mx[i & 7] = fmaxf(mx[i & 7], sv[c][i]);
+              x[i] = (col >= vlo && col <= vhi) ? x[i] : -INFINITY;
             }
-          m_tile = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+#pragma unroll
+            for (int i = 0; i < 16; ++i) mx[i & 3] = tc::max3(mx[i & 3], x[2 * i], x[2 * i + 1]);
+            tc::st32(sbuf + c * 32, x);
+          }
+          tc::wait_st();
         }
+        float m_tile = tc::max3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
+        if (raw) m_tile *= qk_scale;
         // Lazy rescale: the reference max moves only when the row max grows by more than 2^8.
         const float m_new = fmaxf(m_run, m_tile);
         const bool grow = m_new > m_run + 8.0f;
@@ -406,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
         }
         if (j > 0 && __any_sync(0xffffffffu, grow && alpha != 1.0f)) {
           // O holds tiles < j: wait for PV of tile j-1, then scale this warp's rows in place.
-          if (!(ok = wait_idx(&bars.o_done[w], t - 1))) break;
+          if (!(ok = wait_warp(&bars.o_done[w], t - 1))) break;
           tc::fence_after_sync();
 #pragma unroll 1
           for (int c = 0; c < kD / 16; ++c) {
@@ -419,33 +449,48 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           }
           tc::wait_st();
         }
-        // P = 2^(s - m_run) as hi + lo 16-bit halves over the S columns: hi in [0,64), lo in [64,128)
+        // P = 2^(s * kscale - mu) as hi + lo 16-bit halves, per 32-column chunk of S: hi over the
+        // chunk's first 16 columns, lo over its last 16 (each chunk is read before it is overwritten)
         const float mu = m_run == -INFINITY ? 0.f : m_run;
-        const float kscale = raw ? qk_scale : 1.0f;  // p = 2^(s * kscale - mu)
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
+        const float kscale = raw ? qk_scale : 1.0f;
+        const float2 ks2 = make_float2(kscale, kscale), nmu2 = make_float2(-mu, -mu);
+        float2 ls[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll 1
         for (int c = 0; c < kBN / 32; ++c) {
+          float x[32];
+          tc::ld32(sbuf + c * 32, x);
+          tc::wait_ld();
           uint32_t hi[16], lo[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float p0 = tc::ex2(fmaf(sv[c][2 * i], kscale, -mu));
-            const float p1 = tc::ex2(fmaf(sv[c][2 * i + 1], kscale, -mu));
-            ls[i & 3] += p0 + p1;
-            hi[i] = MMA::pack(p0, p1);
-            const float2 h = MMA::unpack(hi[i]);
-            lo[i] = MMA::pack(p0 - h.x, p1 - h.y);
+            const float2 e = tc::fma2(make_float2(x[2 * i], x[2 * i + 1]), ks2, nmu2);
+            const float2 p = make_float2(tc::ex2(e.x), tc::ex2(e.y));
+            ls[i & 1] = tc::add2(ls[i & 1], p);
+            if (kBF16) {
+              // hi = p truncated to bf16 (its upper 16 bits), lo = p - hi exactly, then rounded
+              const uint32_t u0 = __float_as_uint(p.x), u1 = __float_as_uint(p.y);
+              hi[i] = __byte_perm(u0, u1, 0x7632);
+              const float2 l = tc::sub2(p, make_float2(__uint_as_float(u0 & 0xffff0000u), __uint_as_float(u1 & 0xffff0000u)));
+              lo[i] = MMA::pack(l.x, l.y);
+            } else {
+              hi[i] = MMA::pack(p.x, p.y);
+              const float2 h = MMA::unpack(hi[i]);
+              const float2 l = tc::sub2(p, h);
+              lo[i] = MMA::pack(l.x, l.y);
+            }
           }
-          tc::st16u(sbuf + c * 16, hi);
-          tc::st16u(sbuf + 64 + c * 16, lo);
+          tc::st16u(sbuf + c * 32, hi);
+          tc::st16u(sbuf + c * 32 + 16, lo);
         }
-        l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        l_run += (ls[0].x + ls[1].x) + (ls[0].y + ls[1].y);
         tc::wait_st();
         tc::fence_before_sync();
         mbar_arrive(&bars.p_full[w]);
+        if (row == 0) PF_TRACE(t * 16 + 7 + 3 * w);
       }
       if (!ok) break;
       // ---- epilogue: last PV done -> normalise -> store this row
-      if (!wait_idx(&bars.o_done[w], t - 1)) break;
+      if (!wait_warp(&bars.o_done[w], t - 1)) break;
       tc::fence_after_sync();
       float L = l_run;
       if (a.head_sink) {  // l is relative to the reference max m_run; fold the sink in that frame
@@ -472,6 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
             }
         }
       }
+      if (row == 0) PF_TRACE((t - 1) * 16 + 8 + 3 * w);
       tc::fence_before_sync();
     }
   }
@@ -505,5 +551,15 @@ cudaError_t launch_prefill(const AttnArgs& a, const DecodePlan& plan, const Pref
   kernel<<<num_sms, kThreads, smem, stream>>>(a, maps, plan);
   return cudaGetLastError();
 }
+
+#ifdef B200_PREFILL_TRACE
+extern "C" __attribute__((visibility("default"))) int b200_prefill_trace_dump(long long* host, int clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(host, g_prefill_trace, sizeof(long long) * kTraceSlots);
+  void* dev = nullptr;
+  if (e == cudaSuccess && clear) e = cudaGetSymbolAddress(&dev, g_prefill_trace);
+  if (e == cudaSuccess && clear) e = cudaMemset(dev, 0, sizeof(long long) * kTraceSlots);
+  return (int)e;
+}
+#endif
 
 }  // namespace b200
