@@ -191,6 +191,25 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
+// 2^x for a pair on the FMA pipe, to take part of a softmax's exponentials off the MUFU unit.
+// x = n + f with n = round(x) by the 1.5 * 2^23 shift and f in [-1/2, 1/2]; 2^f by a degree-4
+// polynomial minimax in relative error (coefficients from exp2_poly_fit.py, max relative error
+// 2.7e-6); n goes into the exponent field.  x is clamped to >= -125 so the result stays normal:
+// a masked score (-inf) gives 2^-125 instead of 0, which no fp32 or 16-bit sum can see.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 shift = make_float2(12582912.f, 12582912.f);  // 1.5 * 2^23: rounds x to an integer
+  const float2 t = add2(x, shift);
+  const float2 f = sub2(x, sub2(t, shift));
+  float2 p = fma2(make_float2(0.00957010221f, 0.00957010221f), f, make_float2(0.0559178591f, 0.0559178591f));
+  p = fma2(p, f, make_float2(0.240247443f, 0.240247443f));
+  p = fma2(p, f, make_float2(0.693121791f, 0.693121791f));
+  p = fma2(p, f, make_float2(0.999999285f, 0.999999285f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 // Hardware base-2 exponential (PTX ex2.approx.ftz.f32); ex2(-inf) = 0.
 __device__ __forceinline__ float ex2(float x) {
   float y;

@@ -71,6 +71,7 @@ constexpr int kVStages = 3;          // V pipeline depth
 constexpr int kBoxBytes = 128 * 128; // one [128 rows][64 channels] 16-bit box: 16 KB
 constexpr int kTileBytes = 2 * kBoxBytes;  // [128][128] 16-bit tile: 32 KB
 constexpr float kLog2eP = 1.4426950408889634f;
+constexpr int kPolyEvery = 4;        // every 4th exponential pair of a softmax on the FMA pipe
 
 // shared-memory map (offsets from the 1024-aligned base)
 constexpr int kSmemQ = 0;                                   // kQTiles Q tiles
@@ -455,16 +456,14 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
         const float kscale = raw ? qk_scale : 1.0f;
         const float2 ks2 = make_float2(kscale, kscale), nmu2 = make_float2(-mu, -mu);
         float2 ls[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
-          float x[32];
-          tc::ld32(sbuf + c * 32, x);
-          tc::wait_ld();
+        auto exp_chunk = [&](const float(&x)[32], int c) {
           uint32_t hi[16], lo[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float2 e = tc::fma2(make_float2(x[2 * i], x[2 * i + 1]), ks2, nmu2);
-            const float2 p = make_float2(tc::ex2(e.x), tc::ex2(e.y));
+            // every kPolyEvery-th pair on the FMA pipe, the rest on the MUFU unit
+            const float2 p = (kPolyEvery > 0 && i % kPolyEvery == kPolyEvery - 1) ? tc::exp2_poly2(e)
+                                                                                   : make_float2(tc::ex2(e.x), tc::ex2(e.y));
             ls[i & 1] = tc::add2(ls[i & 1], p);
             if (kBF16) {
               // hi = p truncated to bf16 (its upper 16 bits), lo = p - hi exactly, then rounded
@@ -481,6 +480,19 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           }
           tc::st16u(sbuf + c * 32, hi);
           tc::st16u(sbuf + c * 32 + 16, lo);
+        };
+        // Chunk c+1's tensor-memory load is in flight while chunk c is exponentiated.
+        float xa[32], xb[32];
+        tc::ld32(sbuf, xa);
+        tc::wait_ld();
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; c += 2) {
+          tc::ld32(sbuf + (c + 1) * 32, xb);
+          exp_chunk(xa, c);
+          tc::wait_ld();
+          if (c + 2 < kBN / 32) tc::ld32(sbuf + (c + 2) * 32, xa);
+          exp_chunk(xb, c + 1);
+          tc::wait_ld();
         }
         l_run += (ls[0].x + ls[1].x) + (ls[0].y + ls[1].y);
         tc::wait_st();
