@@ -396,7 +396,7 @@ def run_b200(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": peak_src, "frac_of_8tbs": achieved / 8000.0,
-                         "kernel": "attention section (paged_decode_kernel + decode_combine_kernel)",
+                         "kernel": "attention section (paged_decode_kernel, split-K combine fused in)",
                          "alg_bytes_per_launch": alg_bytes, "ms_per_launch": attn_ms},
             "cpu_baseline": cpu,
             "e2e": e2e,

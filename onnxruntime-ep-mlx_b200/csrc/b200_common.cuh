@@ -1,7 +1,7 @@
 // Shared device helpers for the B200 paged-KV attention kernels (sm_100a).
 //
 // Element access for every cache storage type, the device status word, and thin inline-PTX
-// wrappers for mbarrier, TMA (cp.async.bulk.tensor, no multicast), ldmatrix / movmatrix and
+// wrappers for mbarrier, TMA (cp.async.bulk.tensor, single-CTA destination), ldmatrix / movmatrix and
 // the m16n8k16 tensor-core MMA.  Every spin-wait is bounded by %globaltimer and reports a
 // timeout through the status word instead of hanging.
 #pragma once
@@ -181,7 +181,7 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// 3-D tiled TMA load global -> shared, completion counted on an mbarrier (no multicast).
+// 3-D tiled TMA load global -> this CTA's shared memory, completion counted on an mbarrier.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
                                             int z) {
   asm volatile(

@@ -14,8 +14,8 @@
 //  * paged_decode_kernel is persistent (grid = SMs x resident CTAs) and every warp owns an
 //    equal contiguous range of that stream (stream-K: exact balance for ragged lengths, no
 //    scheduling atomics).  A warp streams its tiles through a private STAGES-deep ring of
-//    shared-memory stages filled by TMA (cp.async.bulk.tensor.3d, 128-byte swizzle, no
-//    multicast) from the [NB*bs, KV, d] cache view; the lookahead runs across (sequence, kv
+//    shared-memory stages filled by TMA (cp.async.bulk.tensor.3d, 128-byte swizzle,
+//    single-CTA destination) from the [NB*bs, KV, d] cache view; the lookahead runs across (sequence, kv
 //    head) boundaries, so the ring never drains;
 //  * the g = H/KV query heads of a kv head (times the unit's queries, <= 8 rows) are batched
 //    into one tensor-core tile: S^T[16 tok x 8 rows] = K_tile[16 x d] . Q^T via
