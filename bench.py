@@ -55,9 +55,10 @@ def parse():
     ap.add_argument("--pool-blocks", type=int, default=NB_PER_GPU, help="KV pool blocks per GPU")
     ap.add_argument("--mixed-chunks", type=int, default=8, help="mixed workload: prefill chunks")
     ap.add_argument("--mixed-decode", type=int, default=120, help="mixed workload: decode rows")
-    ap.add_argument("--workload", default="decode", choices=["decode", "mixed"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "mixed", "append"],
                     help="decode = BASELINE config 3 (the metric); mixed = config 4 (8 x 2048-token "
-                         "prefill chunks + 120 decode rows, 64q/8kv)")
+                         "prefill chunks + 120 decode rows, 64q/8kv); append = config 2 (KV append alone)")
+    ap.add_argument("--append-tokens", type=int, default=256, help="append workload: new tokens per call")
     return ap.parse_args()
 
 
@@ -493,10 +494,93 @@ def run_mixed(args):
     print(json.dumps(line), flush=True)
 
 
+def run_append(args):
+    """KV append alone.  256 new bf16 tokens (8 kv heads x 128) scattered by
+    slot_mapping (a seeded permutation of the pool's slots, about 10 % set to -1) into two
+    [65536, 16, 8, 128] pools, plus the scaled variant with 65536 tokens where GB/s is meaningful.
+    Each call is timed alone (event pair) with L2 flushed in between."""
+    import ctypes
+
+    import torch
+
+    from onnxruntime_ep_b200 import _capi, paged
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    nb, kvh, bs = 65536, 8, 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(2)
+    kc = torch.full((nb, bs, kvh, D), -7.0, dtype=torch.bfloat16, device=dev)  # sentinel
+    vc = torch.full_like(kc, -7.0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    results = {}
+    for nt in sorted({args.append_tokens, 65536}):
+        rng = np.random.default_rng(2)
+        slots = rng.permutation(nb * bs)[:nt].astype(np.int32)
+        slots[rng.choice(nt, size=nt // 10, replace=False)] = -1
+        valid = int((slots >= 0).sum())
+        k = torch.randn((nt, kvh * D), generator=g, device=dev).to(torch.bfloat16)
+        v = torch.randn((nt, kvh * D), generator=g, device=dev).to(torch.bfloat16)
+        cum = torch.tensor([0, nt], dtype=torch.int32, device=dev)
+        past = torch.zeros(1, dtype=torch.int32, device=dev)
+        # the table must cover the chunk's logical positions (total <= max_blocks * bs) even
+        # though slot_mapping decides where rows land
+        bt = (torch.arange(-(-nt // bs), dtype=torch.int32, device=dev) % nb).reshape(1, -1)
+        sm = torch.from_numpy(slots).to(dev)
+        # params built once; the timed region holds only the C-ABI call (b200_kv_append)
+        p, keep, _ = paged.build_params(k, k, v, kc, vc, cum, past, bt, num_heads=kvh, kv_num_heads=kvh,
+                                        slot_mapping=sm, kv_only=True)
+        stream = torch.cuda.current_stream(dev)
+        pp, sp = ctypes.byref(p), ctypes.c_void_p(stream.cuda_stream)
+        for _ in range(args.warmup):
+            _capi.check(_capi.LIB.b200_kv_append(pp, sp))
+        _capi.check(_capi.LIB.b200_read_status(pp, sp))
+        steps = max(args.steps, 20)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        launches0 = _capi.LIB.b200_launch_count()
+        for a_, b_ in ev:
+            flush.fill_(1)  # L2 flush between timed calls (not timed)
+            a_.record(stream)
+            _capi.check(_capi.LIB.b200_kv_append(pp, sp))
+            b_.record(stream)
+        torch.cuda.synchronize()
+        launches = (_capi.LIB.b200_launch_count() - launches0) / steps
+        _capi.check(_capi.LIB.b200_read_status(pp, sp))
+        del keep
+        ms = [a_.elapsed_time(b_) for a_, b_ in ev]
+        med = statistics.median(ms)
+        alg = 2 * valid * kvh * D * 2 * 2 + nt * 4  # K+V rows read and written, slots read
+        results[nt] = {"us_per_call": med * 1e3, "p10_us": float(np.percentile(ms, 10)) * 1e3,
+                       "p90_us": float(np.percentile(ms, 90)) * 1e3, "valid_rows": valid,
+                       "alg_bytes": alg, "gbs": alg / (med * 1e-3) / 1e9, "launches_per_call": launches}
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm = peaks.get("hbm_gbs", 6448.7)
+    small, big = results[args.append_tokens], results[65536]
+    line = {"metric": "paged KV append time (config 2)", "value": small["us_per_call"], "unit": "us/call",
+            "higher_is_better": False, "n_gpus": 1, "steps": max(args.steps, 20), "warmup": args.warmup,
+            "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": {"workload": "BASELINE config 2: KV append alone, 256 tokens x 8 kv heads x 128, bf16, "
+                                   "pool 2 x [65536, 16, 8, 128], slot_mapping = seeded permutation with ~10% -1",
+                       "l2": "flushed between calls (256 MiB write, untimed)"},
+            "small": small, "scaled_65536_tokens": big,
+            "roofline": {"bound": "hbm", "achieved": big["gbs"], "peak": hbm, "unit": "GB/s",
+                         "frac": big["gbs"] / hbm, "basis": "scaled variant (65536 tokens)"},
+            "gpu_launches": int(round(small["launches_per_call"] * max(args.steps, 20)))}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.workload == "mixed":
         run_mixed(args)
+        return
+    if args.workload == "append":
+        run_append(args)
         return
     if args.impl == "reference":
         run_reference(args)

@@ -383,7 +383,8 @@ size_t b200_node_info_size(void) { return sizeof(B200NodeInfo); }
 const char* b200_last_error(void) { return g_last_error.c_str(); }
 
 int b200_paged_attention_workspace_size(const B200PagedAttentionParams* p, size_t* bytes) {
-  int rc = check_params(p, false);
+  // Sizing depends on shapes only, so an append-only caller (no query / output) may ask too.
+  int rc = check_params(p, true);
   if (rc) return rc;
   if (!bytes) return fail(B200_ERR_INVALID_ARGUMENT, "PagedAttention: null bytes pointer");
   *bytes = make_layout(p).total;

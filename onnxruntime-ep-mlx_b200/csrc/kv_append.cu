@@ -46,9 +46,11 @@ __device__ __forceinline__ bool token_slot(const PrologueArgs& a, int t, int b, 
 }
 
 // Device-side metadata validation (the checks of attention.rs:3934-3990) and, when asked,
-// the slot -> last-token table.  One thread per sequence and one per token.
+// the slot -> last-token table.  Thread i checks sequence i, block-table entry i (sequence
+// i / max_blocks, entry i % max_blocks, if the sequence needs it) and token i, so no thread
+// walks a whole block-table row.
 __global__ void meta_check_kernel(PrologueArgs a) {
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < a.batch) {
     int c0 = a.cum[i], c1 = a.cum[i + 1];
     int bits = 0;
@@ -57,21 +59,25 @@ __global__ void meta_check_kernel(PrologueArgs a) {
     if (p < 0) bits |= kStatusBadPast;
     int64_t total = (int64_t)p + (c1 - c0);
     if (total > (int64_t)a.max_blocks * a.block_size) bits |= kStatusBadCapacity;
-    if (!(bits & (kStatusBadPast | kStatusBadCapacity)) && c1 >= c0) {
-      int64_t needed = (total + a.block_size - 1) / a.block_size;
-      const int32_t* row = a.block_table + (int64_t)i * a.max_blocks;
-      for (int64_t j = 0; j < needed; ++j) {
-        int32_t blk = row[j];
-        if (blk < 0 || blk >= a.num_blocks) { bits |= kStatusBadBlock; break; }
-      }
-    }
     if (a.rotary_positions > 0 && total > a.rotary_positions) bits |= kStatusBadPosition;
     if (bits) set_status(a.status, bits);
   }
+  if (a.max_blocks > 0 && i < (int64_t)a.batch * a.max_blocks) {
+    const int b = (int)(i / a.max_blocks);
+    const int j = (int)(i % a.max_blocks);
+    const int c0 = a.cum[b], c1 = a.cum[b + 1], p = a.past[b];
+    const int64_t total = (int64_t)p + (c1 - c0);
+    if (p >= 0 && c1 >= c0 && total <= (int64_t)a.max_blocks * a.block_size &&
+        j < (total + a.block_size - 1) / a.block_size) {
+      const int32_t blk = a.block_table[i];
+      if (blk < 0 || blk >= a.num_blocks) set_status(a.status, kStatusBadBlock);
+    }
+  }
   if (i < a.num_tokens) {
-    int b = seq_of_token(a.cum, a.batch, i);
+    const int t = (int)i;
+    int b = seq_of_token(a.cum, a.batch, t);
     int64_t slot;
-    if (!token_slot(a, i, b, slot)) {
+    if (!token_slot(a, t, b, slot)) {
       set_status(a.status, a.slot_mapping ? kStatusBadSlot : kStatusBadBlock);
       return;
     }
@@ -81,7 +87,7 @@ __global__ void meta_check_kernel(PrologueArgs a) {
     for (uint32_t probe = 0; probe < a.owner_capacity; ++probe) {
       int prev = atomicCAS(&a.owner_keys[h], -1, (int)slot);
       if (prev == -1 || prev == (int)slot) {
-        atomicMax(&a.owner_vals[h], i);
+        atomicMax(&a.owner_vals[h], t);
         return;
       }
       h = (h + 1) & mask;
@@ -142,8 +148,78 @@ __device__ void write_cache_row(const PrologueArgs& a, bool is_key, int64_t slot
   }
 }
 
-// One CTA per token.  Shared memory (processing path): fp32 rows [H*d] for Q and [KV*d] for
-// K, plus [KV*d] for V when the cache is integer/fp8 encoded.
+// The prefill kernel reads this call's new keys back from the cache; a prefill sequence may
+// stay on it only when every new row lands in its own block-table slot.
+__device__ __forceinline__ void refine_route(const PrologueArgs& a, int t, int b, int64_t slot, bool write) {
+  if (!a.route || a.route[b] != kRoutePrefill) return;
+  bool canonical = write;
+  if (canonical && a.slot_mapping) {
+    const int64_t logical = (int64_t)a.past[b] + (t - a.cum[b]);
+    const int64_t page = logical / a.block_size;
+    canonical = page < a.max_blocks &&
+                slot == (int64_t)a.block_table[(int64_t)b * a.max_blocks + page] * a.block_size +
+                            logical % a.block_size;
+  }
+  if (!canonical) a.route[b] = kRouteGeneric;
+}
+
+// Plain reshape-and-cache (no norm / RoPE, cache in the activation type): one warp per token,
+// kCopyTokensPerCta tokens per CTA.  The token's [KV*d] K and V rows are contiguous in the
+// input and in the pool; each lane issues all its 16-byte loads of both rows before storing.
+constexpr int kCopyTokensPerCta = 8;
+constexpr int kCopyUnroll = 4;
+
+__global__ void __launch_bounds__(32 * kCopyTokensPerCta) kv_copy_kernel(PrologueArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kCopyTokensPerCta + warp;
+  if (t >= a.num_tokens) return;  // whole warp
+  const int b = seq_of_token(a.cum, a.batch, t);
+  int64_t slot = -1;
+  const bool valid = token_slot(a, t, b, slot);
+  const bool write = valid && slot >= 0 && owns_slot(a, t, slot);
+  if (lane == 0) {
+    if (!valid) set_status(a.status, a.slot_mapping ? kStatusBadSlot : kStatusBadBlock);
+    refine_route(a, t, b, slot, write);
+  }
+  if (!write) return;  // whole warp
+  const int64_t bytes = (int64_t)a.kv_heads * a.head_size * 2;
+  char* kdst = reinterpret_cast<char*>(a.key_cache) + slot * bytes;
+  char* vdst = reinterpret_cast<char*>(a.value_cache) + slot * bytes;
+  const char* ksrc = reinterpret_cast<const char*>(a.key) + (int64_t)t * a.key_stride * 2;
+  const char* vsrc = reinterpret_cast<const char*>(a.value) + (int64_t)t * a.value_stride * 2;
+  const bool vec = ((reinterpret_cast<uintptr_t>(kdst) | reinterpret_cast<uintptr_t>(vdst) |
+                     reinterpret_cast<uintptr_t>(ksrc) | reinterpret_cast<uintptr_t>(vsrc) | bytes) & 15) == 0;
+  if (vec) {
+    const int64_t n16 = bytes / 16;
+    for (int64_t j0 = 0; j0 < n16; j0 += 32 * kCopyUnroll) {
+      uint4 kr[kCopyUnroll], vr[kCopyUnroll];
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t j = j0 + u * 32 + lane;
+        if (j < n16) {
+          kr[u] = __ldg(reinterpret_cast<const uint4*>(ksrc) + j);
+          vr[u] = __ldg(reinterpret_cast<const uint4*>(vsrc) + j);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t j = j0 + u * 32 + lane;
+        if (j < n16) {
+          reinterpret_cast<uint4*>(kdst)[j] = kr[u];
+          reinterpret_cast<uint4*>(vdst)[j] = vr[u];
+        }
+      }
+    }
+  } else {
+    for (int64_t j = lane; j < bytes / 2; j += 32) {
+      reinterpret_cast<uint16_t*>(kdst)[j] = reinterpret_cast<const uint16_t*>(ksrc)[j];
+      reinterpret_cast<uint16_t*>(vdst)[j] = reinterpret_cast<const uint16_t*>(vsrc)[j];
+    }
+  }
+}
+
+// One CTA per token, for the processing paths (RMS norm / RoPE, integer or fp8 caches).  Shared
+// memory: fp32 rows [H*d] for Q and [KV*d] for K, plus [KV*d] for V when the cache is encoded.
 __global__ void kv_prologue_kernel(PrologueArgs a) {
   extern __shared__ float smem[];
   const int t = blockIdx.x;
@@ -156,48 +232,10 @@ __global__ void kv_prologue_kernel(PrologueArgs a) {
   bool valid = token_slot(a, t, b, slot);
   bool write = valid && slot >= 0 && owns_slot(a, t, slot);
   if (!valid && tid == 0) set_status(a.status, a.slot_mapping ? kStatusBadSlot : kStatusBadBlock);
-  if (a.route && tid == 0 && a.route[b] == kRoutePrefill) {
-    // The prefill kernel reads this call's new keys back from the cache; it may only do so
-    // when this token's row lands in its own block-table slot.
-    bool canonical = write;
-    if (canonical && a.slot_mapping) {
-      const int64_t logical = (int64_t)a.past[b] + (t - a.cum[b]);
-      const int64_t page = logical / a.block_size;
-      canonical = page < a.max_blocks &&
-                  slot == (int64_t)a.block_table[(int64_t)b * a.max_blocks + page] * a.block_size +
-                              logical % a.block_size;
-    }
-    if (!canonical) a.route[b] = kRouteGeneric;
-  }
+  if (tid == 0) refine_route(a, t, b, slot, write);
   if (a.kv_only && !write) return;
 
   const bool process = a.do_norm || a.do_rotary;
-  const bool float_cache = a.cache_dtype == dt;
-
-  if (!process && float_cache) {
-    if (!write) return;
-    // Plain reshape-and-cache: the token's [KV*d] K and V rows are contiguous in the pool.
-    const int64_t row_elems = (int64_t)KV * d;
-    char* kdst = reinterpret_cast<char*>(a.key_cache) + slot * row_elems * 2;
-    char* vdst = reinterpret_cast<char*>(a.value_cache) + slot * row_elems * 2;
-    const char* ksrc = reinterpret_cast<const char*>(a.key) + (int64_t)t * a.key_stride * 2;
-    const char* vsrc = reinterpret_cast<const char*>(a.value) + (int64_t)t * a.value_stride * 2;
-    const int64_t bytes = row_elems * 2;
-    bool vec = ((reinterpret_cast<uintptr_t>(kdst) | reinterpret_cast<uintptr_t>(vdst) |
-                 reinterpret_cast<uintptr_t>(ksrc) | reinterpret_cast<uintptr_t>(vsrc) | bytes) & 15) == 0;
-    if (vec) {
-      for (int64_t j = tid; j < bytes / 16; j += nthreads) {
-        reinterpret_cast<uint4*>(kdst)[j] = reinterpret_cast<const uint4*>(ksrc)[j];
-        reinterpret_cast<uint4*>(vdst)[j] = reinterpret_cast<const uint4*>(vsrc)[j];
-      }
-    } else {
-      for (int64_t j = tid; j < bytes / 2; j += nthreads) {
-        reinterpret_cast<uint16_t*>(kdst)[j] = reinterpret_cast<const uint16_t*>(ksrc)[j];
-        reinterpret_cast<uint16_t*>(vdst)[j] = reinterpret_cast<const uint16_t*>(vsrc)[j];
-      }
-    }
-    return;
-  }
 
   // Staged rows: Q (processing path only) then K and V; sized by prologue_smem_bytes().
   const int nq_heads = process && !a.kv_only ? H : 0;
@@ -266,9 +304,11 @@ __global__ void kv_prologue_kernel(PrologueArgs a) {
 }
 
 void launch_meta_check(const PrologueArgs& a, cudaStream_t stream) {
-  int n = a.batch > a.num_tokens ? a.batch : a.num_tokens;
+  int64_t n = a.batch > a.num_tokens ? a.batch : a.num_tokens;
+  const int64_t entries = (int64_t)a.batch * (a.max_blocks > 0 ? a.max_blocks : 0);
+  if (entries > n) n = entries;
   if (n <= 0) return;
-  meta_check_kernel<<<(n + 255) / 256, 256, 0, stream>>>(a);
+  meta_check_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(a);
 }
 
 size_t prologue_smem_bytes(const PrologueArgs& a) {
@@ -284,6 +324,10 @@ cudaError_t launch_prologue(const PrologueArgs& a, cudaStream_t stream) {
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kv_prologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
+  }
+  if (!(a.do_norm || a.do_rotary) && a.cache_dtype == a.act_dtype) {
+    kv_copy_kernel<<<(a.num_tokens + kCopyTokensPerCta - 1) / kCopyTokensPerCta, 32 * kCopyTokensPerCta, 0, stream>>>(a);
+    return cudaGetLastError();
   }
   kv_prologue_kernel<<<a.num_tokens, 128, smem, stream>>>(a);
   return cudaGetLastError();
