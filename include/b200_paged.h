@@ -207,6 +207,80 @@ typedef struct B200NodeInfo {
 
 B200_API int b200_paged_attention_claim(const B200NodeInfo* node, char* reason, size_t reason_len);
 
+/* ---- com.microsoft.GroupQueryAttention over a contiguous BNSH cache -------------------- */
+
+/*
+ * One GroupQueryAttention node, replacing group_query_attention_op
+ * (rust/src/ops/attention.rs:932-1454) and its per-batch form gqa_batched (:586-848) for the
+ * forms b200_group_query_attention_claim accepts.  Per batch row b, with
+ * length = seqlens_k[b] + 1, query_past = max(length - seq, 0),
+ * past = new_seq ? query_past : length and new_rows = new_seq ? length - past : 0 (:662-667):
+ *   present[b, :, :past]       = past_kv[b, :, :past]
+ *   present[b, :, past:length] = the first new_rows rows of key/value[b]
+ *   present[b, :, length:]     = past_kv[b, :, length:cap] (if length < cap), then zeros
+ * and query row i of batch b (absolute position query_past + i) attends over keys
+ * [start, end) with end = min(query_past + i + 1, length) when causal (else length) and
+ * start = max(0, end - local_window_size) when local_window_size > 0 (:704-711).  present has
+ * present_cap = max(cap, total_sequence_length) rows; when present_key == past_key the call
+ * writes only the new rows, in place (shared-buffer contract, :1365-1375).
+ */
+typedef struct B200GqaParams {
+  int32_t num_heads, kv_num_heads, head_size;
+  float scale;               /* 0 = 1/sqrt(head_size)                                   */
+  int32_t is_causal;         /* op attribute `causal` (default 1)                        */
+  int32_t local_window_size; /* -1 (or 0) = none                                         */
+  float softcap;             /* 0 = none                                                 */
+  int32_t smooth_softmax;    /* 1 = a zero sink in every head's denominator              */
+  int32_t dtype;             /* activations and caches: FLOAT, FLOAT16 or BFLOAT16       */
+  int32_t batch, seq;        /* query [batch, seq, num_heads*head_size]                  */
+  int32_t new_seq;           /* key/value rows per batch: seq, or 0 (past only)          */
+  int32_t cap;               /* past axis-2 capacity (0 when past is absent)             */
+  int32_t present_cap;       /* present axis-2 length: max(cap, total_sequence_length)   */
+  int32_t total_sequence_length; /* host value of input 6                                */
+  int64_t query_row_stride, key_row_stride, value_row_stride; /* elements per token; 0 = dense
+                                                                 (packed QKV: (H+2KV)*D)  */
+  const void* query;
+  const void* key;             /* may be NULL when new_seq == 0                          */
+  const void* value;
+  const void* past_key;        /* [batch, KV, cap, D] or NULL                            */
+  const void* past_value;
+  void* present_key;           /* [batch, KV, present_cap, D]; may equal past_key        */
+  void* present_value;
+  const int32_t* seqlens_k;      /* device [batch]                                       */
+  const int32_t* host_seqlens_k; /* host [batch] (the reference reads it on the host)    */
+  const void* head_sink;         /* [num_heads] in dtype, or NULL                        */
+  void* output;                  /* [batch, seq, num_heads*head_size]                    */
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t num_sms;               /* 0 = query the device                                 */
+} B200GqaParams;
+
+B200_API int b200_gqa_params_size(void);
+/* Bytes of device workspace (shapes only). */
+B200_API int b200_group_query_attention_workspace_size(const B200GqaParams* p, size_t* bytes);
+/* Validate (reference messages, attention.rs:989-1030, :613-630, :663-667), then append and
+ * attend.  B200_ERR_FAIL for invalid lengths, B200_ERR_UNSUPPORTED for unclaimed forms. */
+B200_API int b200_group_query_attention(const B200GqaParams* p, void* stream);
+
+/* Claim predicate, restating group_query_attention_claim (attention.rs:2407-2754) over a
+ * plain node description, plus this build's own declines (rotary, attention_bias,
+ * qk_output, sliding_window_cache, integer caches, q/k norm, head size).  Returns 1 (claim)
+ * or 0 (decline, reason written to `reason`). */
+typedef struct B200GqaNodeInfo {
+  int32_t num_inputs;
+  int32_t num_outputs;
+  B200TensorInfo inputs[16];
+  B200TensorInfo outputs[4];
+  int64_t num_heads, kv_num_heads, causal, local_window_size, do_rotary, rotary_interleaved,
+      sliding_window_cache, smooth_softmax, qk_output, kv_cache_bit_width;
+  int32_t has_causal, has_local_window_size, has_smooth_softmax; /* 0 = operator default   */
+  float softcap;
+} B200GqaNodeInfo;
+
+B200_API int b200_group_query_attention_claim(const B200GqaNodeInfo* node, char* reason, size_t reason_len);
+/* sizeof(B200GqaNodeInfo), for binding layout checks. */
+B200_API int b200_gqa_node_info_size(void);
+
 /* ---- diagnostics (no counterpart in the reference) ------------------------------------ */
 
 /* Known-answer test of the tcgen05 tensor-core path: one CTA computes, for 128x128 fp16/bf16

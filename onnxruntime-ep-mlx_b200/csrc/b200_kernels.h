@@ -26,6 +26,8 @@ enum StatusBits : int {
 
 // Record `msg` as this thread's b200_last_error() and return `code` (capi.cu).
 int set_error(int code, const std::string& msg);
+// Add to the library's launch counter (b200_launch_count).
+void add_launches(uint64_t n);
 
 // KV append / Q-K preprocessing (kv_append.cu).
 struct PrologueArgs {

@@ -350,6 +350,7 @@ int run_prologue(const B200PagedAttentionParams* p, const Layout& L, cudaStream_
 
 namespace b200 {
 int set_error(int code, const std::string& msg) { return fail(code, msg); }
+void add_launches(uint64_t n) { count_launches(n); }
 
 int encode_tensor_map(CUtensorMap* map, bool bf16, int rank, const void* base, const uint64_t* dims,
                       const uint64_t* strides, const uint32_t* box) {

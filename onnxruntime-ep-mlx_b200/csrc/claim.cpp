@@ -1,4 +1,5 @@
-// Claim predicate for com.microsoft.PagedAttention over a plain node description.
+// Claim predicates for com.microsoft.PagedAttention and com.microsoft.GroupQueryAttention over
+// plain node descriptions.
 //
 // Restates paged_attention_claim (rust/src/ops/attention.rs:4384-4645) and the integer cache
 // claim it calls (rust/src/ops/kv_cache.rs:16-108), decline messages included, so an EP shell
@@ -10,7 +11,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <string>
+#include <vector>
 
 #include "b200_paged.h"
 
@@ -244,7 +247,145 @@ void paged_claim(const View& v) {
   REQUIRE(head <= 256, "head_size above 256 is not implemented by the B200 kernels");
 }
 
+// ---------------------------------------------------------------------------------------
+// GroupQueryAttention: group_query_attention_claim (attention.rs:2407-2754), then the forms
+// this build does not implement.
+struct GView {
+  const B200GqaNodeInfo* n;
+  bool in_present(int i) const { return i < n->num_inputs && n->inputs[i].present; }
+  bool out_present(int i) const { return i < n->num_outputs && n->outputs[i].present; }
+  const B200TensorInfo* in(int i) const { return in_present(i) ? &n->inputs[i] : nullptr; }
+  const B200TensorInfo* out(int i) const { return out_present(i) ? &n->outputs[i] : nullptr; }
+};
+
+bool same_shape(const B200TensorInfo* a, const B200TensorInfo* b) {
+  if (!a || !b || a->rank != b->rank) return false;
+  for (int i = 0; i < a->rank && i < B200_MAX_RANK; ++i)
+    if (a->shape[i] != b->shape[i]) return false;
+  return true;
+}
+
+void gqa_claim(const GView& v) {
+  const B200GqaNodeInfo& n = *v.n;
+  const int64_t causal = n.has_causal ? n.causal : 1;
+  const int64_t window = n.has_local_window_size ? n.local_window_size : -1;
+  const int64_t smooth = n.has_smooth_softmax ? n.smooth_softmax : -1;
+  REQUIRE(n.num_outputs >= 1 && n.num_outputs <= 4, "requires 1 to 4 outputs");
+  REQUIRE(v.out_present(1) == v.out_present(2), "present_key and present_value must both be provided or both omitted");
+  const bool sliding = n.sliding_window_cache != 0;
+  REQUIRE(causal == 0 || causal == 1, "causal must be 0 or 1");
+  REQUIRE(window == -1 || window > 0, "local_window_size must be -1 or positive");
+  REQUIRE(causal != 0 || window == -1, "bidirectional GroupQueryAttention requires local_window_size=-1");
+  REQUIRE(v.in_present(3) == v.in_present(4), "past_key and past_value must be provided together");
+  const B200TensorInfo* out0 = v.out(0);
+  if (!out0) deny("output lacks tensor type/shape info");
+  const int out_type = out0->dtype;
+  REQUIRE(out_type == B200_DTYPE_FLOAT || out_type == B200_DTYPE_FLOAT16 || out_type == B200_DTYPE_BFLOAT16,
+          "output must have an MLX float dtype, got %s", dtype_name(out_type));
+  const int ninputs = n.num_inputs;
+  REQUIRE(ninputs >= 7 && ninputs <= 16, "expects 7 required inputs plus optional rotary/bias/QK-norm inputs, got %d", ninputs);
+  const bool has_bias = v.in_present(10);
+  const bool do_rotary = n.do_rotary != 0;
+  REQUIRE(ninputs != 7 || !do_rotary, "7-input GroupQueryAttention requires do_rotary=0 because cos/sin caches are absent");
+  if (sliding) {
+    REQUIRE(window > 0, "sliding_window_cache=1 requires local_window_size > 0");
+    REQUIRE(v.out_present(1) && v.out_present(2), "sliding_window_cache requires present key/value outputs");
+  }
+  const bool packed = v.in_present(0) && !v.in_present(1) && !v.in_present(2);
+  REQUIRE(packed || (v.in_present(0) && v.in_present(1) && v.in_present(2)),
+          "Q/K/V must be either all separate or packed in input 0 with inputs 1 and 2 absent");
+  const bool quantized = v.in(3) && integer_cache(v.in(3)->dtype);
+  std::vector<int> float_idx = packed ? std::vector<int>{0} : std::vector<int>{0, 1, 2};
+  if (v.in_present(3) && !quantized) { float_idx.push_back(3); float_idx.push_back(4); }
+  if (do_rotary) { float_idx.push_back(7); float_idx.push_back(8); }
+  if (has_bias) float_idx.push_back(10);
+  if (v.in_present(14)) { float_idx.push_back(14); float_idx.push_back(15); }
+  for (int idx : float_idx) {
+    const B200TensorInfo* t = v.in(idx);
+    if (!t) deny("input %d lacks tensor type/shape info", idx);
+    REQUIRE(t->dtype == out_type, "input %d must have output dtype %s, got %s", idx, dtype_name(out_type), dtype_name(t->dtype));
+  }
+  for (int idx = 1; idx < std::min(n.num_outputs, 3); ++idx) {
+    if (!v.out_present(idx)) continue;
+    const int want = v.in(idx + 2) ? v.in(idx + 2)->dtype : out_type;
+    REQUIRE(v.out(idx)->dtype == want, "output %d must retain its cache dtype (activation dtype %s), got %s", idx,
+            dtype_name(out_type), dtype_name(v.out(idx)->dtype));
+  }
+  for (int idx : {5, 6}) {
+    const B200TensorInfo* t = v.in(idx);
+    if (!t) deny("input %d lacks tensor type/shape info", idx);
+    REQUIRE(t->dtype == B200_DTYPE_INT32, "input %d must have int32 dtype, got %s", idx, dtype_name(t->dtype));
+  }
+  const int64_t nh = n.num_heads, kvh = n.kv_num_heads;
+  REQUIRE(nh > 0 && kvh > 0 && nh % kvh == 0, "num_heads (%lld) must be a positive multiple of kv_num_heads (%lld)",
+          (long long)nh, (long long)kvh);
+  const B200TensorInfo* q = v.in(0);
+  REQUIRE(q->rank == 3 && q->shape[2] > 0, "query must have rank 3 and a positive static hidden size");
+  const int64_t total_heads = packed ? nh + 2 * kvh : nh;
+  REQUIRE(q->shape[2] % total_heads == 0, "query hidden size must match head count");
+  const int64_t head = q->shape[2] / total_heads;
+  if (!packed) {
+    for (int idx : {1, 2}) {
+      const B200TensorInfo* kv = v.in(idx);
+      REQUIRE(kv->rank == 3 && kv->shape[2] == kvh * head &&
+                  (kv->shape[0] < 0 || q->shape[0] < 0 || kv->shape[0] == q->shape[0]) &&
+                  (kv->shape[1] < 0 || q->shape[1] < 0 || kv->shape[1] == q->shape[1] ||
+                   (kv->shape[1] == 0 && v.in_present(3) && !sliding)),
+              "key/value must match query batch, sequence length and KV head geometry");
+    }
+    REQUIRE(same_shape(v.in(1), v.in(2)), "key/value shapes must match");
+  }
+  for (int idx : {3, 4}) {
+    const B200TensorInfo* c = v.in(idx);
+    if (!c) continue;
+    REQUIRE(c->rank == 4 && c->shape[1] == kvh && c->shape[3] == head &&
+                (c->shape[0] < 0 || q->shape[0] < 0 || c->shape[0] == q->shape[0]),
+            "past cache must be [batch,kv_num_heads,capacity,stored_head_size]");
+  }
+  if (v.in_present(3)) REQUIRE(same_shape(v.in(3), v.in(4)), "past key/value cache shapes must match");
+  const B200TensorInfo* lens = v.in(5);
+  REQUIRE(lens && lens->rank == 1 && (lens->shape[0] < 0 || q->shape[0] < 0 || lens->shape[0] == q->shape[0]),
+          "seqlens_k must be [batch]");
+  const B200TensorInfo* tot = v.in(6);
+  REQUIRE(tot && (tot->rank == 0 || (tot->rank == 1 && tot->shape[0] == 1)), "total_sequence_length must be scalar or [1]");
+  if (v.in_present(11)) {
+    const B200TensorInfo* s = v.in(11);
+    REQUIRE(s->dtype == out_type && s->rank == 1 && s->shape[0] == nh, "head_sink must be [num_heads] in activation dtype");
+  }
+  REQUIRE(v.in_present(14) == v.in_present(15), "q_norm_weight and k_norm_weight must be provided together");
+  REQUIRE(smooth >= -1 && smooth <= 1, "smooth_softmax must be -1 (schema default), 0 or 1");
+  REQUIRE(n.qk_output >= 0 && n.qk_output <= 2 && (n.qk_output != 0) == v.out_present(3),
+          "qk_output must be 0, 1 or 2 and enabled exactly when output_qk is present");
+  REQUIRE(std::isfinite(n.softcap) && n.softcap >= 0.f, "softcap must be finite and non-negative");
+  // Forms the reference accepts that this build does not implement (the node stays on ORT).
+  REQUIRE(!sliding, "sliding_window_cache is not implemented on B200");
+  REQUIRE(!do_rotary, "rotary embedding inside GroupQueryAttention is not implemented on B200 (apply RoPE before the node)");
+  REQUIRE(!has_bias, "attention_bias is not implemented on B200");
+  REQUIRE(n.qk_output == 0, "qk_output diagnostics are not implemented on B200");
+  REQUIRE(!quantized && n.kv_cache_bit_width == 0, "integer GroupQueryAttention caches are not implemented on B200");
+  REQUIRE(!v.in_present(14), "q/k RMS norm inside GroupQueryAttention is not implemented on B200");
+  REQUIRE(head % 8 == 0 && head <= 256, "head_size must be a multiple of 8 up to 256 on B200, got %lld", (long long)head);
+}
+
 }  // namespace
+
+extern "C" int b200_gqa_node_info_size(void) { return (int)sizeof(B200GqaNodeInfo); }
+
+extern "C" int b200_group_query_attention_claim(const B200GqaNodeInfo* node, char* reason, size_t reason_len) {
+  std::string why;
+  try {
+    if (!node) deny("null node");
+    gqa_claim(GView{node});
+    if (reason && reason_len) reason[0] = 0;
+    return 1;
+  } catch (const Decline& d) {
+    why = d.reason;
+  } catch (...) {
+    why = "claim predicate failed";
+  }
+  if (reason && reason_len) std::snprintf(reason, reason_len, "%s", why.c_str());
+  return 0;
+}
 
 extern "C" int b200_paged_attention_claim(const B200NodeInfo* node, char* reason, size_t reason_len) {
   std::string why;

@@ -80,6 +80,36 @@ class NodeInfo(ctypes.Structure):
     ]
 
 
+class GqaParams(ctypes.Structure):
+    """Mirror of ``B200GqaParams`` (GroupQueryAttention over a contiguous BNSH cache)."""
+
+    _fields_ = [
+        ("num_heads", _i32), ("kv_num_heads", _i32), ("head_size", _i32), ("scale", _f32),
+        ("is_causal", _i32), ("local_window_size", _i32), ("softcap", _f32), ("smooth_softmax", _i32),
+        ("dtype", _i32), ("batch", _i32), ("seq", _i32), ("new_seq", _i32), ("cap", _i32),
+        ("present_cap", _i32), ("total_sequence_length", _i32),
+        ("query_row_stride", _i64), ("key_row_stride", _i64), ("value_row_stride", _i64),
+        ("query", _vp), ("key", _vp), ("value", _vp), ("past_key", _vp), ("past_value", _vp),
+        ("present_key", _vp), ("present_value", _vp), ("seqlens_k", _vp), ("host_seqlens_k", _vp),
+        ("head_sink", _vp), ("output", _vp), ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+        ("num_sms", _i32),
+    ]
+
+
+class GqaNodeInfo(ctypes.Structure):
+    """Mirror of ``B200GqaNodeInfo`` (GroupQueryAttention claim predicate input)."""
+
+    _fields_ = [
+        ("num_inputs", _i32), ("num_outputs", _i32),
+        ("inputs", TensorInfo * 16), ("outputs", TensorInfo * 4),
+        ("num_heads", _i64), ("kv_num_heads", _i64), ("causal", _i64), ("local_window_size", _i64),
+        ("do_rotary", _i64), ("rotary_interleaved", _i64), ("sliding_window_cache", _i64),
+        ("smooth_softmax", _i64), ("qk_output", _i64), ("kv_cache_bit_width", _i64),
+        ("has_causal", _i32), ("has_local_window_size", _i32), ("has_smooth_softmax", _i32),
+        ("softcap", _f32),
+    ]
+
+
 # Every entry point the header declares, with its ctypes signature.
 SIGNATURES = {
     "b200_version": (ctypes.c_int, []),
@@ -97,6 +127,13 @@ SIGNATURES = {
     "b200_selftest_tcgen05": (ctypes.c_int, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_paged_attention_claim": (
         ctypes.c_int, [ctypes.POINTER(NodeInfo), ctypes.c_char_p, ctypes.c_size_t]),
+    "b200_gqa_params_size": (ctypes.c_int, []),
+    "b200_gqa_node_info_size": (ctypes.c_int, []),
+    "b200_group_query_attention_workspace_size": (
+        ctypes.c_int, [ctypes.POINTER(GqaParams), ctypes.POINTER(ctypes.c_size_t)]),
+    "b200_group_query_attention": (ctypes.c_int, [ctypes.POINTER(GqaParams), _vp]),
+    "b200_group_query_attention_claim": (
+        ctypes.c_int, [ctypes.POINTER(GqaNodeInfo), ctypes.c_char_p, ctypes.c_size_t]),
 }
 
 
@@ -127,6 +164,10 @@ def load() -> ctypes.CDLL:
         raise ImportError("libb200_paged.so: B200PagedAttentionParams layout differs from the binding")
     if lib.b200_node_info_size() != ctypes.sizeof(NodeInfo):
         raise ImportError("libb200_paged.so: B200NodeInfo layout differs from the binding")
+    if lib.b200_gqa_params_size() != ctypes.sizeof(GqaParams):
+        raise ImportError("libb200_paged.so: B200GqaParams layout differs from the binding")
+    if lib.b200_gqa_node_info_size() != ctypes.sizeof(GqaNodeInfo):
+        raise ImportError("libb200_paged.so: B200GqaNodeInfo layout differs from the binding")
     return lib
 
 

@@ -1,0 +1,115 @@
+"""com.microsoft.GroupQueryAttention on B200 over a contiguous BNSH cache.
+
+Mirror of the node's inputs, attributes and outputs (reference op
+rust/src/ops/attention.rs:932-1454, per-batch form :586-848, claim :2407-2754):
+
+    output, present_key, present_value = group_query_attention(
+        query, key, value, past_key, past_value, seqlens_k, total_sequence_length,
+        head_sink=None, num_heads=..., kv_num_heads=..., ...)
+
+``present`` follows the reference's contracts: by default a new ``[B, KV, max(cap, total), D]``
+buffer (growing: past rows, then the new rows); passing ``present_key=past_key,
+present_value=past_value`` writes the new rows in place (shared buffer).  Errors raise
+``B200Error`` with the reference's messages.  There is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from ._capi import (DTYPE_BFLOAT16, DTYPE_FLOAT, DTYPE_FLOAT16, LIB, GqaParams, check)
+
+_DTYPES = {torch.float32: DTYPE_FLOAT, torch.float16: DTYPE_FLOAT16, torch.bfloat16: DTYPE_BFLOAT16}
+_workspaces: dict = {}
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _workspace(device, nbytes):
+    buf = _workspaces.get(device)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[device] = buf
+    return buf
+
+
+def build_params(query, key, value, past_key, past_value, seqlens_k, total_sequence_length,
+                 head_sink=None, *, num_heads, kv_num_heads, scale=0.0, causal=1,
+                 local_window_size=-1, softcap=0.0, smooth_softmax=-1, present_key=None,
+                 present_value=None, with_present=True, host_seqlens_k=None, output=None):
+    """Fill a ``B200GqaParams``.  Returns ``(params, keepalive, output, present_key, present_value)``."""
+    H, KV = int(num_heads), int(kv_num_heads)
+    packed = key is None and value is None  # packed QKV in query (inputs 1 and 2 absent)
+    B, S = int(query.shape[0]), int(query.shape[1])
+    if packed:
+        D = query.shape[2] // (H + 2 * KV)
+        new_seq = S
+    else:
+        D = query.shape[2] // H
+        new_seq = int(key.shape[1]) if key is not None else 0
+    if isinstance(total_sequence_length, torch.Tensor):
+        total = int(total_sequence_length.reshape(-1)[0].item())
+    else:
+        total = int(np.asarray(total_sequence_length).reshape(-1)[0])
+    cap = int(past_key.shape[2]) if past_key is not None else 0
+    if host_seqlens_k is None:
+        host_seqlens_k = seqlens_k.detach().to("cpu", torch.int32).numpy()
+    host_seqlens_k = np.ascontiguousarray(np.asarray(host_seqlens_k, dtype=np.int32))
+    dev = query.device
+    pcap = max(cap, total)
+    if with_present and present_key is None:
+        present_key = torch.empty((B, KV, pcap, D), dtype=query.dtype, device=dev)
+        present_value = torch.empty_like(present_key)
+    if present_key is not None:
+        pcap = int(present_key.shape[2])
+    if output is None:
+        output = torch.empty((B, S, H * D), dtype=query.dtype, device=dev)
+    p = GqaParams()
+    p.num_heads, p.kv_num_heads, p.head_size = H, KV, D
+    p.scale = float(scale)
+    p.is_causal = int(causal)
+    p.local_window_size = int(local_window_size)
+    p.softcap = float(softcap)
+    p.smooth_softmax = int(smooth_softmax)
+    p.dtype = _DTYPES[query.dtype]
+    p.batch, p.seq, p.new_seq, p.cap = B, S, new_seq, cap
+    p.present_cap = pcap if present_key is not None else 0
+    p.total_sequence_length = total
+    p.query = _ptr(query)
+    if packed:
+        row = (H + 2 * KV) * D
+        p.query_row_stride = p.key_row_stride = p.value_row_stride = row
+        esz = query.element_size()
+        p.key = ctypes.c_void_p(query.data_ptr() + H * D * esz)
+        p.value = ctypes.c_void_p(query.data_ptr() + (H + KV) * D * esz)
+    else:
+        p.key, p.value = _ptr(key), _ptr(value)
+    p.past_key, p.past_value = _ptr(past_key), _ptr(past_value)
+    p.present_key, p.present_value = _ptr(present_key), _ptr(present_value)
+    p.seqlens_k = _ptr(seqlens_k)
+    p.host_seqlens_k = host_seqlens_k.ctypes.data_as(ctypes.c_void_p)
+    p.head_sink = _ptr(head_sink)
+    p.output = _ptr(output)
+    nbytes = ctypes.c_size_t(0)
+    check(LIB.b200_group_query_attention_workspace_size(ctypes.byref(p), ctypes.byref(nbytes)))
+    ws = _workspace(dev, nbytes.value)
+    p.workspace = _ptr(ws)
+    p.workspace_bytes = ws.numel()
+    keep = (query, key, value, past_key, past_value, seqlens_k, head_sink, host_seqlens_k, ws)
+    return p, keep, output, present_key, present_value
+
+
+def group_query_attention(query, key, value, past_key, past_value, seqlens_k, total_sequence_length,
+                          head_sink=None, *, stream=None, **kwargs):
+    """One GroupQueryAttention node.  Returns ``(output, present_key, present_value)``."""
+    p, keep, out, pk, pv = build_params(query, key, value, past_key, past_value, seqlens_k,
+                                        total_sequence_length, head_sink, **kwargs)
+    s = stream if stream is not None else torch.cuda.current_stream(query.device)
+    check(LIB.b200_group_query_attention(ctypes.byref(p), ctypes.c_void_p(s.cuda_stream)))
+    del keep
+    return out, pk, pv

@@ -1,0 +1,84 @@
+"""CPU restatement of the reference GroupQueryAttention op over a contiguous BNSH cache (numpy).
+
+TEST INFRASTRUCTURE ONLY.  Imported by ``tests/`` and the ``cpu_baseline`` / ``--impl
+reference`` legs of ``bench.py``; the product path (``onnxruntime_ep_b200``) never imports it.
+
+Semantics:
+* per batch row (rust/src/ops/attention.rs:662-667): ``length = seqlens_k[b] + 1``,
+  ``query_past = max(length - S, 0)``, ``past = length if new_seq == 0 else query_past``,
+  ``new_rows = length - past`` (0 when new_seq == 0);
+* the cache the queries read is past rows ``[0, past)`` then the first ``new_rows`` new rows
+  (attention.rs:688-711); ``present`` has ``max(cap, total)`` rows: those ``length`` rows, then
+  the old buffer's rows ``[length, cap)``, then zeros (attention.rs:782-809);
+* masks, softcap and sink exactly as the reference's own NumPy oracle
+  ``_reference`` (tests/ops/test_gqa_position_cache.py:88-134): query row i sees keys
+  ``[start, end)`` with ``end = min(past + i + 1, length)`` (causal) or ``length``, and
+  ``start = max(0, end - window)`` for ``window > 0``; scores in fp32; softcap
+  ``cap * tanh(s / cap)``; a sink joins only the softmax denominator;
+* ``smooth_softmax == 1`` is a zero sink in every head (attention.rs:1311-1312).
+
+Parity pinning: ``tests/golden/make_gqa_golden.py`` runs the reference's ``_reference`` on
+seeded inputs and commits its outputs (``gqa_golden.npz``); ``tests/test_gqa_oracle.py``
+checks this module against them.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_heads, kv_num_heads,
+                          scale=None, causal=True, window=-1, softcap=0.0, sink=None,
+                          smooth_softmax=-1):
+    """Returns ``(output [B,S,H*D], present_k, present_v [B,KV,max(cap,total),D])``.
+
+    ``q`` [B,S,H*D]; ``k``/``v`` [B,new_seq,KV*D] (new_seq may be 0); ``past_k``/``past_v``
+    [B,KV,cap,D] or None.  Arrays keep their dtype; math is fp32, the output is rounded to
+    the activation dtype."""
+    B, S, hidden = q.shape
+    H, KV = int(num_heads), int(kv_num_heads)
+    D = hidden // H
+    g = H // KV
+    new_seq = 0 if k is None else k.shape[1]
+    total = int(np.asarray(total).reshape(-1)[0])
+    cap = 0 if past_k is None else past_k.shape[2]
+    pcap = max(cap, total)
+    dt = q.dtype
+    scale = 1.0 / np.sqrt(D) if not scale else float(scale)
+    pk = np.zeros((B, KV, pcap, D), dt)
+    pv = np.zeros((B, KV, pcap, D), dt)
+    out = np.empty((B, S, H * D), dt)
+    if sink is None and smooth_softmax == 1:
+        sink = np.zeros(H, np.float32)
+    for b in range(B):
+        length = int(seqlens_k[b]) + 1
+        query_past = max(length - S, 0)
+        past = length if new_seq == 0 else query_past
+        rows = 0 if new_seq == 0 else length - past
+        if past_k is not None:
+            pk[b, :, :past] = past_k[b, :, :past]
+            pv[b, :, :past] = past_v[b, :, :past]
+            if length < cap:
+                pk[b, :, length:cap] = past_k[b, :, length:cap]
+                pv[b, :, length:cap] = past_v[b, :, length:cap]
+        if rows:
+            pk[b, :, past:length] = k[b, :rows].reshape(rows, KV, D).transpose(1, 0, 2)
+            pv[b, :, past:length] = v[b, :rows].reshape(rows, KV, D).transpose(1, 0, 2)
+        keys = np.repeat(pk[b, :, :length].astype(np.float32), g, 0)   # [H, length, D]
+        vals = np.repeat(pv[b, :, :length].astype(np.float32), g, 0)
+        qh = q[b].reshape(S, H, D).transpose(1, 0, 2).astype(np.float32)  # [H, S, D]
+        scores = qh @ keys.transpose(0, 2, 1) * np.float32(scale)
+        if softcap > 0:
+            scores = softcap * np.tanh(scores / softcap)
+        end = np.minimum(query_past + np.arange(S) + 1, length) if causal else np.full(S, length)
+        start = np.maximum(0, end - window) if window > 0 else np.zeros(S, int)
+        cols = np.arange(length)[None]
+        visible = (cols >= start[:, None]) & (cols < end[:, None])
+        logits = np.where(visible[None], scores, -np.inf)
+        if sink is not None:
+            s = np.asarray(sink, np.float32).reshape(H, 1, 1)
+            logits = np.concatenate([logits, np.broadcast_to(s, (H, S, 1))], -1)
+        e = np.exp(logits - logits.max(-1, keepdims=True))
+        probs = (e / e.sum(-1, keepdims=True))[..., :length]
+        out[b] = (probs @ vals).transpose(1, 0, 2).reshape(S, H * D).astype(dt)
+    return out, pk, pv

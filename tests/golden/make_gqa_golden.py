@@ -1,0 +1,94 @@
+"""Generate ``gqa_golden.npz`` from the reference's own NumPy GroupQueryAttention oracle.
+
+Usage (build container only; the reference checkout does not travel to GPU boxes)::
+
+    python tests/golden/make_gqa_golden.py --reference <path to the reference checkout>
+
+``_reference`` (tests/ops/test_gqa_position_cache.py:88-134, pinned there to ORT v1.31.0) is
+taken from the test file with ``ast`` and executed in a private namespace holding ``numpy``;
+the test module itself imports onnx helpers that are absent here.  Its geometry is fixed at
+4 q heads, 2 kv heads, head size 32, scale 1/sqrt(32); composed cases use softcap 0.7 and the
+feed ``sink``.  Inputs are seeded numpy (``default_rng(365 + case index)``) and stored with
+the outputs, so the fixtures are self-contained.  The oracle writes new rows into a copy of
+the past buffer, so every case has ``cap >= total`` (the growing contract, ``total > cap``,
+is covered by the GPU tests against ``oracle/gqa_ref.py``).
+"""
+
+from __future__ import annotations
+
+import argparse
+import ast
+import json
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+# name, dtype, batch, seq, new_seq, cap, lengths (seqlens_k + 1), total, causal, window, composed
+CASES = [
+    ("prefill_shared", "float32", 1, 2, 2, 6, [4], 4, True, -1, False),
+    ("decode_shared", "float32", 1, 1, 1, 6, [6], 6, True, -1, False),
+    ("bidirectional", "float32", 1, 3, 3, 8, [7], 7, False, -1, False),
+    ("window", "float32", 1, 4, 4, 9, [9], 9, True, 3, False),
+    ("composed", "float32", 1, 2, 2, 6, [5], 5, True, -1, True),
+    ("ragged_batch", "float32", 2, 2, 2, 6, [3, 6], 6, True, -1, False),
+    ("padded_prefill", "float32", 2, 5, 5, 7, [3, 5], 5, True, -1, False),
+    ("past_only", "float32", 2, 1, 0, 6, [4, 6], 6, True, -1, False),
+    ("decode_fp16", "float16", 1, 1, 1, 8, [8], 8, True, -1, False),
+    ("composed_fp16", "float16", 2, 3, 3, 8, [5, 8], 8, True, 4, True),
+]
+HEADS, KV, HEAD = 4, 2, 32
+
+
+def load_reference(path):
+    with open(path) as f:
+        tree = ast.parse(f.read(), filename=path)
+    wanted = [n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name in ("_rotate", "_reference")]
+    if len(wanted) != 2:
+        raise SystemExit(f"{path}: _rotate/_reference not found")
+    ns = {"np": np, "__builtins__": __builtins__}
+    exec(compile(ast.Module(body=wanted, type_ignores=[]), path, "exec"), ns)
+    return ns["_reference"]
+
+
+def make_feeds(index, dtype, batch, seq, new_seq, cap, lengths, total, composed):
+    rng = np.random.default_rng(365 + index)
+    dt = np.dtype(dtype)
+    feeds = dict(
+        q=rng.normal(size=(batch, seq, HEADS * HEAD)).astype(dt),
+        k=rng.normal(size=(batch, new_seq, KV * HEAD)).astype(dt),
+        v=rng.normal(size=(batch, new_seq, KV * HEAD)).astype(dt),
+        pk=rng.normal(size=(batch, KV, cap, HEAD)).astype(dt),
+        pv=rng.normal(size=(batch, KV, cap, HEAD)).astype(dt),
+        lengths=np.asarray(lengths, np.int32) - 1,
+        total=np.array([total], np.int32),
+    )
+    if composed:
+        feeds["sink"] = np.array([-1, 0, 1, 2], dt)
+    return feeds
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="path of the reference checkout")
+    args = ap.parse_args()
+    ref = load_reference(os.path.join(args.reference, "tests", "ops", "test_gqa_position_cache.py"))
+    arrays, meta = {}, []
+    for i, (name, dtype, batch, seq, new_seq, cap, lengths, total, causal, window, composed) in enumerate(CASES):
+        feeds = make_feeds(i, dtype, batch, seq, new_seq, cap, lengths, total, composed)
+        out, pk, pv = ref(feeds, causal=causal, window=window, composed=composed)
+        for key, val in feeds.items():
+            arrays[f"{name}/in/{key}"] = val
+        arrays[f"{name}/out/output"] = out
+        arrays[f"{name}/out/present_k"] = pk
+        arrays[f"{name}/out/present_v"] = pv
+        meta.append(dict(name=name, dtype=dtype, batch=batch, seq=seq, new_seq=new_seq, cap=cap,
+                         total=total, causal=causal, window=window, composed=composed))
+    arrays["meta"] = np.frombuffer(json.dumps(meta).encode(), np.uint8)
+    np.savez_compressed(os.path.join(HERE, "gqa_golden.npz"), **arrays)
+    print(f"wrote {len(meta)} cases to gqa_golden.npz")
+
+
+if __name__ == "__main__":
+    main()

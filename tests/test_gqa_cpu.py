@@ -1,0 +1,170 @@
+"""GroupQueryAttention on CPU: the claim predicate (b200_group_query_attention_claim, restating
+group_query_attention_claim, rust/src/ops/attention.rs:2407-2754) and the host-side length
+validation of b200_group_query_attention (reference messages, attention.rs:989-1030,
+:613-630, :663-673).  Validation runs before any device work, so no GPU is needed."""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from onnxruntime_ep_b200 import _capi
+
+F16, BF16, F32, I32, I8 = (_capi.DTYPE_FLOAT16, _capi.DTYPE_BFLOAT16, _capi.DTYPE_FLOAT, _capi.DTYPE_INT32,
+                           _capi.DTYPE_INT8)
+
+
+def tensor(info, dtype, shape):
+    info.present = 1
+    info.dtype = dtype
+    info.rank = len(shape)
+    for i, d in enumerate(shape):
+        info.shape[i] = d
+
+
+def gnode(H=32, KV=8, D=128, dt=F32, B=1, S=1, cap=2048, n_inputs=7, n_outputs=3, past=True):
+    """BASELINE config 1 node: q [1,1,4096], k/v [1,1,1024], past [1,8,2048,128], fp32."""
+    n = _capi.GqaNodeInfo()
+    n.num_inputs, n.num_outputs = n_inputs, n_outputs
+    n.num_heads, n.kv_num_heads = H, KV
+    tensor(n.inputs[0], dt, [B, S, H * D])
+    tensor(n.inputs[1], dt, [B, S, KV * D])
+    tensor(n.inputs[2], dt, [B, S, KV * D])
+    if past:
+        tensor(n.inputs[3], dt, [B, KV, cap, D])
+        tensor(n.inputs[4], dt, [B, KV, cap, D])
+    tensor(n.inputs[5], I32, [B])
+    tensor(n.inputs[6], I32, [1])
+    tensor(n.outputs[0], dt, [B, S, H * D])
+    if n_outputs >= 3:
+        tensor(n.outputs[1], dt, [B, KV, -1, D])
+        tensor(n.outputs[2], dt, [B, KV, -1, D])
+    return n
+
+
+def claim(n):
+    buf = ctypes.create_string_buffer(512)
+    ok = _capi.LIB.b200_group_query_attention_claim(ctypes.byref(n), buf, 512)
+    return ok, buf.value.decode()
+
+
+def test_layouts_match_library():
+    assert _capi.LIB.b200_gqa_params_size() == ctypes.sizeof(_capi.GqaParams)
+    assert _capi.LIB.b200_gqa_node_info_size() == ctypes.sizeof(_capi.GqaNodeInfo)
+
+
+@pytest.mark.parametrize("dt", [F32, F16, BF16])
+def test_claims_config1_node(dt):
+    assert claim(gnode(dt=dt)) == (1, "")
+
+
+def test_claims_packed_qkv_and_no_past():
+    n = gnode(past=False)
+    n.inputs[1].present = n.inputs[2].present = 0
+    tensor(n.inputs[0], F32, [1, 1, (32 + 16) * 128])
+    assert claim(n) == (1, "")
+
+
+def _set(attr, value):
+    def f(n):
+        setattr(n, attr, value)
+        if attr == "causal":
+            n.has_causal = 1
+        if attr == "local_window_size":
+            n.has_local_window_size = 1
+        if attr == "smooth_softmax":
+            n.has_smooth_softmax = 1
+    return f
+
+
+@pytest.mark.parametrize("mutate,reason", [
+    (_set("causal", 2), "causal must be 0 or 1"),
+    (_set("local_window_size", 0), "local_window_size must be -1 or positive"),
+    (lambda n: (_set("causal", 0)(n), _set("local_window_size", 4)(n)),
+     "bidirectional GroupQueryAttention requires local_window_size=-1"),
+    (lambda n: setattr(n.inputs[4], "present", 0), "past_key and past_value must be provided together"),
+    (lambda n: tensor(n.outputs[0], I32, [1, 1, 4096]), "output must have an MLX float dtype, got int32"),
+    (lambda n: setattr(n, "do_rotary", 1), "7-input GroupQueryAttention requires do_rotary=0"),
+    (lambda n: tensor(n.inputs[1], F16, [1, 1, 1024]), "input 1 must have output dtype float32, got float16"),
+    (lambda n: tensor(n.inputs[5], F32, [1]), "input 5 must have int32 dtype, got float32"),
+    (lambda n: setattr(n, "kv_num_heads", 5), "num_heads (32) must be a positive multiple of kv_num_heads (5)"),
+    (lambda n: tensor(n.inputs[1], F32, [1, 1, 512]), "key/value must match query batch"),
+    (lambda n: tensor(n.inputs[3], F32, [1, 4, 2048, 128]), "past cache must be [batch,kv_num_heads"),
+    (lambda n: tensor(n.inputs[6], I32, [2]), "total_sequence_length must be scalar or [1]"),
+    (_set("smooth_softmax", 3), "smooth_softmax must be -1"),
+    (lambda n: setattr(n, "qk_output", 1), "qk_output must be 0, 1 or 2 and enabled exactly when output_qk is present"),
+    (lambda n: setattr(n, "softcap", float("inf")), "softcap must be finite and non-negative"),
+])
+def test_reference_declines(mutate, reason):
+    n = gnode()
+    mutate(n)
+    ok, why = claim(n)
+    assert ok == 0 and why.startswith(reason), why
+
+
+@pytest.mark.parametrize("mutate,reason", [
+    (lambda n: (setattr(n, "num_inputs", 9), setattr(n, "do_rotary", 1),
+                tensor(n.inputs[7], F32, [4096, 64]), tensor(n.inputs[8], F32, [4096, 64])),
+     "rotary embedding inside GroupQueryAttention is not implemented on B200"),
+    (lambda n: (setattr(n, "num_inputs", 11), tensor(n.inputs[10], F32, [1, 1, 1, 2049])),
+     "attention_bias is not implemented on B200"),
+    (lambda n: (tensor(n.inputs[3], I8, [1, 8, 2048, 128]), tensor(n.inputs[4], I8, [1, 8, 2048, 128]),
+                tensor(n.outputs[1], I8, [1, 8, -1, 128]), tensor(n.outputs[2], I8, [1, 8, -1, 128])),
+     "integer GroupQueryAttention caches are not implemented on B200"),
+    (lambda n: (setattr(n, "sliding_window_cache", 1), _set("local_window_size", 64)(n)),
+     "sliding_window_cache is not implemented on B200"),
+])
+def test_b200_declines(mutate, reason):
+    n = gnode()
+    mutate(n)
+    ok, why = claim(n)
+    assert ok == 0 and why.startswith(reason), why
+
+
+def params(lengths, total, S=1, new_seq=1, cap=2048, B=None, causal=1, window=-1, present_cap=None):
+    B = len(lengths) if B is None else B
+    p = _capi.GqaParams()
+    p.num_heads, p.kv_num_heads, p.head_size = 32, 8, 128
+    p.is_causal, p.local_window_size, p.smooth_softmax = causal, window, -1
+    p.dtype = F32
+    p.batch, p.seq, p.new_seq, p.cap = B, S, new_seq, cap
+    p.total_sequence_length = total
+    p.present_cap = max(cap, total) if present_cap is None else present_cap
+    fake = ctypes.c_void_p(0x1000)  # never dereferenced: validation fails first
+    for f in ("query", "key", "value", "past_key", "past_value", "seqlens_k", "output", "workspace"):
+        setattr(p, f, fake)
+    p.present_key, p.present_value = ctypes.c_void_p(0x2000), ctypes.c_void_p(0x3000)
+    host = np.asarray(lengths, np.int32)
+    p.host_seqlens_k = host.ctypes.data_as(ctypes.c_void_p)
+    p.workspace_bytes = 1 << 30
+    return p, host
+
+
+@pytest.mark.parametrize("lengths,total,S,new_seq,cap,message", [
+    ([2047], 2049, 1, 1, 2048, "GroupQueryAttention: inconsistent sequence lengths or cache capacity"),
+    ([2048], 2050, 1, 1, 2048, "GroupQueryAttention: inconsistent sequence lengths or cache capacity"),
+    ([3, 9], 9, 1, 1, 16, "GroupQueryAttention: invalid per-batch or maximum sequence lengths"),
+    ([3, 7], 9, 1, 1, 16, "GroupQueryAttention: invalid per-batch or maximum sequence lengths"),
+    ([0, 8], 9, 4, 4, 16, "GroupQueryAttention: invalid per-batch or maximum sequence lengths"),
+    ([20, 8], 21, 1, 0, 16, "GroupQueryAttention: sequence length exceeds available past cache"),
+    ([2048], -1, 1, 1, 2048, "GroupQueryAttention: total_sequence_length is outside int32 range"),
+])
+def test_length_validation_messages(lengths, total, S, new_seq, cap, message):
+    p, keep = params(lengths, total, S=S, new_seq=new_seq, cap=cap)
+    rc = _capi.LIB.b200_group_query_attention(ctypes.byref(p), None)
+    assert rc == _capi.B200_ERR_FAIL
+    assert _capi.LIB.b200_last_error().decode() == message
+
+
+def test_new_rows_must_match_query_sequence():
+    p, keep = params([2048], 2049, S=2, new_seq=1)
+    assert _capi.LIB.b200_group_query_attention(ctypes.byref(p), None) == _capi.B200_ERR_FAIL
+    assert _capi.LIB.b200_last_error().decode() == (
+        "GroupQueryAttention: K/V must match Q sequence or be empty with paired non-sliding past")
+
+
+def test_workspace_size_is_shape_only():
+    p, keep = params([2048], 2049)
+    n = ctypes.c_size_t(0)
+    assert _capi.LIB.b200_group_query_attention_workspace_size(ctypes.byref(p), ctypes.byref(n)) == 0
+    assert n.value >= 256

@@ -1,0 +1,168 @@
+"""GPU parity of b200_group_query_attention against the reference's own oracle (golden cases)
+and against oracle/gqa_ref.py (BASELINE config 1 at full size and a sweep of forms)."""
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import gqa_ref
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from onnxruntime_ep_b200 import gqa  # noqa: E402
+
+DEV = torch.device("cuda", 0)
+GOLDEN = np.load(os.path.join(os.path.dirname(__file__), "golden", "gqa_golden.npz"))
+META = json.loads(bytes(GOLDEN["meta"]).decode())
+TORCH_DT = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
+
+
+def dev(a, dtype=None):
+    if a is None:
+        return None
+    t = torch.from_numpy(np.ascontiguousarray(a).view(np.uint16) if a.dtype.name == "bfloat16" else np.ascontiguousarray(a))
+    if a.dtype.name == "bfloat16":
+        t = t.view(torch.bfloat16)
+    return t.to(DEV)
+
+
+def host(t):
+    if t.dtype == torch.bfloat16:
+        return t.float().cpu().numpy()
+    return t.cpu().numpy()
+
+
+def check(out, want, dtype):
+    out = np.asarray(out, np.float32)
+    want = np.asarray(want, np.float32)
+    if dtype == "float32":
+        bound = 2e-5 + 2e-5 * np.abs(want)
+    else:
+        ulp = 2.0 ** -8 if dtype == "bfloat16" else 2.0 ** -11
+        bound = 2e-3 + ulp * np.abs(want)  # fp32 recomputation tolerance + the output's rounding
+    err = np.abs(out - want)
+    assert np.all(err <= bound), f"max err {err.max()} (worst excess {(err - bound).max()})"
+
+
+@pytest.mark.parametrize("in_place", [False, True])
+@pytest.mark.parametrize("case", META, ids=[c["name"] for c in META])
+def test_golden_cases(case, in_place):
+    name = case["name"]
+    f = {k.split("/")[-1]: GOLDEN[k] for k in GOLDEN.files if k.startswith(f"{name}/in/")}
+    q, pk, pv = dev(f["q"]), dev(f["pk"]), dev(f["pv"])
+    k = dev(f["k"]) if case["new_seq"] else None
+    v = dev(f["v"]) if case["new_seq"] else None
+    if not case["new_seq"]:
+        k = torch.empty((case["batch"], 0, 2 * 32), dtype=q.dtype, device=DEV)
+        v = torch.empty_like(k)
+    lengths = dev(f["lengths"])
+    kw = dict(num_heads=4, kv_num_heads=2, causal=int(case["causal"]), local_window_size=case["window"],
+              softcap=0.7 if case["composed"] else 0.0)
+    sink = dev(f["sink"]) if "sink" in f else None
+    if in_place:
+        kw.update(present_key=pk, present_value=pv)
+    out, ok, ov = gqa.group_query_attention(q, k, v, pk, pv, lengths, int(f["total"][0]), sink, **kw)
+    torch.cuda.synchronize()
+    check(host(out), GOLDEN[f"{name}/out/output"], case["dtype"])
+    np.testing.assert_array_equal(host(ok), GOLDEN[f"{name}/out/present_k"])
+    np.testing.assert_array_equal(host(ov), GOLDEN[f"{name}/out/present_v"])
+
+
+def run_case(rng, *, dtype="bfloat16", B=1, S=1, H=32, KV=8, D=128, cap=2048, lengths=None, total=None,
+             causal=1, window=-1, softcap=0.0, sink=False, smooth=-1, packed=False, new_rows=True, past=True,
+             in_place=False):
+    npdt = np.float32
+    lengths = [cap + S] * B if lengths is None else lengths
+    B = len(lengths)
+    total = max(lengths) if total is None else total
+    new_seq = S if new_rows else 0
+    q = (rng.standard_normal((B, S, H * D)) * 0.5).astype(npdt)
+    k = (rng.standard_normal((B, new_seq, KV * D)) * 0.5).astype(npdt)
+    v = (rng.standard_normal((B, new_seq, KV * D)) * 0.5).astype(npdt)
+    pkn = (rng.standard_normal((B, KV, cap, D)) * 0.5).astype(npdt) if past else None
+    pvn = (rng.standard_normal((B, KV, cap, D)) * 0.5).astype(npdt) if past else None
+    sk = np.linspace(-1, 1, H).astype(npdt) if sink else None
+    tdt = TORCH_DT[dtype]
+    to = lambda a: None if a is None else torch.from_numpy(a).to(DEV).to(tdt)
+    # round the inputs to the activation type first so the oracle sees the same values
+    qt, kt, vt, pkt, pvt, skt = map(to, (q, k, v, pkn, pvn, sk))
+    back = lambda t: None if t is None else t.float().cpu().numpy()
+    qn, kn, vn, pkr, pvr, skr = map(back, (qt, kt, vt, pkt, pvt, skt))
+    want, wk, wv = gqa_ref.group_query_attention(
+        qn, kn if new_rows else None, vn if new_rows else None, pkr, pvr, np.asarray(lengths) - 1, total,
+        num_heads=H, kv_num_heads=KV, causal=bool(causal), window=window, softcap=softcap, sink=skr,
+        smooth_softmax=smooth)
+    lens = torch.tensor(np.asarray(lengths) - 1, dtype=torch.int32, device=DEV)
+    kw = dict(num_heads=H, kv_num_heads=KV, causal=causal, local_window_size=window, softcap=softcap,
+              smooth_softmax=smooth)
+    if in_place:
+        kw.update(present_key=pkt, present_value=pvt)
+    if packed:
+        qkv = torch.cat([qt, kt, vt], dim=2).contiguous()
+        out, ok, ov = gqa.group_query_attention(qkv, None, None, pkt, pvt, lens, total, skt, **kw)
+    else:
+        out, ok, ov = gqa.group_query_attention(qt, kt, vt, pkt, pvt, lens, total, skt, **kw)
+    torch.cuda.synchronize()
+    check(back(out), want, dtype)
+    if ok is not None:
+        n = min(ok.shape[2], wk.shape[2])
+        np.testing.assert_array_equal(back(ok)[:, :, :n], wk[:, :, :n])
+        np.testing.assert_array_equal(back(ov)[:, :, :n], wv[:, :, :n])
+
+
+def test_config1_fp32_growing_cache():
+    """B=1, 32q/8kv, d128, fp32, past [1,8,2048,128], one new token, total 2049."""
+    run_case(np.random.default_rng(1), dtype="float32", cap=2048, lengths=[2049])
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_decode_dtypes_and_head_sizes(dtype, D):
+    run_case(np.random.default_rng(D), dtype=dtype, D=D, H=16, KV=4, cap=700, lengths=[701, 650, 10])
+
+
+@pytest.mark.parametrize("H,KV", [(8, 8), (32, 4), (64, 8), (24, 2)])
+def test_grouping(H, KV):
+    run_case(np.random.default_rng(H + KV), H=H, KV=KV, cap=300, lengths=[301, 120])
+
+
+def test_long_context_split_merge():
+    run_case(np.random.default_rng(5), cap=9000, lengths=[9001])
+
+
+@pytest.mark.parametrize("S", [7, 40, 300])
+def test_prefill_rows(S):
+    run_case(np.random.default_rng(S), S=S, cap=64, lengths=[64 + S, S + 5], H=8, KV=2)
+
+
+def test_prefill_without_past():
+    run_case(np.random.default_rng(9), S=33, past=False, cap=0, lengths=[33, 20], H=8, KV=2)
+
+
+@pytest.mark.parametrize("window,softcap,sink,smooth", [(16, 0.0, False, -1), (-1, 5.0, True, -1),
+                                                        (40, 3.0, False, 1), (-1, 0.0, False, 1)])
+def test_window_softcap_sink(window, softcap, sink, smooth):
+    run_case(np.random.default_rng(11), dtype="float16", S=5, cap=128, lengths=[133, 90], H=8, KV=2,
+             window=window, softcap=softcap, sink=sink, smooth=smooth)
+
+
+def test_bidirectional():
+    run_case(np.random.default_rng(12), S=9, cap=50, lengths=[59, 30], H=8, KV=4, causal=0)
+
+
+def test_packed_qkv():
+    run_case(np.random.default_rng(13), S=3, cap=40, lengths=[43], packed=True)
+
+
+def test_past_only_decode():
+    run_case(np.random.default_rng(14), S=1, cap=500, lengths=[500, 321], new_rows=False)
+
+
+def test_in_place_shared_buffer():
+    run_case(np.random.default_rng(15), S=2, cap=1024, lengths=[600, 1000], in_place=True)
