@@ -55,9 +55,10 @@ def parse():
     ap.add_argument("--pool-blocks", type=int, default=NB_PER_GPU, help="KV pool blocks per GPU")
     ap.add_argument("--mixed-chunks", type=int, default=8, help="mixed workload: prefill chunks")
     ap.add_argument("--mixed-decode", type=int, default=120, help="mixed workload: decode rows")
-    ap.add_argument("--workload", default="decode", choices=["decode", "mixed", "append"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "mixed", "append", "gqa"],
                     help="decode = BASELINE config 3 (the metric); mixed = config 4 (8 x 2048-token "
-                         "prefill chunks + 120 decode rows, 64q/8kv); append = config 2 (KV append alone)")
+                         "prefill chunks + 120 decode rows, 64q/8kv); append = config 2 (KV append alone); "
+                         "gqa = config 1 (GroupQueryAttention decode, contiguous fp32 cache)")
     ap.add_argument("--append-tokens", type=int, default=256, help="append workload: new tokens per call")
     return ap.parse_args()
 
@@ -574,8 +575,118 @@ def run_append(args):
     print(json.dumps(line), flush=True)
 
 
+def run_gqa(args):
+    """one GroupQueryAttention decode step, B=1, 32 q / 8 kv heads, d128, fp32,
+    past K/V [1, 8, 2048, 128] (BNSH), one new token, seqlens_k=[2048], total 2049, no rotary:
+    the growing contract, present = past ++ new rows [1, 8, 2049, 128]."""
+    import ctypes
+
+    import torch
+
+    from oracle import gqa_ref
+    from onnxruntime_ep_b200 import _capi, gqa
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    Hg, KVg, Dg, cap = 32, 8, 128, 2048
+    rng = np.random.default_rng(1)
+    qn = rng.standard_normal((1, 1, Hg * Dg), np.float32)
+    kn = rng.standard_normal((1, 1, KVg * Dg), np.float32)
+    vn = rng.standard_normal((1, 1, KVg * Dg), np.float32)
+    pkn = rng.standard_normal((1, KVg, cap, Dg), np.float32)
+    pvn = rng.standard_normal((1, KVg, cap, Dg), np.float32)
+    lens_h = np.array([cap], np.int32)
+    q, k, v, pk, pv = (torch.from_numpy(a).to(dev) for a in (qn, kn, vn, pkn, pvn))
+    lens = torch.from_numpy(lens_h).to(dev)
+    p, keep, out, present_k, present_v = gqa.build_params(q, k, v, pk, pv, lens, cap + 1, num_heads=Hg,
+                                                         kv_num_heads=KVg, host_seqlens_k=lens_h)
+    stream = torch.cuda.current_stream(dev)
+    pp, sp = ctypes.byref(p), ctypes.c_void_p(stream.cuda_stream)
+    for _ in range(max(args.warmup, 3)):
+        _capi.check(_capi.LIB.b200_group_query_attention(pp, sp))
+    torch.cuda.synchronize()
+    want, _, _ = gqa_ref.group_query_attention(qn, kn, vn, pkn, pvn, lens_h, cap + 1, num_heads=Hg, kv_num_heads=KVg)
+    max_err = float(np.abs(out.cpu().numpy() - want).max())
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    steps = max(args.steps, 20)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    launches0 = _capi.LIB.b200_launch_count()
+    with ClockSampler(0) as clocks:
+        for a_, b_ in ev:
+            flush.fill_(1)  # inputs (33.6 MB) fit in L2: flush between timed calls (untimed)
+            a_.record(stream)
+            _capi.check(_capi.LIB.b200_group_query_attention(pp, sp))
+            b_.record(stream)
+        torch.cuda.synchronize()
+    launches = (_capi.LIB.b200_launch_count() - launches0) / steps
+    ms = [a_.elapsed_time(b_) for a_, b_ in ev]
+    med = statistics.median(ms)
+    # past K/V read once, present K/V written once, plus q / new rows in and the output out
+    alg = (2 * KVg * cap * Dg * 4) + 2 * (KVg * (cap + 1) * Dg * 4) + (Hg * Dg + 2 * KVg * Dg) * 4 + Hg * Dg * 4
+
+    # e2e: the step's new inputs (q, k, v, seqlens) from pinned host memory, output back to the host
+    e2e_ms = None
+    if not args.no_e2e:
+        hq, hk, hv = (torch.from_numpy(a).pin_memory() for a in (qn, kn, vn))
+        hl = torch.from_numpy(lens_h).pin_memory()
+        ho = torch.empty((1, 1, Hg * Dg), dtype=torch.float32).pin_memory()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            q.copy_(hq, non_blocking=True)
+            k.copy_(hk, non_blocking=True)
+            v.copy_(hv, non_blocking=True)
+            lens.copy_(hl, non_blocking=True)
+            _capi.check(_capi.LIB.b200_group_query_attention(pp, sp))
+            ho.copy_(out, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / steps
+
+    # CPU baseline: the numpy restatement on this host's cores (ORT's CPU EP is not installed)
+    cpu = None
+    if not args.no_cpu_baseline:
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < min(args.cpu_seconds, 10.0) or n < 3:
+            gqa_ref.group_query_attention(qn, kn, vn, pkn, pvn, lens_h, cap + 1, num_heads=Hg, kv_num_heads=KVg)
+            n += 1
+        cpu_us = (time.perf_counter() - t0) / n * 1e6
+        cpu = {"value": cpu_us, "unit": "us/call", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"the whole config-1 call, {n} repetitions, numpy (BLAS threads) restatement of the op"}
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm = peaks.get("hbm_gbs", 6448.7)
+    gbs = alg / (med * 1e-3) / 1e9
+    line = {"metric": "GroupQueryAttention decode step time (config 1)", "value": med * 1e3, "unit": "us/call",
+            "higher_is_better": False, "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 3), "dtype": "f32",
+            "data": "synthetic (seeded numpy N(0,1))",
+            "config": {"workload": "BASELINE config 1: GroupQueryAttention decode, B=1, 32q/8kv, d128, fp32, past "
+                                   "[1,8,2048,128] BNSH, seqlens_k=[2048], total 2049, growing present [1,8,2049,128]",
+                       "l2": "flushed between calls (256 MiB write, untimed)"},
+            "p10_us": float(np.percentile(ms, 10)) * 1e3, "p90_us": float(np.percentile(ms, 90)) * 1e3,
+            "max_abs_err_vs_oracle": max_err,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "alg_bytes": alg, "kernel": "gqa_attention_kernel (split-K, fused present copy)"},
+            "cpu_baseline": cpu,
+            "e2e": None if e2e_ms is None else {"value": e2e_ms * 1e3, "unit": "us/call",
+                                                 "h2d_bytes_per_step": (Hg * Dg + 2 * KVg * Dg) * 4 + 4,
+                                                 "d2h_bytes_per_step": Hg * Dg * 4},
+            "clocks": clocks.summary(), "gpu_launches": int(round(launches * steps)),
+            "launches_per_call": launches}
+    print(json.dumps(line), flush=True)
+    del keep
+
+
 def main():
     args = parse()
+    if args.workload == "gqa":
+        run_gqa(args)
+        return
     if args.workload == "mixed":
         run_mixed(args)
         return

@@ -20,6 +20,7 @@
 //    one read and one write of the cache.  Otherwise a copy kernel builds `present`.
 #include <atomic>
 #include <cmath>
+#include <type_traits>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -30,10 +31,11 @@
 namespace b200 {
 namespace {
 
-constexpr int kRows = 16;      // query rows per CTA
+constexpr int kMaxRows = 16;   // query rows per CTA: 4, 8 or 16 (template R, from seq * g)
 constexpr int kKeys = 64;      // keys per chunk
 constexpr int kThreads = 128;
 constexpr int kMaxD = 256;
+constexpr int kMaxSplits = 128;  // key splits per row tile (merge weights live in shared memory)
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct GqaArgs {
@@ -52,8 +54,8 @@ struct GqaArgs {
   const void* sink;
   void* out;
   int row_tiles, splits, fused_copy, present_separate;
-  float* part_o;   // [groups][splits][kRows][D]
-  float* part_ml;  // [groups][splits][kRows][2]
+  float* part_o;   // [groups][splits][R][D]
+  float* part_ml;  // [groups][splits][R][2]
   int* counters;   // [groups]
 };
 
@@ -65,6 +67,45 @@ template <typename T> __device__ __forceinline__ T from_f(float x);
 template <> __device__ __forceinline__ float from_f<float>(float x) { return x; }
 template <> __device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_rn(x); }
 template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+// Read-only element and 4-element vector loads (ld.global.nc).  Nothing the attention kernel
+// reads is written during the call: in place, only the new-row positions of the past buffer are
+// written, and those rows are read from the key/value inputs.
+template <typename T> struct Vec4 { using raw = uint2; };  // 4 x 16-bit
+template <> struct Vec4<float> { using raw = float4; };
+template <typename T> __device__ __forceinline__ typename Vec4<T>::raw ld4(const T* p) {
+  return __ldg(reinterpret_cast<const typename Vec4<T>::raw*>(p));
+}
+template <typename T> __device__ __forceinline__ void st4(T* p, const typename Vec4<T>::raw& v) {
+  *reinterpret_cast<typename Vec4<T>::raw*>(p) = v;
+}
+__device__ __forceinline__ void unpack4(const float4& v, float (&x)[4]) {
+  x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+}
+template <typename T> __device__ __forceinline__ void unpack4(const uint2& v, float (&x)[4]);
+template <> __device__ __forceinline__ void unpack4<__half>(const uint2& v, float (&x)[4]) {
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+  x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
+}
+template <> __device__ __forceinline__ void unpack4<__nv_bfloat16>(const uint2& v, float (&x)[4]) {
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+  x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
+}
+template <typename T> __device__ __forceinline__ void unpack_raw(const typename Vec4<T>::raw& v, float (&x)[4]) {
+  if constexpr (std::is_same<T, float>::value) unpack4(v, x);
+  else unpack4<T>(v, x);
+}
+template <typename T> __device__ __forceinline__ T ldg1(const T* p) {
+  if constexpr (std::is_same<T, float>::value) return __ldg(p);
+  else {
+    const unsigned short u = __ldg(reinterpret_cast<const unsigned short*>(p));
+    T t;
+    memcpy(&t, &u, sizeof(u));
+    return t;
+  }
+}
 
 // Per batch row (:662-667): length, query_past, past (rows taken from the past cache).
 struct BatchGeom {
@@ -96,13 +137,13 @@ __device__ __forceinline__ T* present_row(const GqaArgs& a, int b, int kh, int p
   return base + (((int64_t)b * a.KV + kh) * a.pcap + pos) * a.D;
 }
 
-template <typename T>
+template <typename T, int R, int NC>
 __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a) {
-  __shared__ float qs[kRows][kMaxD];
-  __shared__ float sc[kRows][kKeys + 1];
-  __shared__ float m_run[kRows], l_run[kRows], alpha_s[kRows];
-  __shared__ int row_pos[kRows];  // absolute position of each row, or -1 (padding row)
-  __shared__ int row_end[kRows], row_start[kRows];
+  __shared__ float qs[R][kMaxD];
+  __shared__ float sc[R][kKeys + 1];
+  __shared__ float m_run[R], l_run[R], alpha_s[R];
+  __shared__ int row_pos[R];  // absolute position of each row, or -1 (padding row)
+  __shared__ int row_end[R], row_start[R];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int idx = blockIdx.x;
@@ -119,8 +160,8 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
 
   // Query rows of this tile (fp32, pre-scaled into the log2 domain unless softcap is on).
   const float qmul = a.softcap > 0.f ? 1.f : a.scale * kLog2e;
-  for (int i = tid; i < kRows * D; i += kThreads) {
-    const int r = i / D, d = i % D, rho = rt * kRows + r;
+  for (int i = tid; i < R * D; i += kThreads) {
+    const int r = i / D, d = i % D, rho = rt * R + r;
     float x = 0.f;
     if (rho < rows_total) {
       const int s = rho / g, hl = rho % g;
@@ -128,8 +169,8 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
     }
     qs[r][d] = x;
   }
-  if (tid < kRows) {
-    const int rho = rt * kRows + tid;
+  if (tid < R) {
+    const int rho = rt * R + tid;
     if (rho < rows_total) {
       const int pos = bg.query_past + rho / g;
       const int end = a.causal ? min(pos + 1, bg.length) : bg.length;
@@ -148,7 +189,7 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
 
   // Key range of the tile, then this CTA's share of its chunks.
   int kmin = bg.length, kmax = 0;
-  for (int r = 0; r < kRows; ++r)
+  for (int r = 0; r < R; ++r)
     if (row_pos[r] >= 0) {
       kmin = min(kmin, row_start[r]);
       kmax = max(kmax, row_end[r]);
@@ -162,44 +203,57 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
   const int my_lo = c_lo + (int)((int64_t)nch * sp / a.splits), my_hi = c_lo + (int)((int64_t)nch * (sp + 1) / a.splits);
 
   // Channels of this thread in P.V.
-  float o[kRows][2];
+  float o[R][NC];  // channels d0 = tid and, when NC == 2 (D > 128), d1 = tid + 128
 #pragma unroll
-  for (int r = 0; r < kRows; ++r) o[r][0] = o[r][1] = 0.f;
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int c = 0; c < NC; ++c) o[r][c] = 0.f;
   const int d0 = tid, d1 = tid + kThreads;
 
   for (int c = my_lo; c < my_hi; ++c) {
+    const int kend = min(kKeys, bg.length - c * kKeys);
     // ---- scores: thread = (key kk, channel half)
     {
       const int kk = tid >> 1, half = tid & 1;
       const int pos = c * kKeys + kk;
-      float acc[kRows];
+      float acc[R];
 #pragma unroll
-      for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
+      for (int r = 0; r < R; ++r) acc[r] = 0.f;
       if (pos < bg.length) {
         const T* krow = key_row<T>(a, bg, b, kh, pos, false);
         const bool copy = a.fused_copy && (a.present_separate || pos >= bg.past);
         T* kdst = copy ? present_row<T>(a, b, kh, pos, false) : nullptr;
-        const int dh = D / 2, dbeg = half * dh;
-        for (int d = dbeg; d < dbeg + dh; d += 4) {
-          float kx[4];
+        const int dh = D / 2, dbeg = half * dh, dend = dbeg + dh;
+        // groups of 16 vectors (64 channels): all loads of a group in flight before its stores
+        for (int d = dbeg; d < dend; d += 64) {
+          typename Vec4<T>::raw raw[16];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const T kv = krow[d + e];
-            kx[e] = to_f(kv);
-            if (copy) kdst[d + e] = kv;
+          for (int u = 0; u < 16; ++u)
+            if (d + 4 * u < dend) raw[u] = ld4(krow + d + 4 * u);
+          if (copy) {
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+              if (d + 4 * u < dend) st4(kdst + d + 4 * u, raw[u]);
           }
 #pragma unroll
-          for (int r = 0; r < kRows; ++r) {
-            const float4 qv = *reinterpret_cast<const float4*>(&qs[r][d]);
-            acc[r] = fmaf(qv.x, kx[0], fmaf(qv.y, kx[1], fmaf(qv.z, kx[2], fmaf(qv.w, kx[3], acc[r]))));
+          for (int u = 0; u < 16; ++u) {
+            if (d + 4 * u < dend) {
+              float kx[4];
+              unpack_raw<T>(raw[u], kx);
+#pragma unroll
+              for (int r = 0; r < R; ++r) {
+                const float4 qv = *reinterpret_cast<const float4*>(&qs[r][d + 4 * u]);
+                acc[r] = fmaf(qv.x, kx[0], fmaf(qv.y, kx[1], fmaf(qv.z, kx[2], fmaf(qv.w, kx[3], acc[r]))));
+              }
+            }
           }
         }
       }
 #pragma unroll
-      for (int r = 0; r < kRows; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
+      for (int r = 0; r < R; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
 #pragma unroll
-      for (int r = 0; r < kRows; ++r) {
-        if ((r >> 3) != half) continue;
+      for (int r = 0; r < R; ++r) {
+        if (r / (R / 2) != half) continue;
         float s = -INFINITY;
         if (row_pos[r] >= 0 && pos >= row_start[r] && pos < row_end[r]) {
           s = acc[r];
@@ -211,8 +265,8 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
     __syncthreads();
     // ---- online softmax: warp w owns rows 4w..4w+3, lane = keys 2*lane, 2*lane+1
 #pragma unroll
-    for (int rr = 0; rr < kRows / 4; ++rr) {
-      const int r = warp * (kRows / 4) + rr;
+    for (int rr = 0; rr < R / 4; ++rr) {
+      const int r = warp * (R / 4) + rr;
       const float s0 = sc[r][2 * lane], s1 = sc[r][2 * lane + 1];
       float mx = fmaxf(s0, s1);
       for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -236,33 +290,43 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
     // ---- P.V: thread = channels d0 (and d1 when D > 128)
     {
 #pragma unroll
-      for (int r = 0; r < kRows; ++r) {
+      for (int r = 0; r < R; ++r) {
         const float al = alpha_s[r];
-        o[r][0] *= al;
-        o[r][1] *= al;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) o[r][c] *= al;
       }
-      const int kend = min(kKeys, bg.length - c * kKeys);
-      for (int kk = 0; kk < kend; ++kk) {
-        const int pos = c * kKeys + kk;
-        const T* vrow = key_row<T>(a, bg, b, kh, pos, true);
-        const bool copy = a.fused_copy && (a.present_separate || pos >= bg.past);
-        T* vdst = copy ? present_row<T>(a, b, kh, pos, true) : nullptr;
-        float v0 = 0.f, v1 = 0.f;
-        if (d0 < D) {
-          const T x = vrow[d0];
-          v0 = to_f(x);
-          if (copy) vdst[d0] = x;
+      constexpr int kGroup = 16;  // keys whose V loads are in flight together
+      for (int k0 = 0; k0 < kend; k0 += kGroup) {
+        T x0[kGroup], x1[kGroup];
+#pragma unroll
+        for (int u = 0; u < kGroup; ++u) {
+          x0[u] = x1[u] = from_f<T>(0.f);
+          if (k0 + u < kend) {
+            const T* vrow = key_row<T>(a, bg, b, kh, c * kKeys + k0 + u, true);
+            if (d0 < D) x0[u] = ldg1(vrow + d0);
+            if (NC == 2 && d1 < D) x1[u] = ldg1(vrow + d1);
+          }
         }
-        if (d1 < D) {
-          const T x = vrow[d1];
-          v1 = to_f(x);
-          if (copy) vdst[d1] = x;
+        if (a.fused_copy) {
+#pragma unroll
+          for (int u = 0; u < kGroup; ++u) {
+            const int pos = c * kKeys + k0 + u;
+            if (k0 + u < kend && (a.present_separate || pos >= bg.past)) {
+              T* vdst = present_row<T>(a, b, kh, pos, true);
+              if (d0 < D) vdst[d0] = x0[u];
+              if (NC == 2 && d1 < D) vdst[d1] = x1[u];
+            }
+          }
         }
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) {
-          const float p = sc[r][kk];
-          o[r][0] = fmaf(p, v0, o[r][0]);
-          o[r][1] = fmaf(p, v1, o[r][1]);
+        for (int u = 0; u < kGroup; ++u) {
+          const float v0 = to_f(x0[u]), v1 = to_f(x1[u]);
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const float p = sc[r][min(k0 + u, kKeys - 1)];
+            o[r][0] = fmaf(p, v0, o[r][0]);
+            if constexpr (NC == 2) o[r][NC - 1] = fmaf(p, v1, o[r][NC - 1]);
+          }
         }
       }
     }
@@ -272,17 +336,17 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
   // ---- finish: direct output, or partial + last-CTA merge
   auto sink_log2 = [&](int r) -> float {
     if (a.sink == nullptr && !a.smooth) return -INFINITY;
-    const int hl = (rt * kRows + r) % g;
+    const int hl = (rt * R + r) % g;
     const float s = a.sink ? to_f(static_cast<const T*>(a.sink)[kh * g + hl]) : 0.f;
     return s * kLog2e;
   };
   auto store_row = [&](int r, int d, float v) {
-    const int rho = rt * kRows + r;
+    const int rho = rt * R + r;
     const int s = rho / g, hl = rho % g;
     static_cast<T*>(a.out)[((int64_t)b * a.S + s) * a.H * D + (int64_t)(kh * g + hl) * D + d] = from_f<T>(v);
   };
   if (a.splits == 1) {
-    for (int r = 0; r < kRows; ++r) {
+    for (int r = 0; r < R; ++r) {
       if (row_pos[r] < 0) continue;
       const float m = m_run[r], mu = m == -INFINITY ? 0.f : m;
       float L = l_run[r];
@@ -290,18 +354,23 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
       if (sk != -INFINITY) L += exp2f(sk - mu);
       const float inv = L > 0.f ? 1.f / L : 0.f;
       if (d0 < D) store_row(r, d0, o[r][0] * inv);
-      if (d1 < D) store_row(r, d1, o[r][1] * inv);
+      if constexpr (NC == 2) {
+        if (d1 < D) store_row(r, d1, o[r][NC - 1] * inv);
+      }
     }
     return;
   }
   {
-    float* po = a.part_o + ((int64_t)group * a.splits + sp) * kRows * D;
-    float* pml = a.part_ml + ((int64_t)group * a.splits + sp) * kRows * 2;
-    for (int r = 0; r < kRows; ++r) {
+    float* po = a.part_o + ((int64_t)group * a.splits + sp) * R * D;
+    float* pml = a.part_ml + ((int64_t)group * a.splits + sp) * R * 2;
+    for (int r = 0; r < R; ++r) {
+      if (row_pos[r] < 0) continue;
       if (d0 < D) po[r * D + d0] = o[r][0];
-      if (d1 < D) po[r * D + d1] = o[r][1];
+      if constexpr (NC == 2) {
+        if (d1 < D) po[r * D + d1] = o[r][NC - 1];
+      }
     }
-    if (tid < kRows) {
+    if (tid < R) {
       pml[tid * 2] = m_run[tid];
       pml[tid * 2 + 1] = l_run[tid];
     }
@@ -313,26 +382,62 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
   __syncthreads();
   if (!last) return;
   __threadfence();
-  for (int r = 0; r < kRows; ++r) {
+  // Merge, step 1: a warp per row (rows w, w+4, ...), lanes over splits: max, weights, sum.
+  __shared__ float wts[R][kMaxSplits];
+  __shared__ float inv_s[R];
+  const float* pml_g = a.part_ml + (int64_t)group * a.splits * R * 2;
+  for (int r = warp; r < R; r += kThreads / 32) {
     if (row_pos[r] < 0) continue;
-    const float* pml = a.part_ml + (int64_t)group * a.splits * kRows * 2;
     float M = -INFINITY;
-    for (int j = 0; j < a.splits; ++j) M = fmaxf(M, __ldcg(&pml[(j * kRows + r) * 2]));
+    for (int j = lane; j < a.splits; j += 32) M = fmaxf(M, __ldcg(&pml_g[(j * R + r) * 2]));
+    for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
     const float mu = M == -INFINITY ? 0.f : M;
-    float L = 0.f, acc0 = 0.f, acc1 = 0.f;
-    for (int j = 0; j < a.splits; ++j) {
-      const float mj = __ldcg(&pml[(j * kRows + r) * 2]);
+    float L = 0.f;
+    for (int j = lane; j < a.splits; j += 32) {
+      const float mj = __ldcg(&pml_g[(j * R + r) * 2]);
       const float w = mj == -INFINITY ? 0.f : exp2f(mj - mu);
-      L += w * __ldcg(&pml[(j * kRows + r) * 2 + 1]);
-      const float* po = a.part_o + ((int64_t)group * a.splits + j) * kRows * D + r * D;
-      if (d0 < D) acc0 += w * __ldcg(&po[d0]);
-      if (d1 < D) acc1 += w * __ldcg(&po[d1]);
+      wts[r][j] = w;
+      L += w * __ldcg(&pml_g[(j * R + r) * 2 + 1]);
     }
-    const float sk = sink_log2(r);
-    if (sk != -INFINITY) L += exp2f(sk - mu);
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    if (d0 < D) store_row(r, d0, acc0 * inv);
-    if (d1 < D) store_row(r, d1, acc1 * inv);
+    for (int off = 16; off; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    if (lane == 0) {
+      const float sk = sink_log2(r);
+      if (sk != -INFINITY) L += exp2f(sk - mu);
+      inv_s[r] = L > 0.f ? 1.f / L : 0.f;
+    }
+  }
+  __syncthreads();
+  // Step 2: each thread sums its channels over the splits for every row at once.
+  float acc[R][NC];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int c = 0; c < NC; ++c) acc[r][c] = 0.f;
+  const float* po_g = a.part_o + (int64_t)group * a.splits * R * D;
+  for (int j0 = 0; j0 < a.splits; j0 += 8) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u;
+      if (j >= a.splits) break;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if (row_pos[r] < 0) continue;
+        const float w = wts[r][j];
+        const float* po = po_g + ((int64_t)j * R + r) * D;
+        if (d0 < D) acc[r][0] = fmaf(w, __ldcg(&po[d0]), acc[r][0]);
+        if constexpr (NC == 2) {
+          if (d1 < D) acc[r][NC - 1] = fmaf(w, __ldcg(&po[d1]), acc[r][NC - 1]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (row_pos[r] < 0) continue;
+    if (d0 < D) store_row(r, d0, acc[r][0] * inv_s[r]);
+    if constexpr (NC == 2) {
+      if (d1 < D) store_row(r, d1, acc[r][NC - 1] * inv_s[r]);
+    }
   }
 }
 
@@ -379,18 +484,20 @@ int sm_count(const B200GqaParams* p) {
 }
 
 struct GqaPlan {
-  int row_tiles = 1, splits = 1, fused = 0;
+  int rows = kMaxRows, row_tiles = 1, splits = 1, fused = 0;
   size_t counters = 0, part_o = 0, part_ml = 0, total = 0;
 };
 
 GqaPlan gqa_plan(const B200GqaParams* p) {
   GqaPlan P;
   const int g = p->num_heads / p->kv_num_heads;
-  P.row_tiles = (p->seq * g + kRows - 1) / kRows;
+  const int rows_total = p->seq * g;
+  P.rows = rows_total <= 4 ? 4 : rows_total <= 8 ? 8 : kMaxRows;
+  P.row_tiles = (rows_total + P.rows - 1) / P.rows;
   const int64_t groups = (int64_t)p->batch * p->kv_num_heads * P.row_tiles;
   const int chunks = (std::max(p->total_sequence_length, 1) + kKeys - 1) / kKeys;
   const int target = 2 * sm_count(p);
-  P.splits = groups >= target ? 1 : (int)std::min<int64_t>(chunks, (target + groups - 1) / groups);
+  P.splits = groups >= target ? 1 : (int)std::min<int64_t>(std::min(chunks, kMaxSplits), (target + groups - 1) / groups);
   if (P.splits < 1) P.splits = 1;
   P.fused = P.row_tiles == 1 && !(p->local_window_size > 0);
   size_t off = 0;
@@ -401,8 +508,8 @@ GqaPlan gqa_plan(const B200GqaParams* p) {
   };
   if (P.splits > 1) {
     P.counters = take(sizeof(int) * groups);
-    P.part_o = take(sizeof(float) * groups * P.splits * kRows * p->head_size);
-    P.part_ml = take(sizeof(float) * groups * P.splits * kRows * 2);
+    P.part_o = take(sizeof(float) * groups * P.splits * P.rows * p->head_size);
+    P.part_ml = take(sizeof(float) * groups * P.splits * P.rows * 2);
   }
   P.total = std::max<size_t>(off, 256);
   return P;
@@ -430,6 +537,18 @@ int check_gqa(const B200GqaParams* p) {
     return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: softcap must be finite and non-negative");
   if (p->local_window_size < -1)
     return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: local_window_size must be -1 or positive");
+  {
+    // the kernels load K/V rows as 4-element vectors
+    const size_t align = p->dtype == B200_DTYPE_FLOAT ? 16 : 8;
+    const void* ptrs[] = {p->query, p->key, p->value, p->past_key, p->past_value, p->present_key, p->present_value};
+    bool ok = true;
+    for (const void* q : ptrs) ok &= (reinterpret_cast<uintptr_t>(q) % align) == 0;
+    const int64_t strides[] = {p->query_row_stride, p->key_row_stride, p->value_row_stride};
+    for (int64_t st : strides) ok &= st % 4 == 0;
+    if (!ok)
+      return gfail(B200_ERR_INVALID_ARGUMENT,
+                   "GroupQueryAttention: tensors must be aligned to 4 elements (16 bytes for float, 8 for 16-bit)");
+  }
   // attention.rs:992-997
   if (p->new_seq != p->seq && (p->new_seq != 0 || !p->past_key))
     return gfail(B200_ERR_FAIL, "GroupQueryAttention: K/V must match Q sequence or be empty with paired non-sliding past");
@@ -485,7 +604,17 @@ cudaError_t launch_gqa(const GqaArgs& a, const GqaPlan& P, bool tail_rows, cudaS
     if (e != cudaSuccess) return e;
     ++*launches;
   }
-  gqa_attention_kernel<T><<<(unsigned)grid, kThreads, 0, stream>>>(a);
+  const bool two = a.D > kThreads;
+  if (P.rows == 4) {
+    if (two) gqa_attention_kernel<T, 4, 2><<<(unsigned)grid, kThreads, 0, stream>>>(a);
+    else gqa_attention_kernel<T, 4, 1><<<(unsigned)grid, kThreads, 0, stream>>>(a);
+  } else if (P.rows == 8) {
+    if (two) gqa_attention_kernel<T, 8, 2><<<(unsigned)grid, kThreads, 0, stream>>>(a);
+    else gqa_attention_kernel<T, 8, 1><<<(unsigned)grid, kThreads, 0, stream>>>(a);
+  } else {
+    if (two) gqa_attention_kernel<T, kMaxRows, 2><<<(unsigned)grid, kThreads, 0, stream>>>(a);
+    else gqa_attention_kernel<T, kMaxRows, 1><<<(unsigned)grid, kThreads, 0, stream>>>(a);
+  }
   ++*launches;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
