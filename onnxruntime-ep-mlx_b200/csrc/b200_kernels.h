@@ -111,6 +111,9 @@ cudaError_t launch_decode_plan(const AttnArgs& a, const DecodePlan& plan, cudaSt
 // the byte strides of dims 1..rank-1.  Returns the CUresult.
 int encode_tensor_map(CUtensorMap* map, bool bf16, int rank, const void* base, const uint64_t* dims,
                       const uint64_t* strides, const uint32_t* box);
+// Same, for 8-bit elements (fp8 caches).
+int encode_tensor_map_u8(CUtensorMap* map, int rank, const void* base, const uint64_t* dims,
+                         const uint64_t* strides, const uint32_t* box);
 
 cudaError_t launch_decode(const AttnArgs& a, const DecodePlan& plan, const DecodeMaps& maps, int num_sms,
                           cudaStream_t stream);

@@ -247,11 +247,16 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // [NB*bs, KV, d] view of a cache: box {64 channels, 1 head, 16 slots}, 128-byte swizzle.
 int encode_cache_map(CUtensorMap* map, const void* base, const B200PagedAttentionParams* p) {
+  // [NB*bs, KV, d] view of a cache; a box is 16 slots of one kv head x 128 bytes of channels
+  // (64 16-bit or 128 fp8 elements)
+  const bool fp8 = p->cache_dtype == B200_DTYPE_FLOAT8E4M3FN;
+  const uint64_t esz = fp8 ? 1 : 2;
   const uint64_t dims[3] = {(uint64_t)p->head_size, (uint64_t)p->kv_num_heads,
                             (uint64_t)p->num_blocks * (uint64_t)p->block_size};
-  const uint64_t strides[2] = {(uint64_t)p->head_size * 2, (uint64_t)p->kv_num_heads * p->head_size * 2};
-  const uint32_t box[3] = {64, 1, (uint32_t)b200::kTile};
-  int r = b200::encode_tensor_map(map, p->act_dtype == B200_DTYPE_BFLOAT16, 3, base, dims, strides, box);
+  const uint64_t strides[2] = {(uint64_t)p->head_size * esz, (uint64_t)p->kv_num_heads * p->head_size * esz};
+  const uint32_t box[3] = {fp8 ? 128u : 64u, 1, (uint32_t)b200::kTile};
+  int r = fp8 ? b200::encode_tensor_map_u8(map, 3, base, dims, strides, box)
+              : b200::encode_tensor_map(map, p->act_dtype == B200_DTYPE_BFLOAT16, 3, base, dims, strides, box);
   if (r != CUDA_SUCCESS)
     return fail(B200_ERR_CUDA, "PagedAttention: cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
   return B200_OK;
@@ -368,6 +373,23 @@ int encode_tensor_map(CUtensorMap* map, bool bf16, int rank, const void* base, c
   return (int)enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank,
                   const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+int encode_tensor_map_u8(CUtensorMap* map, int rank, const void* base, const uint64_t* dims,
+                         const uint64_t* strides, const uint32_t* box) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return CUDA_ERROR_NOT_SUPPORTED;
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i > 0) st[i - 1] = strides[i - 1];
+  }
+  return (int)enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 }  // namespace b200
 

@@ -37,8 +37,10 @@ constexpr int kDecodeWarps = kDecodeWarpsPerCta;
 constexpr float kLog2e = 1.4426950408889634f;
 
 bool decode_supported(int head_size, int block_size, int act_dtype, int cache_dtype) {
-  return (head_size == 64 || head_size == 128 || head_size == 256) && block_size % kTile == 0 &&
-         act_dtype == cache_dtype && (act_dtype == B200_DTYPE_FLOAT16 || act_dtype == B200_DTYPE_BFLOAT16);
+  const bool act16 = act_dtype == B200_DTYPE_FLOAT16 || act_dtype == B200_DTYPE_BFLOAT16;
+  if (!act16 || block_size % kTile != 0) return false;
+  if (cache_dtype == B200_DTYPE_FLOAT8E4M3FN) return head_size == 128 || head_size == 256;
+  return (head_size == 64 || head_size == 128 || head_size == 256) && act_dtype == cache_dtype;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -120,13 +122,33 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(AttnArgs a, DecodePla
 // ---------------------------------------------------------------------------------------
 // Decode kernel
 // ---------------------------------------------------------------------------------------
-template <int D>
+template <int D, bool FP8>
 struct DecodeLayout {
-  static constexpr int kBoxes = D / 64;                 // 64-channel TMA boxes per tile row
-  static constexpr int kBoxBytes = kTile * 128;         // 16 rows x 128 B
-  static constexpr int kTileBytes = kTile * D * 2;      // one tensor, one tile
-  static constexpr int kStageBytes = 2 * kTileBytes;    // K + V
+  static constexpr int kElem = FP8 ? 1 : 2;              // stored bytes per element
+  static constexpr int kBoxCols = 128 / kElem;           // elements per 128-byte TMA box row
+  static constexpr int kBoxes = D / kBoxCols;            // TMA boxes per tile row
+  static constexpr int kBoxBytes = kTile * 128;          // 16 rows x 128 B
+  static constexpr int kTileBytes = kTile * D * kElem;   // one tensor, one tile, as stored
+  static constexpr int kStageBytes = 2 * kTileBytes;     // K + V
+  static constexpr int kWideBytes = kTile * D * 2;       // one tensor, one tile, 16-bit (MMA input)
 };
+
+// fp8 e4m3 -> fp16, 16 values (exact: every e4m3 value is an fp16 value).
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(r) : "r"(pair));
+  return r;
+}
+__device__ __forceinline__ void e4m3x16_to_f16(const uint4& q, uint4& lo, uint4& hi) {
+  lo.x = e4m3x2_to_f16x2(q.x & 0xffffu);
+  lo.y = e4m3x2_to_f16x2(q.x >> 16);
+  lo.z = e4m3x2_to_f16x2(q.y & 0xffffu);
+  lo.w = e4m3x2_to_f16x2(q.y >> 16);
+  hi.x = e4m3x2_to_f16x2(q.z & 0xffffu);
+  hi.y = e4m3x2_to_f16x2(q.z >> 16);
+  hi.z = e4m3x2_to_f16x2(q.w & 0xffffu);
+  hi.w = e4m3x2_to_f16x2(q.w >> 16);
+}
 
 // Byte offset of 16-byte chunk `chunk` (global over the d channels) of tile row `row` in a
 // 128B-swizzled tile written by the TMA boxes.
@@ -146,11 +168,14 @@ struct Piece {
 __device__ __forceinline__ int64_t range_start(int64_t g, int64_t T, int64_t W) { return g * T / W; }
 __device__ __forceinline__ int64_t warp_of(int64_t x, int64_t T, int64_t W) { return ((x + 1) * W + T - 1) / T - 1; }
 
-template <typename T, int D, int STAGES>
+// T: the MMA type (the activation type; fp16 for fp8 caches, whose tiles are converted to fp16
+// in shared memory and whose per-(block, kv head) scales multiply S and P per tile).
+template <typename T, int D, int STAGES, bool FP8>
 __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant__ AttnArgs a,
                                                            const __grid_constant__ DecodeMaps maps,
                                                            const DecodePlan plan) {
-  using L = DecodeLayout<D>;
+  using L = DecodeLayout<D, FP8>;
+  constexpr int kWarpBytes = STAGES * L::kStageBytes + (FP8 ? 2 * L::kWideBytes : 0);
   using MMA = mma_op<T>;
   constexpr int KSTEPS = D / 16;
   constexpr int RING = STAGES + 1;  // pieces live at once: one per in-flight tile + the newest
@@ -160,7 +185,8 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* wbase = smem + warp * STAGES * L::kStageBytes;
+  uint8_t* wbase = smem + warp * kWarpBytes;
+  uint8_t* wide = wbase + STAGES * L::kStageBytes;  // fp8 only: the current tile as fp16 K, V
   const uint32_t wbase_u32 = smem_u32(wbase);
   Piece* myring = ring[warp];
 
@@ -230,8 +256,8 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
     mbar_arrive_expect_tx(bar, L::kStageBytes);
 #pragma unroll
     for (int h = 0; h < L::kBoxes; ++h) {
-      tma_load_3d(kdst + h * L::kBoxBytes, &maps.k_map, bar, h * 64, u.kh, z);
-      tma_load_3d(vdst + h * L::kBoxBytes, &maps.v_map, bar, h * 64, u.kh, z);
+      tma_load_3d(kdst + h * L::kBoxBytes, &maps.k_map, bar, h * L::kBoxCols, u.kh, z);
+      tma_load_3d(vdst + h * L::kBoxBytes, &maps.v_map, bar, h * L::kBoxCols, u.kh, z);
     }
   };
 
@@ -282,8 +308,15 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
             reinterpret_cast<const T*>(a.q) + (int64_t)(u.c0 + qi) * a.q_stride + (int64_t)(u.kh * g + hl) * D;
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; ++kk) {
-          qf[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + kq);
-          qf[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + kq);
+          if constexpr (FP8) {
+            // fp16 MMA: the activation row (fp16 or bf16) converted pairwise
+            const int64_t e0 = (int64_t)(u.c0 + qi) * a.q_stride + (int64_t)(u.kh * g + hl) * D + kk * 16 + kq;
+            qf[kk][0] = MMA::pack(load_act(a.q, e0, a.act_dtype), load_act(a.q, e0 + 1, a.act_dtype));
+            qf[kk][1] = MMA::pack(load_act(a.q, e0 + 8, a.act_dtype), load_act(a.q, e0 + 9, a.act_dtype));
+          } else {
+            qf[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + kq);
+            qf[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + kq);
+          }
         }
       } else {
 #pragma unroll
@@ -312,17 +345,55 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
       pending &= ~(1u << s);
       const int32_t blk = a.block_table[(int64_t)u.b * a.max_blocks + pos0 / a.block_size];
       const bool blk_ok = blk >= 0 && blk < a.num_blocks;
-      const uint32_t kbase = wbase_u32 + s * L::kStageBytes;
-      const uint32_t vbase = kbase + L::kTileBytes;
+      uint32_t kbase = wbase_u32 + s * L::kStageBytes;
+      uint32_t vbase = kbase + L::kTileBytes;
+      float k_sc = 1.f, v_sc = 1.f;
+      if constexpr (FP8) {
+        // fp8 tile -> fp16 tile in the 16-bit swizzled layout the fragment loads expect
+        const uint8_t* kst = wbase + s * L::kStageBytes;
+        const uint8_t* vst = kst + L::kTileBytes;
+        constexpr int FC = D / 16;  // 16-byte fp8 chunks per row
+        for (int idx = lane; idx < kTile * FC; idx += 32) {
+          const int row = idx / FC, c = idx % FC;
+          const uint32_t off = (uint32_t)((c >> 3) * L::kBoxBytes + row * 128 + (((c & 7) ^ (row & 7)) << 4));
+          uint4 lo, hi;
+          e4m3x16_to_f16(*reinterpret_cast<const uint4*>(kst + off), lo, hi);
+          *reinterpret_cast<uint4*>(wide + swz(row, 2 * c)) = lo;
+          *reinterpret_cast<uint4*>(wide + swz(row, 2 * c + 1)) = hi;
+          // V rows past the sequence (or of an invalid block) become zeros: P is 0 there, and
+          // 0 x NaN from whatever an unused slot holds would still poison O
+          if (blk_ok && pos0 + row < u.total) {
+            e4m3x16_to_f16(*reinterpret_cast<const uint4*>(vst + off), lo, hi);
+          } else {
+            lo = hi = make_uint4(0u, 0u, 0u, 0u);
+          }
+          *reinterpret_cast<uint4*>(wide + L::kWideBytes + swz(row, 2 * c)) = lo;
+          *reinterpret_cast<uint4*>(wide + L::kWideBytes + swz(row, 2 * c + 1)) = hi;
+        }
+        __syncwarp();
+        kbase = smem_u32(wide);
+        vbase = kbase + L::kWideBytes;
+        if (blk_ok) {
+          k_sc = a.k_scale[(int64_t)blk * KV + u.kh];
+          v_sc = a.v_scale[(int64_t)blk * KV + u.kh];
+        }
+      }
 
-      // Overlay: tile rows at positions >= past hold the sequence's own new K/V rows.
-      const bool overlay = pos0 + kTile > u.past;
+      // Overlay: tile rows at positions >= past hold the sequence's own new K/V rows (16-bit
+      // caches; an fp8 cache is read whole, new rows included, as encoded caches are).
+      const bool overlay = !FP8 && pos0 + kTile > u.past;
       if (overlay) {
         constexpr int CH = D / 8;  // 16-byte chunks per row
         for (int idx = lane; idx < kTile * CH; idx += 32) {
           const int row = idx / CH, chunk = idx % CH;
           const int pos = pos0 + row;
-          if (pos < u.past || pos >= u.total) continue;
+          if (pos >= u.total) {
+            // rows past the sequence: V becomes zeros (P is 0 there; 0 x NaN from an unused slot
+            // would still poison O)
+            *reinterpret_cast<uint4*>(wbase + (vbase - wbase_u32) + swz(row, chunk)) = make_uint4(0u, 0u, 0u, 0u);
+            continue;
+          }
+          if (pos < u.past) continue;
           const int64_t tok = u.c0 + (pos - u.past);
           const uint4 kv = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) + tok * a.k_stride +
                                                            (int64_t)u.kh * D + chunk * 8);
@@ -362,7 +433,7 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
         bool vis = blk_ok && col < rows && pos < u.total;
         if (a.is_causal) vis = vis && pos <= u.past + qi;
         if (a.window > 0) vis = vis && pos >= u.past + qi - a.window + 1;
-        float x = c[e] * qk_scale;
+        float x = c[e] * k_sc * qk_scale;
         if (a.softcap > 0.f) x = a.softcap * tanhf(x / a.softcap) * kLog2e;
         sc[e] = vis ? x : -INFINITY;
       }
@@ -387,10 +458,11 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
         o[mt][1] *= al1; o[mt][3] *= al1;
       }
 
-      // P^T -> B fragments (hi + lo 16-bit split).
-      const uint32_t x0 = MMA::pack(p0, p1), x1 = MMA::pack(p2, p3);
+      // P^T -> B fragments (hi + lo 16-bit split); an fp8 tile's V scale rides on P.
+      const float q0 = p0 * v_sc, q1 = p1 * v_sc, q2 = p2 * v_sc, q3 = p3 * v_sc;
+      const uint32_t x0 = MMA::pack(q0, q1), x1 = MMA::pack(q2, q3);
       const float2 h0 = MMA::unpack(x0), h1 = MMA::unpack(x1);
-      const uint32_t y0 = MMA::pack(p0 - h0.x, p1 - h0.y), y1 = MMA::pack(p2 - h1.x, p3 - h1.y);
+      const uint32_t y0 = MMA::pack(q0 - h0.x, q1 - h0.y), y1 = MMA::pack(q2 - h1.x, q3 - h1.y);
       const uint32_t bh0 = movm_t(x0), bh1 = movm_t(x1), bl0 = movm_t(y0), bl1 = movm_t(y1);
 
       // O^T += V_tile^T . P^T
@@ -528,25 +600,25 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
 // ---------------------------------------------------------------------------------------
 // Launch
 // ---------------------------------------------------------------------------------------
-template <typename T, int D, int STAGES>
+template <typename T, int D, int STAGES, bool FP8 = false>
 static cudaError_t launch_decode_t(const AttnArgs& a, const DecodePlan& plan, const DecodeMaps& maps, int num_sms,
                                    cudaStream_t stream) {
-  using L = DecodeLayout<D>;
-  constexpr size_t smem = (size_t)kDecodeWarps * STAGES * L::kStageBytes + 1024;
+  using L = DecodeLayout<D, FP8>;
+  constexpr size_t smem = (size_t)kDecodeWarps * (STAGES * L::kStageBytes + (FP8 ? 2 * L::kWideBytes : 0)) + 1024;
   static int occupancy[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
   if (occupancy[dev] == 0) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<T, D, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<T, D, STAGES, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, paged_decode_kernel<T, D, STAGES>, 128, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, paged_decode_kernel<T, D, STAGES, FP8>, 128, smem);
     if (e != cudaSuccess) return e;
     occupancy[dev] = occ < 1 ? 1 : (occ > kDecodeMaxCtasPerSm ? kDecodeMaxCtasPerSm : occ);
   }
-  paged_decode_kernel<T, D, STAGES><<<num_sms * occupancy[dev], 128, smem, stream>>>(a, maps, plan);
+  paged_decode_kernel<T, D, STAGES, FP8><<<num_sms * occupancy[dev], 128, smem, stream>>>(a, maps, plan);
   return cudaGetLastError();
 }
 
@@ -558,6 +630,13 @@ cudaError_t launch_decode_plan(const AttnArgs& a, const DecodePlan& plan, cudaSt
 cudaError_t launch_decode(const AttnArgs& a, const DecodePlan& plan, const DecodeMaps& maps, int num_sms,
                           cudaStream_t stream) {
   const bool bf = a.act_dtype == B200_DTYPE_BFLOAT16;
+  if (a.cache_dtype == B200_DTYPE_FLOAT8E4M3FN) {
+    switch (a.head_size) {
+      case 128: return launch_decode_t<__half, 128, 4, true>(a, plan, maps, num_sms, stream);
+      case 256: return launch_decode_t<__half, 256, 2, true>(a, plan, maps, num_sms, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (a.head_size) {
     case 64: return bf ? launch_decode_t<__nv_bfloat16, 64, 4>(a, plan, maps, num_sms, stream)
                        : launch_decode_t<__half, 64, 4>(a, plan, maps, num_sms, stream);

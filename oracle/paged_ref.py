@@ -244,7 +244,8 @@ def paged_attention(q, k, v, key_cache, value_cache, cum, past, block_table,
     Returns ``(output fp32 [nt, H*d], key_cache', value_cache')``; the caches are copies
     updated exactly as the reference updates its input buffers (bit-exact contract).
     ``k``/``v`` ``None`` means packed QKV in ``q`` (attention.rs:3877-3890).
-    ``fp8_scales`` (fp32 ``[NB, KV]``) selects the fp8-e4m3 per-block-per-head extension.
+    ``fp8_scales`` (fp32 ``[NB, KV]``, or a ``(k_scales, v_scales)`` pair) selects the
+    fp8-e4m3 per-block-per-head extension.
     ``round_activations`` rounds the normalised / rotated Q and K rows back to the activation
     dtype after each step, as the reference's MLX ops do (their outputs carry dtype T); the
     reference test oracle keeps them in fp32, which differs only within tolerance.
@@ -282,11 +283,12 @@ def paged_attention(q, k, v, key_cache, value_cache, cum, past, block_table,
 
     pairs = write_slots(cum, past, block_table, slot_mapping, bs)
     if fp8_scales is not None:
+        k8, v8 = fp8_scales if isinstance(fp8_scales, tuple) else (fp8_scales, fp8_scales)
+        k8, v8 = np.asarray(k8, np.float32), np.asarray(v8, np.float32)
         for token, slot in pairs:
             blk, off = divmod(slot, bs)
-            s = np.asarray(fp8_scales, np.float32)[blk][:, None]
-            kc[blk, off] = fp8_encode(kf[token], s)
-            vc[blk, off] = fp8_encode(vf[token], s)
+            kc[blk, off] = fp8_encode(kf[token], k8[blk][:, None])
+            vc[blk, off] = fp8_encode(vf[token], v8[blk][:, None])
     else:
         kv_append(kc, vc, kf, vf, pairs, kquant, vquant)
 
@@ -307,9 +309,8 @@ def paged_attention(q, k, v, key_cache, value_cache, cum, past, block_table,
             keys = quant_decode(kc[blocks, offs], kquant.scale_view(KV, d), kquant.bits, d)
             vals = quant_decode(vc[blocks, offs], vquant.scale_view(KV, vf.shape[-1]), vquant.bits, vf.shape[-1])
         elif fp8_scales is not None:
-            s = np.asarray(fp8_scales, np.float32)[blocks][:, :, None]
-            keys = fp8_decode(kc[blocks, offs], s)
-            vals = fp8_decode(vc[blocks, offs], s)
+            keys = fp8_decode(kc[blocks, offs], k8[blocks][:, :, None])
+            vals = fp8_decode(vc[blocks, offs], v8[blocks][:, :, None])
         else:
             keys = to_f32(kc[blocks, offs])
             vals = to_f32(vc[blocks, offs])
