@@ -55,10 +55,11 @@ def parse():
     ap.add_argument("--pool-blocks", type=int, default=NB_PER_GPU, help="KV pool blocks per GPU")
     ap.add_argument("--mixed-chunks", type=int, default=8, help="mixed workload: prefill chunks")
     ap.add_argument("--mixed-decode", type=int, default=120, help="mixed workload: decode rows")
-    ap.add_argument("--workload", default="decode", choices=["decode", "mixed", "append", "gqa"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "mixed", "append", "gqa", "fp8"],
                     help="decode = BASELINE config 3 (the metric); mixed = config 4 (8 x 2048-token "
                          "prefill chunks + 120 decode rows, 64q/8kv); append = config 2 (KV append alone); "
-                         "gqa = config 1 (GroupQueryAttention decode, contiguous fp32 cache)")
+                         "gqa = config 1 (GroupQueryAttention decode, contiguous fp32 cache); "
+                         "fp8 = config 5 (fp8 e4m3 KV decode, 256 seqs, 64q/8kv sharded over the GPUs)")
     ap.add_argument("--append-tokens", type=int, default=256, help="append workload: new tokens per call")
     return ap.parse_args()
 
@@ -682,8 +683,194 @@ def run_gqa(args):
     del keep
 
 
+def run_fp8(args):
+    """paged GQA decode over an fp8 e4m3 KV cache with per-(block, kv head)
+    fp32 scales U(0.01, 0.1); 64 q / 8 kv heads, d128, bs16, B=256 one-token sequences with
+    contexts U[4096, 32768]; Q bf16 N(0,1).  The 8 kv heads are sharded over the N ranks (strong
+    scaling: the job is fixed) and one NCCL all-gather reassembles the outputs."""
+    import ctypes
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    n = max(world, 1)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from onnxruntime_ep_b200 import _capi, paged, sharding
+
+    H5, KV5, B5, bs = 64, 8, 256, 16
+    if KV5 % n:
+        raise SystemExit(f"--gpus {n} must divide the 8 kv heads")
+    kvh, qh = KV5 // n, H5 // n
+    rng = np.random.default_rng(5)
+    L = rng.integers(4096, 32768, size=B5, endpoint=True)
+    need = -(-L // bs)
+    NB = int(need.sum())
+    perm = rng.permutation(NB).astype(np.int32)
+    bt = np.zeros((B5, int(need.max())), np.int32)
+    off = 0
+    for b in range(B5):
+        bt[b, :need[b]] = perm[off:off + need[b]]
+        off += int(need[b])
+    cum = np.arange(B5 + 1, dtype=np.int32)
+    past = (L - 1).astype(np.int32)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5000 + rank)
+    ks = torch.empty((NB, kvh), dtype=torch.float32, device=dev).uniform_(0.01, 0.1, generator=g)
+    vs = torch.empty_like(ks).uniform_(0.01, 0.1, generator=g)
+    kc = torch.empty((NB, bs, kvh, D), dtype=torch.float8_e4m3fn, device=dev)
+    vc = torch.empty_like(kc)
+    step_b = 8192
+    for b0 in range(0, NB, step_b):  # codes of N(0,1) / scale, generated in slices
+        b1 = min(NB, b0 + step_b)
+        for cache, sc in ((kc, ks), (vc, vs)):
+            x = torch.randn((b1 - b0, bs, kvh, D), generator=g, device=dev) / sc[b0:b1, None, :, None]
+            cache[b0:b1] = x.clamp_(-448.0, 448.0).to(torch.float8_e4m3fn)
+    q = torch.randn((B5, qh * D), generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn((B5, kvh * D), generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn((B5, kvh * D), generator=g, device=dev).to(torch.bfloat16)
+    cum_d, past_d, bt_d = (torch.from_numpy(a).to(dev) for a in (cum, past, bt))
+    host = {"cumulative_sequence_length": cum, "past_seqlens": past, "block_table": bt}
+    p, keep, out = paged.build_params(q, k, v, kc, vc, cum_d, past_d, bt_d, num_heads=qh, kv_num_heads=kvh,
+                                      k_scale=ks, v_scale=vs, host_metadata=host)
+    stream = torch.cuda.current_stream(dev)
+    sp, pp = ctypes.c_void_p(stream.cuda_stream), ctypes.byref(p)
+    gathered = torch.empty((n, B5, qh * D), dtype=torch.bfloat16, device=dev) if n > 1 else None
+
+    def step():
+        _capi.check(_capi.LIB.b200_paged_attention(pp, sp))
+        if n > 1:
+            dist.all_gather_into_tensor(gathered, out)
+            return sharding.reassemble(gathered)
+        return out
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    _capi.check(_capi.LIB.b200_read_status(pp, sp))
+    steps = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a_, b_ in ev:
+        a_.record(stream)
+        b_.record(stream)
+    launches0 = _capi.LIB.b200_launch_count()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t0.record(stream)
+        for i in range(steps):
+            p.attention_event_begin = ctypes.c_void_p(ev[i][0].cuda_event)
+            p.attention_event_end = ctypes.c_void_p(ev[i][1].cuda_event)
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+    p.attention_event_begin = p.attention_event_end = None
+    launches = _capi.LIB.b200_launch_count() - launches0
+    elapsed_ms = t0.elapsed_time(t1)
+    attn_ms = statistics.mean(a_.elapsed_time(b_) for a_, b_ in ev)
+
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        hcum, hpast, hbt = (torch.from_numpy(a).pin_memory() for a in (cum, past, bt))
+        hout = torch.empty((B5, H5 * D), dtype=torch.bfloat16).pin_memory()
+        h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hcum, hpast, hbt))
+
+        def e2e_step():
+            q.copy_(hq, non_blocking=True); k.copy_(hk, non_blocking=True); v.copy_(hv, non_blocking=True)
+            cum_d.copy_(hcum, non_blocking=True); past_d.copy_(hpast, non_blocking=True)
+            bt_d.copy_(hbt, non_blocking=True)
+            hout.copy_(step(), non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([elapsed_ms, attn_ms, e_ms if e2e is None and not args.no_e2e else 0.0], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, attn_ms = float(t[0]), float(t[1])
+        if not args.no_e2e:
+            e_ms = float(t[2])
+    if not args.no_e2e:
+        e2e = {"value": B5 / (e_ms / steps / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(hout.numel() * hout.element_size())}
+    _capi.check(_capi.LIB.b200_read_status(pp, sp))
+    ms_per_step = elapsed_ms / steps
+    kv_bytes = int(L.sum()) * kvh * D * 2 + int(need.sum()) * kvh * 4 * 2
+    alg = kv_bytes + B5 * (qh + 2 * kvh) * D * 2 + B5 * qh * D * 2 + int(need.sum()) * 4
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm = peaks.get("hbm_gbs", 6448.7)
+    achieved = alg / (attn_ms / 1e3) / 1e9
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and n == 1:
+            from oracle import paged_ref as ref
+            import ml_dtypes
+            sample = [0, 1]
+            cpu_s = 0.0
+            for b in sample:
+                blocks = bt[b, :need[b]]
+                kcb = kc[torch.from_numpy(blocks).to(dev)].view(torch.uint8).cpu().numpy().view(ml_dtypes.float8_e4m3fn)
+                vcb = vc[torch.from_numpy(blocks).to(dev)].view(torch.uint8).cpu().numpy().view(ml_dtypes.float8_e4m3fn)
+                ksb, vsb = ks[torch.from_numpy(blocks).to(dev)].cpu().numpy(), vs[torch.from_numpy(blocks).to(dev)].cpu().numpy()
+                qb = q[b:b + 1].float().cpu().numpy().astype(ref.BF16)
+                kb = k[b:b + 1].float().cpu().numpy().astype(ref.BF16)
+                vb = v[b:b + 1].float().cpu().numpy().astype(ref.BF16)
+                btb = np.arange(need[b], dtype=np.int32)[None]
+                t_b = time.perf_counter()
+                ref.paged_attention(qb, kb, vb, kcb, vcb, np.array([0, 1], np.int32), past[b:b + 1], btb, H5, KV5,
+                                    fp8_scales=(ksb, vsb))
+                cpu_s += time.perf_counter() - t_b  # only the oracle call is timed
+            cpu = {"value": len(sample) / cpu_s if cpu_s > 0 else None, "unit": UNIT, "cores": 1, "kind": "port",
+                   "sample": f"sequences {sample} (L={[int(L[b]) for b in sample]}) through the numpy restatement"}
+        line = {"metric": "paged GQA fp8 decode tokens/s (config 5)", "value": B5 / (ms_per_step / 1e3),
+                "unit": UNIT, "n_gpus": n, "steps": steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp8-e4m3 KV, bf16 Q",
+                "data": "synthetic (seeded numpy metadata, torch-seeded codes of N(0,1)/scale)",
+                "config": {"workload": "BASELINE config 5: fp8 e4m3 paged GQA decode, 64q/8kv (sharded by kv head), d128, "
+                                       "bs16, B=256, ctx U[4096,32768], per-(block, kv head) scales U(0.01,0.1)",
+                           "kv_heads_per_gpu": kvh, "num_blocks": NB,
+                           "l2": f"inputs larger than L2 ({kv_bytes / 1e9:.2f} GB of KV per step per GPU)",
+                           "parallelism": f"kv-head shard x{n}" + (" + NCCL all-gather" if n > 1 else "")},
+                "kv_read_gbs": kv_bytes / (attn_ms / 1e3) / 1e9,
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                             "kernel": "attention section (paged_decode_kernel fp8, split-K combine fused in)",
+                             "alg_bytes_per_launch": alg, "ms_per_launch": attn_ms},
+                "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(), "gpu_launches": int(launches)}
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.workload == "fp8":
+        run_fp8(args)
+        return
     if args.workload == "gqa":
         run_gqa(args)
         return

@@ -130,24 +130,25 @@ struct DecodeLayout {
   static constexpr int kBoxBytes = kTile * 128;          // 16 rows x 128 B
   static constexpr int kTileBytes = kTile * D * kElem;   // one tensor, one tile, as stored
   static constexpr int kStageBytes = 2 * kTileBytes;     // K + V
-  static constexpr int kWideBytes = kTile * D * 2;       // one tensor, one tile, 16-bit (MMA input)
 };
 
-// fp8 e4m3 -> fp16, 16 values (exact: every e4m3 value is an fp16 value).
+// Two fp8 e4m3 values (low, high byte of `pair`) -> fp16x2, exact (every e4m3 value is an
+// fp16 value); the low byte lands in the low half.
 __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair) {
   uint32_t r;
   asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(r) : "r"(pair));
   return r;
 }
-__device__ __forceinline__ void e4m3x16_to_f16(const uint4& q, uint4& lo, uint4& hi) {
-  lo.x = e4m3x2_to_f16x2(q.x & 0xffffu);
-  lo.y = e4m3x2_to_f16x2(q.x >> 16);
-  lo.z = e4m3x2_to_f16x2(q.y & 0xffffu);
-  lo.w = e4m3x2_to_f16x2(q.y >> 16);
-  hi.x = e4m3x2_to_f16x2(q.z & 0xffffu);
-  hi.y = e4m3x2_to_f16x2(q.z >> 16);
-  hi.z = e4m3x2_to_f16x2(q.w & 0xffffu);
-  hi.w = e4m3x2_to_f16x2(q.w >> 16);
+
+// fp8 tiles feed the fp16 MMAs straight from registers:
+//  * K: ldmatrix of the fp8 bytes as 16-bit pairs gives lane (g, t) channels 4t..4t+3 of its
+//    row; the MMA's K index 2t+j is channel 4t+j and 2t+8+j is channel 4t+2+j within each
+//    16-channel block, and Q's fragments are loaded with the same permutation;
+//  * V: ldmatrix.trans gives lane (g, t) channels 2g, 2g+1 of tokens 2t, 2t+1; after the
+//    conversion a byte permute regroups them per channel, so MMA row g is channel 2g and row
+//    g+8 is channel 2g+1 of the 16-channel block (the output channel index follows).
+__device__ __forceinline__ int out_channel(bool fp8, int mt, int dr, int hi) {
+  return fp8 ? mt * 16 + 2 * dr + hi : mt * 16 + dr + 8 * hi;
 }
 
 // Byte offset of 16-byte chunk `chunk` (global over the d channels) of tile row `row` in a
@@ -175,7 +176,7 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
                                                            const __grid_constant__ DecodeMaps maps,
                                                            const DecodePlan plan) {
   using L = DecodeLayout<D, FP8>;
-  constexpr int kWarpBytes = STAGES * L::kStageBytes + (FP8 ? 2 * L::kWideBytes : 0);
+  constexpr int kWarpBytes = STAGES * L::kStageBytes;
   using MMA = mma_op<T>;
   constexpr int KSTEPS = D / 16;
   constexpr int RING = STAGES + 1;  // pieces live at once: one per in-flight tile + the newest
@@ -186,7 +187,6 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* wbase = smem + warp * kWarpBytes;
-  uint8_t* wide = wbase + STAGES * L::kStageBytes;  // fp8 only: the current tile as fp16 K, V
   const uint32_t wbase_u32 = smem_u32(wbase);
   Piece* myring = ring[warp];
 
@@ -309,10 +309,11 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; ++kk) {
           if constexpr (FP8) {
-            // fp16 MMA: the activation row (fp16 or bf16) converted pairwise
-            const int64_t e0 = (int64_t)(u.c0 + qi) * a.q_stride + (int64_t)(u.kh * g + hl) * D + kk * 16 + kq;
+            // fp16 MMA on the fp8 channel permutation: K index 2t+j -> channel 4t+j, 2t+8+j -> 4t+2+j
+            const int64_t e0 =
+                (int64_t)(u.c0 + qi) * a.q_stride + (int64_t)(u.kh * g + hl) * D + kk * 16 + (lane & 3) * 4;
             qf[kk][0] = MMA::pack(load_act(a.q, e0, a.act_dtype), load_act(a.q, e0 + 1, a.act_dtype));
-            qf[kk][1] = MMA::pack(load_act(a.q, e0 + 8, a.act_dtype), load_act(a.q, e0 + 9, a.act_dtype));
+            qf[kk][1] = MMA::pack(load_act(a.q, e0 + 2, a.act_dtype), load_act(a.q, e0 + 3, a.act_dtype));
           } else {
             qf[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + kq);
             qf[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + kq);
@@ -349,30 +350,6 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
       uint32_t vbase = kbase + L::kTileBytes;
       float k_sc = 1.f, v_sc = 1.f;
       if constexpr (FP8) {
-        // fp8 tile -> fp16 tile in the 16-bit swizzled layout the fragment loads expect
-        const uint8_t* kst = wbase + s * L::kStageBytes;
-        const uint8_t* vst = kst + L::kTileBytes;
-        constexpr int FC = D / 16;  // 16-byte fp8 chunks per row
-        for (int idx = lane; idx < kTile * FC; idx += 32) {
-          const int row = idx / FC, c = idx % FC;
-          const uint32_t off = (uint32_t)((c >> 3) * L::kBoxBytes + row * 128 + (((c & 7) ^ (row & 7)) << 4));
-          uint4 lo, hi;
-          e4m3x16_to_f16(*reinterpret_cast<const uint4*>(kst + off), lo, hi);
-          *reinterpret_cast<uint4*>(wide + swz(row, 2 * c)) = lo;
-          *reinterpret_cast<uint4*>(wide + swz(row, 2 * c + 1)) = hi;
-          // V rows past the sequence (or of an invalid block) become zeros: P is 0 there, and
-          // 0 x NaN from whatever an unused slot holds would still poison O
-          if (blk_ok && pos0 + row < u.total) {
-            e4m3x16_to_f16(*reinterpret_cast<const uint4*>(vst + off), lo, hi);
-          } else {
-            lo = hi = make_uint4(0u, 0u, 0u, 0u);
-          }
-          *reinterpret_cast<uint4*>(wide + L::kWideBytes + swz(row, 2 * c)) = lo;
-          *reinterpret_cast<uint4*>(wide + L::kWideBytes + swz(row, 2 * c + 1)) = hi;
-        }
-        __syncwarp();
-        kbase = smem_u32(wide);
-        vbase = kbase + L::kWideBytes;
         if (blk_ok) {
           k_sc = a.k_scale[(int64_t)blk * KV + u.kh];
           v_sc = a.v_scale[(int64_t)blk * KV + u.kh];
@@ -413,8 +390,22 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; kk += 2) {
           uint32_t af[4], bf[4];
-          ldsm_x4(kbase + swz(row, kk * 2 + half), af[0], af[1], af[2], af[3]);
-          ldsm_x4(kbase + swz(row, kk * 2 + 2 + half), bf[0], bf[1], bf[2], bf[3]);
+          if constexpr (FP8) {
+            // 16-byte chunks kk, kk+1 = channel blocks of k-steps kk, kk+1
+            uint32_t d0, d1, d2, d3;
+            ldsm_x4(kbase + swz(row, kk + half), d0, d1, d2, d3);
+            af[0] = e4m3x2_to_f16x2(d0 & 0xffffu);
+            af[1] = e4m3x2_to_f16x2(d1 & 0xffffu);
+            af[2] = e4m3x2_to_f16x2(d0 >> 16);
+            af[3] = e4m3x2_to_f16x2(d1 >> 16);
+            bf[0] = e4m3x2_to_f16x2(d2 & 0xffffu);
+            bf[1] = e4m3x2_to_f16x2(d3 & 0xffffu);
+            bf[2] = e4m3x2_to_f16x2(d2 >> 16);
+            bf[3] = e4m3x2_to_f16x2(d3 >> 16);
+          } else {
+            ldsm_x4(kbase + swz(row, kk * 2 + half), af[0], af[1], af[2], af[3]);
+            ldsm_x4(kbase + swz(row, kk * 2 + 2 + half), bf[0], bf[1], bf[2], bf[3]);
+          }
           MMA::run(c, af, qf[kk][0], qf[kk][1]);
           MMA::run(c2, bf, qf[kk + 1][0], qf[kk + 1][1]);
         }
@@ -470,12 +461,39 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
         const int jm = lane >> 3;
         const int row = (lane & 7) + (jm >> 1) * 8;
         const int sub = jm & 1;
+        if constexpr (FP8) {
+          // tokens 2t, 2t+1 (and +8) of this lane; tokens past the sequence (or of an invalid
+          // block) read as zeros: P is 0 there, and 0 x NaN from an unused slot would poison O
+          const int t2 = (lane & 3) * 2;
+          const uint32_t mlo = (blk_ok && pos0 + t2 < u.total ? 0x0000ffffu : 0u) |
+                               (blk_ok && pos0 + t2 + 1 < u.total ? 0xffff0000u : 0u);
+          const uint32_t mhi = (blk_ok && pos0 + t2 + 8 < u.total ? 0x0000ffffu : 0u) |
+                               (blk_ok && pos0 + t2 + 9 < u.total ? 0xffff0000u : 0u);
 #pragma unroll
-        for (int mt = 0; mt < KSTEPS; ++mt) {
-          uint32_t af[4];
-          ldsm_x4_t(vbase + swz(row, mt * 2 + sub), af[0], af[1], af[2], af[3]);
-          MMA::run(o[mt], af, bh0, bh1);
-          MMA::run(o[mt], af, bl0, bl1);
+          for (int mt = 0; mt < KSTEPS; mt += 2) {
+            uint32_t d[4];
+            ldsm_x4_t(vbase + swz(row, mt + sub), d[0], d[1], d[2], d[3]);
+#pragma unroll
+            for (int blk2 = 0; blk2 < 2; ++blk2) {  // channel blocks mt, mt+1
+              const uint32_t lo_x = e4m3x2_to_f16x2(d[blk2] & 0xffffu), lo_y = e4m3x2_to_f16x2(d[blk2] >> 16);
+              const uint32_t hi_x = e4m3x2_to_f16x2(d[blk2 + 2] & 0xffffu), hi_y = e4m3x2_to_f16x2(d[blk2 + 2] >> 16);
+              uint32_t af[4];
+              af[0] = __byte_perm(lo_x, lo_y, 0x5410) & mlo;  // channel 2g, tokens 2t, 2t+1
+              af[1] = __byte_perm(lo_x, lo_y, 0x7632) & mlo;  // channel 2g+1
+              af[2] = __byte_perm(hi_x, hi_y, 0x5410) & mhi;  // channel 2g, tokens 2t+8, 2t+9
+              af[3] = __byte_perm(hi_x, hi_y, 0x7632) & mhi;
+              MMA::run(o[mt + blk2], af, bh0, bh1);
+              MMA::run(o[mt + blk2], af, bl0, bl1);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int mt = 0; mt < KSTEPS; ++mt) {
+            uint32_t af[4];
+            ldsm_x4_t(vbase + swz(row, mt * 2 + sub), af[0], af[1], af[2], af[3]);
+            MMA::run(o[mt], af, bh0, bh1);
+            MMA::run(o[mt], af, bl0, bl1);
+          }
         }
       }
       __syncwarp();
@@ -511,8 +529,8 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
         T* orow = reinterpret_cast<T*>(a.out) + (int64_t)(u.c0 + qi) * H * D + (int64_t)(u.kh * g + hl) * D;
 #pragma unroll
         for (int mt = 0; mt < KSTEPS; ++mt) {
-          store_act(orow, mt * 16 + dr, o[mt][e] * inv, a.act_dtype);
-          store_act(orow, mt * 16 + dr + 8, o[mt][e + 2] * inv, a.act_dtype);
+          store_act(orow, out_channel(FP8, mt, dr, 0), o[mt][e] * inv, a.act_dtype);
+          store_act(orow, out_channel(FP8, mt, dr, 1), o[mt][e + 2] * inv, a.act_dtype);
         }
       }
     } else {
@@ -531,8 +549,8 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
         }
 #pragma unroll
         for (int mt = 0; mt < KSTEPS; ++mt) {
-          po[mt * 16 + dr] = o[mt][e];
-          po[mt * 16 + dr + 8] = o[mt][e + 2];
+          po[out_channel(FP8, mt, dr, 0)] = o[mt][e];
+          po[out_channel(FP8, mt, dr, 1)] = o[mt][e + 2];
         }
       }
       __threadfence();
@@ -604,7 +622,7 @@ template <typename T, int D, int STAGES, bool FP8 = false>
 static cudaError_t launch_decode_t(const AttnArgs& a, const DecodePlan& plan, const DecodeMaps& maps, int num_sms,
                                    cudaStream_t stream) {
   using L = DecodeLayout<D, FP8>;
-  constexpr size_t smem = (size_t)kDecodeWarps * (STAGES * L::kStageBytes + (FP8 ? 2 * L::kWideBytes : 0)) + 1024;
+  constexpr size_t smem = (size_t)kDecodeWarps * STAGES * L::kStageBytes + 1024;
   static int occupancy[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
