@@ -132,12 +132,12 @@ struct DecodeLayout {
   static constexpr int kStageBytes = 2 * kTileBytes;     // K + V
 };
 
-// Two fp8 e4m3 values (low, high byte of `pair`) -> fp16x2, exact (every e4m3 value is an
-// fp16 value); the low byte lands in the low half.
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair) {
-  uint32_t r;
-  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(r) : "r"(pair));
-  return r;
+// Four fp8 e4m3 values of `w` -> two fp16x2: lo = bytes 0, 1 and hi = bytes 2, 3 (exact: every
+// e4m3 value is an fp16 value; the lower byte of a pair lands in the lower half).
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
 }
 
 // fp8 tiles feed the fp16 MMAs straight from registers:
@@ -394,14 +394,10 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
             // 16-byte chunks kk, kk+1 = channel blocks of k-steps kk, kk+1
             uint32_t d0, d1, d2, d3;
             ldsm_x4(kbase + swz(row, kk + half), d0, d1, d2, d3);
-            af[0] = e4m3x2_to_f16x2(d0 & 0xffffu);
-            af[1] = e4m3x2_to_f16x2(d1 & 0xffffu);
-            af[2] = e4m3x2_to_f16x2(d0 >> 16);
-            af[3] = e4m3x2_to_f16x2(d1 >> 16);
-            bf[0] = e4m3x2_to_f16x2(d2 & 0xffffu);
-            bf[1] = e4m3x2_to_f16x2(d3 & 0xffffu);
-            bf[2] = e4m3x2_to_f16x2(d2 >> 16);
-            bf[3] = e4m3x2_to_f16x2(d3 >> 16);
+            e4m3x4_to_f16x2x2(d0, af[0], af[2]);
+            e4m3x4_to_f16x2x2(d1, af[1], af[3]);
+            e4m3x4_to_f16x2x2(d2, bf[0], bf[2]);
+            e4m3x4_to_f16x2x2(d3, bf[1], bf[3]);
           } else {
             ldsm_x4(kbase + swz(row, kk * 2 + half), af[0], af[1], af[2], af[3]);
             ldsm_x4(kbase + swz(row, kk * 2 + 2 + half), bf[0], bf[1], bf[2], bf[3]);
@@ -464,6 +460,7 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
         if constexpr (FP8) {
           // tokens 2t, 2t+1 (and +8) of this lane; tokens past the sequence (or of an invalid
           // block) read as zeros: P is 0 there, and 0 x NaN from an unused slot would poison O
+          // byte masks on the fp8 register [t0 c0, t0 c1, t1 c0, t1 c1] (tokens 2t, 2t+1)
           const int t2 = (lane & 3) * 2;
           const uint32_t mlo = (blk_ok && pos0 + t2 < u.total ? 0x0000ffffu : 0u) |
                                (blk_ok && pos0 + t2 + 1 < u.total ? 0xffff0000u : 0u);
@@ -475,13 +472,10 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
             ldsm_x4_t(vbase + swz(row, mt + sub), d[0], d[1], d[2], d[3]);
 #pragma unroll
             for (int blk2 = 0; blk2 < 2; ++blk2) {  // channel blocks mt, mt+1
-              const uint32_t lo_x = e4m3x2_to_f16x2(d[blk2] & 0xffffu), lo_y = e4m3x2_to_f16x2(d[blk2] >> 16);
-              const uint32_t hi_x = e4m3x2_to_f16x2(d[blk2 + 2] & 0xffffu), hi_y = e4m3x2_to_f16x2(d[blk2 + 2] >> 16);
+              // regroup the fp8 bytes per channel first: [t0 c0, t1 c0, t0 c1, t1 c1]
               uint32_t af[4];
-              af[0] = __byte_perm(lo_x, lo_y, 0x5410) & mlo;  // channel 2g, tokens 2t, 2t+1
-              af[1] = __byte_perm(lo_x, lo_y, 0x7632) & mlo;  // channel 2g+1
-              af[2] = __byte_perm(hi_x, hi_y, 0x5410) & mhi;  // channel 2g, tokens 2t+8, 2t+9
-              af[3] = __byte_perm(hi_x, hi_y, 0x7632) & mhi;
+              e4m3x4_to_f16x2x2(__byte_perm(d[blk2] & mlo, 0u, 0x3120), af[0], af[1]);
+              e4m3x4_to_f16x2x2(__byte_perm(d[blk2 + 2] & mhi, 0u, 0x3120), af[2], af[3]);
               MMA::run(o[mt + blk2], af, bh0, bh1);
               MMA::run(o[mt + blk2], af, bl0, bl1);
             }
