@@ -61,6 +61,7 @@ def parse():
                          "gqa = config 1 (GroupQueryAttention decode, contiguous fp32 cache); "
                          "fp8 = config 5 (fp8 e4m3 KV decode, 256 seqs, 64q/8kv sharded over the GPUs)")
     ap.add_argument("--append-tokens", type=int, default=256, help="append workload: new tokens per call")
+    ap.add_argument("--fp8-seqs", type=int, default=256, help="fp8 workload: sequences (profiling runs use fewer)")
     return ap.parse_args()
 
 
@@ -706,12 +707,12 @@ def run_fp8(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     from onnxruntime_ep_b200 import _capi, paged, sharding
 
-    H5, KV5, B5, bs = 64, 8, 256, 16
+    H5, KV5, B5, bs = 64, 8, args.fp8_seqs, 16
     if KV5 % n:
         raise SystemExit(f"--gpus {n} must divide the 8 kv heads")
     kvh, qh = KV5 // n, H5 // n
     rng = np.random.default_rng(5)
-    L = rng.integers(4096, 32768, size=B5, endpoint=True)
+    L = rng.integers(4096, 32768, size=256, endpoint=True)[:B5]
     need = -(-L // bs)
     NB = int(need.sum())
     perm = rng.permutation(NB).astype(np.int32)
