@@ -330,9 +330,45 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
 #pragma unroll
     for (int mt = 0; mt < KSTEPS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
 
+    // Tile metadata in windows of 32 tiles: lane i holds tile wb + i's physical block (and, for
+    // fp8 caches, its K and V scales).  The next window's block entries are loaded when a
+    // window starts and its scales 8 tiles later, so no tile waits on a dependent global load.
+    auto tile_block = [&](int t) -> int32_t {
+      return t < u.t1 ? __ldg(a.block_table + (int64_t)u.b * a.max_blocks + (t * kTile) / a.block_size) : -1;
+    };
+    auto block_scale = [&](const float* sc, int32_t blk) -> float {
+      return blk >= 0 && blk < a.num_blocks ? __ldg(sc + (int64_t)blk * KV + u.kh) : 1.f;
+    };
+    int wb = ct;
+    int32_t w_blk = tile_block(wb + lane), n_blk = -1;
+    float w_ks = 1.f, w_vs = 1.f, n_ks = 1.f, n_vs = 1.f;
+    if constexpr (FP8) {
+      w_ks = block_scale(a.k_scale, w_blk);
+      w_vs = block_scale(a.v_scale, w_blk);
+    }
+    // A tile needs no per-position mask when it lies inside the sequence, before every query's
+    // causal limit and after every query's window start.
+    const int full_end = a.is_causal ? min(u.total, u.past + 1) : u.total;
+    const int full_begin = a.window > 0 ? u.past + u.nq - a.window : 0;
+
     for (; ct < u.t1; ++ct) {
       const int s = consumed % STAGES;
       const int pos0 = ct * kTile;
+      int wi = ct - wb;
+      if (wi == 32) {
+        wb = ct;
+        wi = 0;
+        w_blk = n_blk;
+        w_ks = n_ks;
+        w_vs = n_vs;
+      }
+      if (wi == 0) n_blk = tile_block(wb + 32 + lane);
+      if constexpr (FP8) {
+        if (wi == 8) {
+          n_ks = block_scale(a.k_scale, n_blk);
+          n_vs = block_scale(a.v_scale, n_blk);
+        }
+      }
       if (!mbar_wait(&bars[warp][s], (phase >> s) & 1u)) {
         if (lane == 0) set_status(a.status, kStatusTimeout);
         failed = true;
@@ -344,16 +380,15 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
       }
       phase ^= 1u << s;
       pending &= ~(1u << s);
-      const int32_t blk = a.block_table[(int64_t)u.b * a.max_blocks + pos0 / a.block_size];
+      const int32_t blk = __shfl_sync(0xffffffffu, w_blk, wi);
       const bool blk_ok = blk >= 0 && blk < a.num_blocks;
+      const bool full = blk_ok && pos0 >= full_begin && pos0 + kTile <= full_end;
       uint32_t kbase = wbase_u32 + s * L::kStageBytes;
       uint32_t vbase = kbase + L::kTileBytes;
       float k_sc = 1.f, v_sc = 1.f;
       if constexpr (FP8) {
-        if (blk_ok) {
-          k_sc = a.k_scale[(int64_t)blk * KV + u.kh];
-          v_sc = a.v_scale[(int64_t)blk * KV + u.kh];
-        }
+        k_sc = __shfl_sync(0xffffffffu, w_ks, wi);
+        v_sc = __shfl_sync(0xffffffffu, w_vs, wi);
       }
 
       // Overlay: tile rows at positions >= past hold the sequence's own new K/V rows (16-bit
@@ -411,16 +446,20 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
 
       // Masks, scale (log2 domain), online softmax per q-row column.
       float sc[4];
+      const float ksq = k_sc * qk_scale;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int tok = (lane >> 2) + ((e >> 1) << 3);
         const int col = col0 + (e & 1);
         const int qi = (e & 1) ? qi1 : qi0;
         const int pos = pos0 + tok;
-        bool vis = blk_ok && col < rows && pos < u.total;
-        if (a.is_causal) vis = vis && pos <= u.past + qi;
-        if (a.window > 0) vis = vis && pos >= u.past + qi - a.window + 1;
-        float x = c[e] * k_sc * qk_scale;
+        bool vis = col < rows;
+        if (!full) {
+          vis = vis && blk_ok && pos < u.total;
+          if (a.is_causal) vis = vis && pos <= u.past + qi;
+          if (a.window > 0) vis = vis && pos >= u.past + qi - a.window + 1;
+        }
+        float x = c[e] * ksq;
         if (a.softcap > 0.f) x = a.softcap * tanhf(x / a.softcap) * kLog2e;
         sc[e] = vis ? x : -INFINITY;
       }
@@ -461,21 +500,25 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
           // tokens 2t, 2t+1 (and +8) of this lane; tokens past the sequence (or of an invalid
           // block) read as zeros: P is 0 there, and 0 x NaN from an unused slot would poison O
           // byte masks on the fp8 register [t0 c0, t0 c1, t1 c0, t1 c1] (tokens 2t, 2t+1)
+          // The byte permute [t0 c0, t0 c1, t1 c0, t1 c1] -> [t0 c0, t1 c0, t0 c1, t1 c1] (selector
+          // 0x3120) regroups the bytes per channel; a masked token's bytes select the zero operand
+          // (selector nibble 4) instead.
           const int t2 = (lane & 3) * 2;
-          const uint32_t mlo = (blk_ok && pos0 + t2 < u.total ? 0x0000ffffu : 0u) |
-                               (blk_ok && pos0 + t2 + 1 < u.total ? 0xffff0000u : 0u);
-          const uint32_t mhi = (blk_ok && pos0 + t2 + 8 < u.total ? 0x0000ffffu : 0u) |
-                               (blk_ok && pos0 + t2 + 9 < u.total ? 0xffff0000u : 0u);
+          auto perm_sel = [&](int p) -> uint32_t {
+            const bool ok0 = full || (blk_ok && pos0 + p < u.total);
+            const bool ok1 = full || (blk_ok && pos0 + p + 1 < u.total);
+            return (ok0 ? 0x0100u : 0x0404u) | (ok1 ? 0x3020u : 0x4040u);
+          };
+          const uint32_t sel_lo = perm_sel(t2), sel_hi = perm_sel(t2 + 8);
 #pragma unroll
           for (int mt = 0; mt < KSTEPS; mt += 2) {
             uint32_t d[4];
             ldsm_x4_t(vbase + swz(row, mt + sub), d[0], d[1], d[2], d[3]);
 #pragma unroll
             for (int blk2 = 0; blk2 < 2; ++blk2) {  // channel blocks mt, mt+1
-              // regroup the fp8 bytes per channel first: [t0 c0, t1 c0, t0 c1, t1 c1]
               uint32_t af[4];
-              e4m3x4_to_f16x2x2(__byte_perm(d[blk2] & mlo, 0u, 0x3120), af[0], af[1]);
-              e4m3x4_to_f16x2x2(__byte_perm(d[blk2 + 2] & mhi, 0u, 0x3120), af[2], af[3]);
+              e4m3x4_to_f16x2x2(__byte_perm(d[blk2], 0u, sel_lo), af[0], af[1]);
+              e4m3x4_to_f16x2x2(__byte_perm(d[blk2 + 2], 0u, sel_hi), af[2], af[3]);
               MMA::run(o[mt + blk2], af, bh0, bh1);
               MMA::run(o[mt + blk2], af, bl0, bl1);
             }
