@@ -687,7 +687,7 @@ cudaError_t launch_decode(const AttnArgs& a, const DecodePlan& plan, const Decod
   const bool bf = a.act_dtype == B200_DTYPE_BFLOAT16;
   if (a.cache_dtype == B200_DTYPE_FLOAT8E4M3FN) {
     switch (a.head_size) {
-      case 128: return launch_decode_t<__half, 128, 4, true>(a, plan, maps, num_sms, stream);
+      case 128: return launch_decode_t<__half, 128, 3, true>(a, plan, maps, num_sms, stream);
       case 256: return launch_decode_t<__half, 256, 2, true>(a, plan, maps, num_sms, stream);
       default: return cudaErrorInvalidValue;
     }
