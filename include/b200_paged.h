@@ -261,6 +261,11 @@ B200_API int b200_group_query_attention_workspace_size(const B200GqaParams* p, s
 /* Validate (reference messages, attention.rs:989-1030, :613-630, :663-667), then append and
  * attend.  B200_ERR_FAIL for invalid lengths, B200_ERR_UNSUPPORTED for unclaimed forms. */
 B200_API int b200_group_query_attention(const B200GqaParams* p, void* stream);
+/* Synchronise `stream` and report the device status word of the last call that used this
+ * workspace: B200_ERR_DEVICE when a bounded device wait ran out.  The reference runs the node
+ * on the host and has no device status; this plays the role of its error return for the
+ * device side (lib.rs:53-92 turns failures into an OrtStatus). */
+B200_API int b200_group_query_attention_read_status(const B200GqaParams* p, void* stream);
 
 /* Claim predicate, restating group_query_attention_claim (attention.rs:2407-2754) over a
  * plain node description, plus this build's own declines (rotary, attention_bias,

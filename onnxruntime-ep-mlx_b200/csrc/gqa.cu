@@ -20,6 +20,10 @@
 //    one read and one write of the cache.  Otherwise a copy kernel builds `present`.
 #include <atomic>
 #include <cmath>
+#include <cooperative_groups.h>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <type_traits>
 #include <cstring>
 #include <string>
@@ -57,6 +61,7 @@ struct GqaArgs {
   float* part_o;   // [groups][splits][R][D]
   float* part_ml;  // [groups][splits][R][2]
   int* counters;   // [groups]
+  int* status;     // kStatus* bits (a bounded wait ran out); cleared by CTA 0 of every call
 };
 
 template <typename T> __device__ __forceinline__ float to_f(T x);
@@ -157,6 +162,7 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
   const BatchGeom bg = batch_geom(a, b);
   const int D = a.D, g = a.g;
   const int rows_total = a.S * g;
+  if (blockIdx.x == 0 && tid == 0) *a.status = 0;
 
   // Query rows of this tile (fp32, pre-scaled into the log2 domain unless softcap is on).
   const float qmul = a.softcap > 0.f ? 1.f : a.scale * kLog2e;
@@ -441,6 +447,299 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
   }
 }
 
+// Decode-shaped groups (one row tile covers every key, no window): a thread-block cluster per
+// (batch, kv head).  Each CTA of the cluster owns a contiguous key range, stages its K and V
+// rows in shared memory with one 1-D bulk copy each (the past rows of a BNSH head are
+// contiguous; K and V on separate barriers, so the scores start while V is still arriving),
+// writes the fused present rows from there, and keeps an fp32 partial (m, l, o).  The partials are merged through
+// distributed shared memory: each CTA finishes a slice of the channels.  No workspace, no
+// counters, one launch.
+constexpr int kClThreads = 256;
+constexpr int kClMaxCluster = 16;
+
+// Dynamic shared memory of one CTA: K staging [kc][D] T (reused, after the last chunk, for the
+// key-group reduction of P.V [1024/D][R][D] fp32), V staging [kc][D] T, probabilities [R][kc]
+// and the CTA partial o [R][D] (fp32).
+__host__ __device__ inline size_t cluster_kbuf_bytes(int R, int D, int esz, int kc) {
+  const size_t k = (size_t)kc * D * esz, r = (size_t)1024 * R * 4;
+  return k > r ? k : r;
+}
+__host__ __device__ inline size_t cluster_smem_bytes(int R, int D, int esz, int kc) {
+  return cluster_kbuf_bytes(R, D, esz, kc) + (size_t)kc * D * esz + (size_t)R * kc * 4 + (size_t)R * D * 4;
+}
+
+template <typename T, int R, int D>
+__global__ void __launch_bounds__(kClThreads) gqa_cluster_kernel(const GqaArgs a, int kc) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int CL = (int)cluster.num_blocks();
+  const int cr = (int)cluster.block_rank();
+  extern __shared__ __align__(16) uint8_t cl_smem[];
+  __shared__ float m_run[R], l_run[R], alpha_s[R];
+  __shared__ int row_pos[R], row_end[R];
+  __shared__ __align__(8) uint64_t bar_k, bar_v;
+
+  // Scores: LPK lanes per key, each holding the q values of UPL 4-channel units (units
+  // j, j + LPK, ...: one 128-byte bank row per key and instruction) for all R rows.
+  constexpr int kUnits = D / 4;
+  constexpr int LPK = (R * D / 64) < 4 ? 4 : (R * D / 64) > 32 ? 32 : (R * D / 64);
+  constexpr int UPL = kUnits / LPK;
+  constexpr int KPP = kClThreads / LPK;  // keys per pass
+  // P.V: thread = (4-channel unit, key group)
+  constexpr int KG = kClThreads / kUnits;
+
+  const int g = a.g, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = blockIdx.x / CL;  // (b, kh)
+  const int kh = grp % a.KV, b = grp / a.KV;
+  const BatchGeom bg = batch_geom(a, b);
+  const int rows_total = a.S * g;
+
+  T* kbuf = reinterpret_cast<T*>(cl_smem);
+  T* vbuf = reinterpret_cast<T*>(cl_smem + cluster_kbuf_bytes(R, D, (int)sizeof(T), kc));
+  float* sc = reinterpret_cast<float*>(vbuf + (size_t)kc * D);
+  float* opart = sc + R * kc;
+  float* red = reinterpret_cast<float*>(cl_smem);  // after the last chunk: K is no longer read
+
+  if (tid < R) {
+    if (tid < rows_total) {
+      const int pos = bg.query_past + tid / g;
+      row_pos[tid] = pos;
+      row_end[tid] = a.causal ? min(pos + 1, bg.length) : bg.length;
+    } else {
+      row_pos[tid] = -1;
+      row_end[tid] = 0;
+    }
+    m_run[tid] = -INFINITY;
+    l_run[tid] = 0.f;
+  }
+  if (tid == 0) {
+    if (blockIdx.x == 0) *a.status = 0;
+    mbar_init(&bar_k, 1);
+    mbar_init(&bar_v, 1);
+    fence_mbar_init();
+  }
+  uint32_t phase = 0;
+  bool failed = false;  // a staging wait ran out: skip the math, still meet the cluster barriers
+  // This lane's q units (fp32, scaled into the log2 domain unless softcap is on).
+  const int sj = tid % LPK;
+  float qr[R][UPL][4];
+  {
+    const float qmul = a.softcap > 0.f ? 1.f : a.scale * kLog2e;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const bool live = r < rows_total;
+      const T* qrow = static_cast<const T*>(a.q) +
+                      ((int64_t)b * a.S + (live ? r / g : 0)) * a.q_stride + (int64_t)(kh * g + (live ? r % g : 0)) * D;
+#pragma unroll
+      for (int i = 0; i < UPL; ++i) {
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        if (live) unpack_raw<T>(ld4(qrow + (sj + LPK * i) * 4), x);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) qr[r][i][e] = x[e] * qmul;
+      }
+    }
+  }
+
+  const int k0 = (int)((int64_t)bg.length * cr / CL), k1 = (int)((int64_t)bg.length * (cr + 1) / CL);
+  const int cq = tid % kUnits, kgrp = tid / kUnits;
+  float o[R][4];
+#pragma unroll
+  for (int r = 0; r < R; ++r) o[r][0] = o[r][1] = o[r][2] = o[r][3] = 0.f;
+  __syncthreads();
+
+  for (int c0 = k0; c0 < k1 && !failed; c0 += kc) {
+    const int nk = min(kc, k1 - c0);
+    const int np = max(0, min(nk, bg.past - c0));  // rows from the past cache
+    // ---- stage: the past rows of K and of V (contiguous in the BNSH head) by one bulk copy
+    // each, on separate barriers so the scores start while V is in flight; new rows by plain
+    // loads
+    const uint32_t pbytes = (uint32_t)np * D * sizeof(T);
+    if (np > 0 && tid == 0) {
+      const T* kpast = static_cast<const T*>(a.pk) + (((int64_t)b * a.KV + kh) * a.cap + c0) * D;
+      const T* vpast = static_cast<const T*>(a.pv) + (((int64_t)b * a.KV + kh) * a.cap + c0) * D;
+      fence_proxy_async_smem();  // the previous chunk's generic reads and writes come first
+      mbar_arrive_expect_tx(&bar_k, pbytes);
+      bulk_load(kbuf, kpast, pbytes, &bar_k);
+      mbar_arrive_expect_tx(&bar_v, pbytes);
+      bulk_load(vbuf, vpast, pbytes, &bar_v);
+    }
+    for (int i = tid; i < (nk - np) * kUnits; i += kClThreads) {
+      const int k = np + i / kUnits, d = (i % kUnits) * 4;
+      st4(kbuf + (size_t)k * D + d, ld4(key_row<T>(a, bg, b, kh, c0 + k, false) + d));
+      st4(vbuf + (size_t)k * D + d, ld4(key_row<T>(a, bg, b, kh, c0 + k, true) + d));
+    }
+    if (np > 0 && !mbar_wait(&bar_k, phase)) failed = true;
+    if (__syncthreads_or(failed)) {
+      // one more bounded wait on each copy still in flight, then no further work
+      if (tid == 0) {
+        set_status(a.status, kStatusTimeout);
+        mbar_wait(&bar_k, phase);
+        mbar_wait(&bar_v, phase);
+      }
+      failed = true;
+      break;
+    }
+
+    // ---- fused present rows of K (all rows when present is its own buffer, else the new ones)
+    if (a.fused_copy) {
+      const int first = a.present_separate ? 0 : np;
+      for (int i = tid; i < (nk - first) * kUnits; i += kClThreads) {
+        const int k = first + i / kUnits, d = (i % kUnits) * 4;
+        st4(present_row<T>(a, b, kh, c0 + k, false) + d, *reinterpret_cast<const typename Vec4<T>::raw*>(kbuf + (size_t)k * D + d));
+      }
+    }
+
+    // ---- scores
+    for (int kb = 0; kb < nk; kb += KPP) {
+      const int k = kb + tid / LPK;
+      float acc[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r] = 0.f;
+      if (k < nk) {
+        const T* krow = kbuf + (size_t)k * D;
+#pragma unroll
+        for (int i = 0; i < UPL; ++i) {
+          float kx[4];
+          unpack_raw<T>(*reinterpret_cast<const typename Vec4<T>::raw*>(krow + (sj + LPK * i) * 4), kx);
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+            acc[r] = fmaf(qr[r][i][0], kx[0], fmaf(qr[r][i][1], kx[1], fmaf(qr[r][i][2], kx[2], fmaf(qr[r][i][3], kx[3], acc[r]))));
+        }
+      }
+#pragma unroll
+      for (int off = 1; off < LPK; off <<= 1)
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+      if (k < nk && sj == 0) {
+        const int pos = c0 + k;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float s = -INFINITY;
+          if (row_pos[r] >= 0 && pos < row_end[r]) {
+            s = acc[r];
+            if (a.softcap > 0.f) s = a.softcap * tanhf(s * a.scale / a.softcap) * kLog2e;
+          }
+          sc[r * kc + k] = s;
+        }
+      }
+    }
+    __syncthreads();
+
+    // ---- online softmax over the chunk: a warp per row
+    for (int r = warp; r < R; r += kClThreads / 32) {
+      float mx = -INFINITY;
+      for (int k = lane; k < nk; k += 32) mx = fmaxf(mx, sc[r * kc + k]);
+      for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_old = m_run[r], m_new = fmaxf(m_old, mx);
+      const float mu = m_new == -INFINITY ? 0.f : m_new;
+      float sum = 0.f;
+      for (int k = lane; k < nk; k += 32) {
+        const float p = exp2f(sc[r * kc + k] - mu);
+        sc[r * kc + k] = p;
+        sum += p;
+      }
+      for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      if (lane == 0) {
+        const float al = m_old == -INFINITY ? 0.f : exp2f(m_old - mu);
+        alpha_s[r] = al;
+        l_run[r] = l_run[r] * al + sum;
+        m_run[r] = m_new;
+      }
+    }
+    if (np > 0 && !mbar_wait(&bar_v, phase)) failed = true;
+    if (np > 0) phase ^= 1u;
+    if (__syncthreads_or(failed)) {
+      if (tid == 0) {
+        set_status(a.status, kStatusTimeout);
+        mbar_wait(&bar_v, phase ^ 1u);
+      }
+      failed = true;
+      break;
+    }
+
+    // ---- fused present rows of V
+    if (a.fused_copy) {
+      const int first = a.present_separate ? 0 : np;
+      for (int i = tid; i < (nk - first) * kUnits; i += kClThreads) {
+        const int k = first + i / kUnits, d = (i % kUnits) * 4;
+        st4(present_row<T>(a, b, kh, c0 + k, true) + d, *reinterpret_cast<const typename Vec4<T>::raw*>(vbuf + (size_t)k * D + d));
+      }
+    }
+
+    // ---- P.V: thread = (4-channel unit cq, key group kgrp)
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float al = alpha_s[r];
+      o[r][0] *= al; o[r][1] *= al; o[r][2] *= al; o[r][3] *= al;
+    }
+    for (int k = kgrp; k < nk; k += KG) {
+      float vx[4];
+      unpack_raw<T>(*reinterpret_cast<const typename Vec4<T>::raw*>(vbuf + (size_t)k * D + cq * 4), vx);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float p = sc[r * kc + k];
+        o[r][0] = fmaf(p, vx[0], o[r][0]);
+        o[r][1] = fmaf(p, vx[1], o[r][1]);
+        o[r][2] = fmaf(p, vx[2], o[r][2]);
+        o[r][3] = fmaf(p, vx[3], o[r][3]);
+      }
+    }
+    __syncthreads();  // the next chunk overwrites the staging buffers and the probabilities
+  }
+
+  // ---- CTA partial: sum the key groups
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    *reinterpret_cast<float4*>(red + (kgrp * R + r) * D + cq * 4) = make_float4(o[r][0], o[r][1], o[r][2], o[r][3]);
+  __syncthreads();
+  for (int i = tid; i < R * D; i += kClThreads) {
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < KG; ++q) s += red[q * R * D + i];
+    opart[i] = s;
+  }
+  cluster.sync();  // every partial of the cluster is complete and visible
+
+  // ---- merge: this CTA finishes channels [d_lo, d_hi) of every row from all CTAs' partials
+  const int per = (D + CL - 1) / CL, d_lo = min(D, cr * per), d_hi = min(D, d_lo + per);
+  for (int i = tid; i < R * (d_hi - d_lo); i += kClThreads) {
+    const int r = i / (d_hi - d_lo), d = d_lo + i % (d_hi - d_lo);
+    if (row_pos[r] < 0) continue;
+    float mj[kClMaxCluster], lj[kClMaxCluster], oj[kClMaxCluster];
+#pragma unroll
+    for (int j = 0; j < kClMaxCluster; ++j) {
+      if (j < CL) {
+        mj[j] = *cluster.map_shared_rank(&m_run[r], j);
+        lj[j] = *cluster.map_shared_rank(&l_run[r], j);
+        oj[j] = *cluster.map_shared_rank(&opart[r * D + d], j);
+      } else {
+        mj[j] = -INFINITY;
+        lj[j] = oj[j] = 0.f;
+      }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kClMaxCluster; ++j) M = fmaxf(M, mj[j]);
+    const float mu = M == -INFINITY ? 0.f : M;
+    float L = 0.f, acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < kClMaxCluster; ++j) {
+      const float w = mj[j] == -INFINITY ? 0.f : exp2f(mj[j] - mu);
+      L += w * lj[j];
+      acc += w * oj[j];
+    }
+    if (a.sink != nullptr || a.smooth) {
+      const int hl = r % g;
+      const float sk = (a.sink ? to_f(static_cast<const T*>(a.sink)[kh * g + hl]) : 0.f) * kLog2e;
+      L += exp2f(sk - mu);
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const int s = r / g, hl = r % g;
+    static_cast<T*>(a.out)[((int64_t)b * a.S + s) * a.H * D + (int64_t)(kh * g + hl) * D + d] = from_f<T>(acc * inv);
+  }
+  cluster.sync();  // no CTA leaves while another still reads its shared memory
+}
+
 // present rows the attention kernel does not write: everything (copy mode) or the tail
 // [length, pcap) (fused mode); in shared-buffer mode only the new rows.  One thread per element.
 template <typename T>
@@ -485,7 +784,7 @@ int sm_count(const B200GqaParams* p) {
 
 struct GqaPlan {
   int rows = kMaxRows, row_tiles = 1, splits = 1, fused = 0;
-  size_t counters = 0, part_o = 0, part_ml = 0, total = 0;
+  size_t status = 0, counters = 0, part_o = 0, part_ml = 0, total = 0;
 };
 
 GqaPlan gqa_plan(const B200GqaParams* p) {
@@ -506,6 +805,7 @@ GqaPlan gqa_plan(const B200GqaParams* p) {
     off = (off + bytes + 255) / 256 * 256;
     return at;
   };
+  P.status = take(sizeof(int));
   if (P.splits > 1) {
     P.counters = take(sizeof(int) * groups);
     P.part_o = take(sizeof(float) * groups * P.splits * P.rows * p->head_size);
@@ -596,8 +896,133 @@ int validate_lengths(const B200GqaParams* p) {
   return B200_OK;
 }
 
+// Cluster path (decode-shaped groups: one row tile covers every key, no window).
+constexpr size_t kClSmemBudget = 220 * 1024;
+
+bool cluster_path(const B200GqaParams* p, const GqaPlan& P) {
+  const int D = p->head_size;
+  if (!P.fused || !(D == 64 || D == 128 || D == 256)) return false;
+  for (const void* ptr : {p->past_key, p->past_value})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16) return false;  // cp.async stages 16-byte chunks
+  return true;
+}
+
+// Active clusters per (kernel, cluster size, shared memory, device), queried once each.
+struct OccKey {
+  const void* kern;
+  int cl;
+  size_t smem;
+  int dev;
+  bool operator<(const OccKey& o) const { return std::tie(kern, cl, smem, dev) < std::tie(o.kern, o.cl, o.smem, o.dev); }
+};
+
+template <typename T, int R, int D>
+cudaError_t launch_cluster_rd(const GqaArgs& a, cudaStream_t stream) {
+  static std::mutex mu;
+  static std::map<OccKey, int> occ;
+  static std::map<std::pair<const void*, int>, bool> prepared;
+  auto kern = gqa_cluster_kernel<T, R, D>;
+  const void* kp = reinterpret_cast<const void*>(kern);
+  constexpr int esz = (int)sizeof(T);
+  int kc_max = 0;  // the most keys per staging chunk that fit the shared-memory budget
+  for (int kc = 16; kc <= 512; kc += 16)
+    if (cluster_smem_bytes(R, D, esz, kc) <= kClSmemBudget) kc_max = kc;
+  if (kc_max < 16) return cudaErrorInvalidValue;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kClThreads);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+
+  // Cluster size: fewest waves of clusters times keys per CTA (each staging chunk also costs a
+  // memory round trip, worth about 256 keys), from the device's own count of co-resident
+  // clusters.
+  const int64_t groups = (int64_t)a.B * a.KV;
+  const int maxlen = std::max(a.total, 1);
+  int best_cl = 0, best_kc = 0;
+  double best_cost = 0.0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!prepared[{kp, dev}]) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cluster_smem_bytes(R, D, esz, kc_max));
+      if (e != cudaSuccess) return e;
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return e;
+      prepared[{kp, dev}] = true;
+    }
+    for (int cl = kClMaxCluster; cl >= 1; --cl) {
+      const int per_cta = (maxlen + cl - 1) / cl;
+      const int kc = std::min(kc_max, (per_cta + 15) / 16 * 16);
+      const size_t smem = cluster_smem_bytes(R, D, esz, kc);
+      const OccKey key{kp, cl, smem, dev};
+      auto it = occ.find(key);
+      int active = 0;
+      if (it != occ.end()) {
+        active = it->second;
+      } else {
+        attr[0].val.clusterDim.x = cl;
+        cfg.gridDim = dim3((unsigned)cl);
+        cfg.dynamicSmemBytes = smem;
+        if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) != cudaSuccess) active = 0;
+        cudaGetLastError();  // a refused size is not an error of the call
+        occ[key] = active;
+      }
+      if (active <= 0) continue;
+      const int64_t waves = (groups + active - 1) / active;
+      const int chunks = (per_cta + kc - 1) / kc;
+      const double cost = (double)waves * (per_cta + 256.0 * chunks);
+      if (best_cl == 0 || cost < best_cost) {
+        best_cl = cl;
+        best_kc = kc;
+        best_cost = cost;
+      }
+    }
+  }
+  if (best_cl == 0) return cudaErrorLaunchOutOfResources;
+  attr[0].val.clusterDim.x = best_cl;
+  cfg.gridDim = dim3((unsigned)(groups * best_cl));
+  cfg.dynamicSmemBytes = cluster_smem_bytes(R, D, esz, best_kc);
+  return cudaLaunchKernelEx(&cfg, kern, a, best_kc);
+}
+
+template <typename T, int R>
+cudaError_t launch_cluster_r(const GqaArgs& a, cudaStream_t stream) {
+  if (a.D == 64) return launch_cluster_rd<T, R, 64>(a, stream);
+  if (a.D == 128) return launch_cluster_rd<T, R, 128>(a, stream);
+  return launch_cluster_rd<T, R, 256>(a, stream);
+}
+
 template <typename T>
-cudaError_t launch_gqa(const GqaArgs& a, const GqaPlan& P, bool tail_rows, cudaStream_t stream, int* launches) {
+cudaError_t launch_cluster(const GqaArgs& a, const GqaPlan& P, cudaStream_t stream) {
+  if (P.rows == 4) return launch_cluster_r<T, 4>(a, stream);
+  if (P.rows == 8) return launch_cluster_r<T, 8>(a, stream);
+  return launch_cluster_r<T, kMaxRows>(a, stream);
+}
+
+template <typename T>
+cudaError_t launch_gqa(const GqaArgs& a, const GqaPlan& P, bool cluster, bool tail_rows, cudaStream_t stream,
+                       int* launches) {
+  if (cluster) {
+    cudaError_t e = launch_cluster<T>(a, P, stream);
+    ++*launches;
+    if (e != cudaSuccess) return e;
+    if (a.ok != nullptr && a.present_separate && tail_rows) {
+      const int64_t n = (int64_t)a.B * a.KV * a.pcap * a.D;
+      const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
+      gqa_present_kernel<T><<<blocks, 256, 0, stream>>>(a, 1);
+      ++*launches;
+      e = cudaGetLastError();
+    }
+    return e;
+  }
   const int64_t grid = (int64_t)a.B * a.KV * a.row_tiles * a.splits;
   if (P.splits > 1) {
     cudaError_t e = cudaMemsetAsync(a.counters, 0, sizeof(int) * (size_t)a.B * a.KV * a.row_tiles, stream);
@@ -689,6 +1114,7 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
     a.fused_copy = P.fused && p->present_key != nullptr;
     a.present_separate = p->present_key != nullptr && p->present_key != p->past_key;
     char* ws = static_cast<char*>(p->workspace);
+    a.status = reinterpret_cast<int*>(ws + P.status);
     if (P.splits > 1) {
       a.counters = reinterpret_cast<int*>(ws + P.counters);
       a.part_o = reinterpret_cast<float*>(ws + P.part_o);
@@ -700,9 +1126,10 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
     // Rows past some batch's length exist in present only when a length is below its capacity.
     bool tail_rows = false;
     for (int b = 0; b < p->batch; ++b) tail_rows |= p->host_seqlens_k[b] + 1 < a.pcap;
-    if (a.dtype == B200_DTYPE_FLOAT) e = launch_gqa<float>(a, P, tail_rows, stream, &launches);
-    else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_gqa<__half>(a, P, tail_rows, stream, &launches);
-    else e = launch_gqa<__nv_bfloat16>(a, P, tail_rows, stream, &launches);
+    const bool cluster = cluster_path(p, P);
+    if (a.dtype == B200_DTYPE_FLOAT) e = launch_gqa<float>(a, P, cluster, tail_rows, stream, &launches);
+    else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_gqa<__half>(a, P, cluster, tail_rows, stream, &launches);
+    else e = launch_gqa<__nv_bfloat16>(a, P, cluster, tail_rows, stream, &launches);
     add_launches(launches);
     if (e != cudaSuccess)
       return gfail(B200_ERR_CUDA, std::string("GroupQueryAttention: CUDA error: ") + cudaGetErrorString(e));
@@ -712,6 +1139,23 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
   } catch (...) {
     return gfail(B200_ERR_FAIL, "GroupQueryAttention: unknown failure");
   }
+}
+
+int b200_group_query_attention_read_status(const B200GqaParams* p, void* stream_ptr) {
+  using namespace b200;
+  if (!p || !p->workspace) return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: no workspace");
+  const GqaPlan P = gqa_plan(p);
+  int bits = 0;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  cudaError_t e = cudaMemcpyAsync(&bits, static_cast<char*>(p->workspace) + P.status, sizeof(int),
+                                  cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess)
+    return gfail(B200_ERR_CUDA, std::string("GroupQueryAttention: CUDA error: ") + cudaGetErrorString(e));
+  if (bits == 0) return B200_OK;
+  if (bits & kStatusTimeout)
+    return gfail(B200_ERR_DEVICE, "GroupQueryAttention: a device wait timed out (bulk copy did not complete)");
+  return gfail(B200_ERR_DEVICE, "GroupQueryAttention: device status " + std::to_string(bits));
 }
 
 }  // extern "C"

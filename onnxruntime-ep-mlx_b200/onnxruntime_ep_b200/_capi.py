@@ -132,6 +132,7 @@ SIGNATURES = {
     "b200_group_query_attention_workspace_size": (
         ctypes.c_int, [ctypes.POINTER(GqaParams), ctypes.POINTER(ctypes.c_size_t)]),
     "b200_group_query_attention": (ctypes.c_int, [ctypes.POINTER(GqaParams), _vp]),
+    "b200_group_query_attention_read_status": (ctypes.c_int, [ctypes.POINTER(GqaParams), _vp]),
     "b200_group_query_attention_claim": (
         ctypes.c_int, [ctypes.POINTER(GqaNodeInfo), ctypes.c_char_p, ctypes.c_size_t]),
 }

@@ -105,11 +105,16 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
 
 
 def group_query_attention(query, key, value, past_key, past_value, seqlens_k, total_sequence_length,
-                          head_sink=None, *, stream=None, **kwargs):
-    """One GroupQueryAttention node.  Returns ``(output, present_key, present_value)``."""
+                          head_sink=None, *, stream=None, check_status=False, **kwargs):
+    """One GroupQueryAttention node.  Returns ``(output, present_key, present_value)``.
+
+    ``check_status=True`` synchronises and raises ``B200Error`` when a bounded device wait of
+    the call ran out."""
     p, keep, out, pk, pv = build_params(query, key, value, past_key, past_value, seqlens_k,
                                         total_sequence_length, head_sink, **kwargs)
     s = stream if stream is not None else torch.cuda.current_stream(query.device)
     check(LIB.b200_group_query_attention(ctypes.byref(p), ctypes.c_void_p(s.cuda_stream)))
+    if check_status:
+        check(LIB.b200_group_query_attention_read_status(ctypes.byref(p), ctypes.c_void_p(s.cuda_stream)))
     del keep
     return out, pk, pv

@@ -67,7 +67,7 @@ def test_golden_cases(case, in_place):
     sink = dev(f["sink"]) if "sink" in f else None
     if in_place:
         kw.update(present_key=pk, present_value=pv)
-    out, ok, ov = gqa.group_query_attention(q, k, v, pk, pv, lengths, int(f["total"][0]), sink, **kw)
+    out, ok, ov = gqa.group_query_attention(q, k, v, pk, pv, lengths, int(f["total"][0]), sink, check_status=True, **kw)
     torch.cuda.synchronize()
     check(host(out), GOLDEN[f"{name}/out/output"], case["dtype"])
     np.testing.assert_array_equal(host(ok), GOLDEN[f"{name}/out/present_k"])
@@ -105,9 +105,9 @@ def run_case(rng, *, dtype="bfloat16", B=1, S=1, H=32, KV=8, D=128, cap=2048, le
         kw.update(present_key=pkt, present_value=pvt)
     if packed:
         qkv = torch.cat([qt, kt, vt], dim=2).contiguous()
-        out, ok, ov = gqa.group_query_attention(qkv, None, None, pkt, pvt, lens, total, skt, **kw)
+        out, ok, ov = gqa.group_query_attention(qkv, None, None, pkt, pvt, lens, total, skt, check_status=True, **kw)
     else:
-        out, ok, ov = gqa.group_query_attention(qt, kt, vt, pkt, pvt, lens, total, skt, **kw)
+        out, ok, ov = gqa.group_query_attention(qt, kt, vt, pkt, pvt, lens, total, skt, check_status=True, **kw)
     torch.cuda.synchronize()
     check(back(out), want, dtype)
     if ok is not None:
