@@ -673,7 +673,7 @@ def run_gqa(args):
             "p10_us": float(np.percentile(ms, 10)) * 1e3, "p90_us": float(np.percentile(ms, 90)) * 1e3,
             "max_abs_err_vs_oracle": max_err,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
-                         "alg_bytes": alg, "kernel": "gqa_attention_kernel (split-K, fused present copy)"},
+                         "alg_bytes": alg, "kernel": "gqa_cluster_kernel (cluster per kv head, DSMEM merge, fused present copy)"},
             "cpu_baseline": cpu,
             "e2e": None if e2e_ms is None else {"value": e2e_ms * 1e3, "unit": "us/call",
                                                  "h2d_bytes_per_step": (Hg * Dg + 2 * KVg * Dg) * 4 + 4,
