@@ -53,6 +53,11 @@ struct PrologueArgs {
 void launch_meta_check(const PrologueArgs& a, cudaStream_t stream);
 size_t prologue_smem_bytes(const PrologueArgs& a);
 cudaError_t launch_prologue(const PrologueArgs& a, cudaStream_t stream);
+// Plain append with a device slot_mapping of at most kAppendFusedMaxTokens tokens: the metadata
+// checks, the duplicate-slot resolution and the copy in one launch (no slot table).
+constexpr int kAppendFusedMaxTokens = 4096;
+bool append_fused_eligible(const PrologueArgs& a);
+cudaError_t launch_append_fused(const PrologueArgs& a, cudaStream_t stream);
 
 // Attention over the paged cache (paged_generic.cu, paged_decode.cu).
 struct AttnArgs {

@@ -336,6 +336,12 @@ int run_prologue(const B200PagedAttentionParams* p, const Layout& L, cudaStream_
   }
   if (duplicates_out) *duplicates_out = dedup;
   b200::PrologueArgs a = prologue_args(p, L, ws, status, dedup, kv_only, route);
+  if ((dedup || !host_meta) && b200::append_fused_eligible(a)) {
+    e = b200::launch_append_fused(a, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "kv_append_fused_kernel");
+    count_launches(1);
+    return B200_OK;
+  }
   if (dedup) {
     e = cudaMemsetAsync(ws + L.owner_keys, 0xff, sizeof(int) * 2 * (size_t)L.owner_cap, stream);
     if (e != cudaSuccess) return cuda_fail(e, "slot table reset");

@@ -49,8 +49,7 @@ __device__ __forceinline__ bool token_slot(const PrologueArgs& a, int t, int b, 
 // the slot -> last-token table.  Thread i checks sequence i, block-table entry i (sequence
 // i / max_blocks, entry i % max_blocks, if the sequence needs it) and token i, so no thread
 // walks a whole block-table row.
-__global__ void meta_check_kernel(PrologueArgs a) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+__device__ __forceinline__ void check_sequence_and_table(const PrologueArgs& a, int64_t i) {
   if (i < a.batch) {
     int c0 = a.cum[i], c1 = a.cum[i + 1];
     int bits = 0;
@@ -73,6 +72,11 @@ __global__ void meta_check_kernel(PrologueArgs a) {
       if (blk < 0 || blk >= a.num_blocks) set_status(a.status, kStatusBadBlock);
     }
   }
+}
+
+__global__ void meta_check_kernel(PrologueArgs a) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  check_sequence_and_table(a, i);
   if (i < a.num_tokens) {
     const int t = (int)i;
     int b = seq_of_token(a.cum, a.batch, t);
@@ -216,6 +220,78 @@ __global__ void __launch_bounds__(32 * kCopyTokensPerCta) kv_copy_kernel(Prologu
       reinterpret_cast<uint16_t*>(vdst)[j] = reinterpret_cast<const uint16_t*>(vsrc)[j];
     }
   }
+}
+
+// Small plain append with a device slot_mapping, in one launch: the metadata checks of
+// meta_check_kernel (grid-stride), then a warp per token.  Every CTA stages the whole
+// slot_mapping (at most kAppendFusedMaxTokens entries) in shared memory, and a token writes only
+// when no later token names the same slot, which is the reference's token-order scatter
+// (the last writer wins) without the slot table and its reset.
+__global__ void __launch_bounds__(32 * kCopyTokensPerCta) kv_append_fused_kernel(PrologueArgs a) {
+  __shared__ int32_t slots[kAppendFusedMaxTokens];
+  const int nt = a.num_tokens;
+  const int64_t checks = max((int64_t)a.batch * max(a.max_blocks, 0), (int64_t)a.batch);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < checks; i += (int64_t)gridDim.x * blockDim.x)
+    check_sequence_and_table(a, i);
+  for (int i = threadIdx.x; i < nt; i += blockDim.x) slots[i] = __ldg(a.slot_mapping + i);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kCopyTokensPerCta + warp;
+  if (t >= nt) return;  // whole warp
+  const int32_t slot = slots[t];
+  if (slot < -1 || (int64_t)slot >= (int64_t)a.num_blocks * a.block_size) {
+    if (lane == 0) set_status(a.status, kStatusBadSlot);
+    return;
+  }
+  if (slot < 0) return;
+  bool later = false;
+  for (int u = t + 1 + lane; u < nt && !later; u += 32) later = slots[u] == slot;
+  if (__any_sync(0xffffffffu, later)) return;  // a later token writes this slot
+  const int64_t bytes = (int64_t)a.kv_heads * a.head_size * 2;
+  char* kdst = reinterpret_cast<char*>(a.key_cache) + (int64_t)slot * bytes;
+  char* vdst = reinterpret_cast<char*>(a.value_cache) + (int64_t)slot * bytes;
+  const char* ksrc = reinterpret_cast<const char*>(a.key) + (int64_t)t * a.key_stride * 2;
+  const char* vsrc = reinterpret_cast<const char*>(a.value) + (int64_t)t * a.value_stride * 2;
+  const bool vec = ((reinterpret_cast<uintptr_t>(kdst) | reinterpret_cast<uintptr_t>(vdst) |
+                     reinterpret_cast<uintptr_t>(ksrc) | reinterpret_cast<uintptr_t>(vsrc) | bytes) & 15) == 0;
+  if (vec) {
+    const int64_t n16 = bytes / 16;
+    for (int64_t j0 = 0; j0 < n16; j0 += 32 * kCopyUnroll) {
+      uint4 kr[kCopyUnroll], vr[kCopyUnroll];
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t j = j0 + u * 32 + lane;
+        if (j < n16) {
+          kr[u] = __ldg(reinterpret_cast<const uint4*>(ksrc) + j);
+          vr[u] = __ldg(reinterpret_cast<const uint4*>(vsrc) + j);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t j = j0 + u * 32 + lane;
+        if (j < n16) {
+          reinterpret_cast<uint4*>(kdst)[j] = kr[u];
+          reinterpret_cast<uint4*>(vdst)[j] = vr[u];
+        }
+      }
+    }
+  } else {
+    for (int64_t j = lane; j < bytes / 2; j += 32) {
+      reinterpret_cast<uint16_t*>(kdst)[j] = reinterpret_cast<const uint16_t*>(ksrc)[j];
+      reinterpret_cast<uint16_t*>(vdst)[j] = reinterpret_cast<const uint16_t*>(vsrc)[j];
+    }
+  }
+}
+
+bool append_fused_eligible(const PrologueArgs& a) {
+  return a.kv_only && a.slot_mapping != nullptr && !(a.do_norm || a.do_rotary) && a.cache_dtype == a.act_dtype &&
+         a.num_tokens > 0 && a.num_tokens <= kAppendFusedMaxTokens && a.route == nullptr;
+}
+
+cudaError_t launch_append_fused(const PrologueArgs& a, cudaStream_t stream) {
+  kv_append_fused_kernel<<<(a.num_tokens + kCopyTokensPerCta - 1) / kCopyTokensPerCta, 32 * kCopyTokensPerCta, 0,
+                           stream>>>(a);
+  return cudaGetLastError();
 }
 
 // One CTA per token, for the processing paths (RMS norm / RoPE, integer or fp8 caches).  Shared

@@ -44,3 +44,58 @@ def test_config2_append_bit_exact(nt):
         keeps_sentinel = (rows.view(torch.int16) == sentinel).all(dim=1)
         assert bool((keeps_sentinel | touched).all())
         assert int(touched.sum()) == valid.numel()
+
+
+@pytest.mark.parametrize("nt", [300, 5000])
+def test_append_duplicate_slots_last_writer_wins(nt):
+    """Many tokens share slots (and some are padding): every slot ends up holding the row of the
+    last token that names it, as the reference's token-order scatter leaves it
+    (attention.rs:4080-4120).  300 tokens take the single-launch path, 5000 the slot table."""
+    dev = torch.device("cuda", 0)
+    nb, bs, kvh, d = 64, 16, 2, 64
+    rng = np.random.default_rng(7)
+    slots = rng.integers(0, 96, size=nt).astype(np.int32)
+    slots[rng.choice(nt, size=nt // 8, replace=False)] = -1
+    k = torch.randn((nt, kvh * d), device=dev).to(torch.bfloat16)
+    v = torch.randn((nt, kvh * d), device=dev).to(torch.bfloat16)
+    kc = torch.full((nb, bs, kvh, d), -3.0, dtype=torch.bfloat16, device=dev)
+    vc = torch.full_like(kc, -3.0)
+    cum = torch.tensor([0, nt], dtype=torch.int32, device=dev)
+    past = torch.zeros(1, dtype=torch.int32, device=dev)
+    bt = (torch.arange(-(-nt // bs), dtype=torch.int32, device=dev) % nb).reshape(1, -1)
+    sm = torch.from_numpy(slots).to(dev)
+    paged.kv_append(k, v, kc, vc, cum, past, bt, sm, kv_num_heads=kvh, check_status=True)
+    last = {}
+    for t, s in enumerate(slots.tolist()):
+        if s >= 0:
+            last[s] = t
+    for new, cache in ((k, kc), (v, vc)):
+        rows = cache.view(nb * bs, kvh * d).view(torch.int16).cpu()
+        src = new.view(torch.int16).cpu()
+        for s, t in last.items():
+            assert torch.equal(rows[s], src[t]), (s, t)
+        untouched = sorted(set(range(nb * bs)) - set(last))
+        assert bool((rows[untouched] == torch.tensor(-3.0, dtype=torch.bfloat16).view(torch.int16)).all())
+
+
+def test_append_invalid_slot_reports_status():
+    from onnxruntime_ep_b200 import B200Error
+    dev = torch.device("cuda", 0)
+    nb, bs, kvh, d = 16, 16, 2, 64
+    nt = 40
+    slots = np.arange(nt, dtype=np.int32)
+    slots[7] = nb * bs  # one past the pool
+    k = torch.randn((nt, kvh * d), device=dev).to(torch.bfloat16)
+    v = torch.randn_like(k)
+    kc = torch.zeros((nb, bs, kvh, d), dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    cum = torch.tensor([0, nt], dtype=torch.int32, device=dev)
+    past = torch.zeros(1, dtype=torch.int32, device=dev)
+    bt = torch.arange(-(-nt // bs), dtype=torch.int32, device=dev).reshape(1, -1)
+    with pytest.raises(B200Error, match="slot_mapping must contain -1 or valid physical cache slots"):
+        paged.kv_append(k, v, kc, vc, cum, past, bt, torch.from_numpy(slots).to(dev), kv_num_heads=kvh,
+                        check_status=True)
+    # the next good call clears the status word
+    slots[7] = 7
+    paged.kv_append(k, v, kc, vc, cum, past, bt, torch.from_numpy(slots).to(dev), kv_num_heads=kvh,
+                    check_status=True)
