@@ -512,11 +512,28 @@ __global__ void __launch_bounds__(kClThreads) gqa_cluster_kernel(const GqaArgs a
     m_run[tid] = -INFINITY;
     l_run[tid] = 0.f;
   }
+  const int k0 = (int)((int64_t)bg.length * cr / CL), k1 = (int)((int64_t)bg.length * (cr + 1) / CL);
+  // Past rows of K and of V of the chunk at c0 (contiguous in the BNSH head): one bulk copy
+  // each, on separate barriers so the scores start while V is in flight (thread 0).
+  auto issue_chunk = [&](int c0) {
+    const int nk = min(kc, k1 - c0);
+    const int np = max(0, min(nk, bg.past - c0));
+    if (np <= 0) return;
+    const uint32_t pbytes = (uint32_t)np * D * sizeof(T);
+    const T* kpast = static_cast<const T*>(a.pk) + (((int64_t)b * a.KV + kh) * a.cap + c0) * D;
+    const T* vpast = static_cast<const T*>(a.pv) + (((int64_t)b * a.KV + kh) * a.cap + c0) * D;
+    fence_proxy_async_smem();  // the previous chunk's generic reads and writes come first
+    mbar_arrive_expect_tx(&bar_k, pbytes);
+    bulk_load(kbuf, kpast, pbytes, &bar_k);
+    mbar_arrive_expect_tx(&bar_v, pbytes);
+    bulk_load(vbuf, vpast, pbytes, &bar_v);
+  };
   if (tid == 0) {
     if (blockIdx.x == 0) *a.status = 0;
     mbar_init(&bar_k, 1);
     mbar_init(&bar_v, 1);
     fence_mbar_init();
+    if (k0 < k1) issue_chunk(k0);  // the first chunk's copies go out before the q loads
   }
   uint32_t phase = 0;
   bool failed = false;  // a staging wait ran out: skip the math, still meet the cluster barriers
@@ -540,7 +557,6 @@ __global__ void __launch_bounds__(kClThreads) gqa_cluster_kernel(const GqaArgs a
     }
   }
 
-  const int k0 = (int)((int64_t)bg.length * cr / CL), k1 = (int)((int64_t)bg.length * (cr + 1) / CL);
   const int cq = tid % kUnits, kgrp = tid / kUnits;
   float o[R][4];
 #pragma unroll
@@ -550,19 +566,9 @@ __global__ void __launch_bounds__(kClThreads) gqa_cluster_kernel(const GqaArgs a
   for (int c0 = k0; c0 < k1 && !failed; c0 += kc) {
     const int nk = min(kc, k1 - c0);
     const int np = max(0, min(nk, bg.past - c0));  // rows from the past cache
-    // ---- stage: the past rows of K and of V (contiguous in the BNSH head) by one bulk copy
-    // each, on separate barriers so the scores start while V is in flight; new rows by plain
-    // loads
-    const uint32_t pbytes = (uint32_t)np * D * sizeof(T);
-    if (np > 0 && tid == 0) {
-      const T* kpast = static_cast<const T*>(a.pk) + (((int64_t)b * a.KV + kh) * a.cap + c0) * D;
-      const T* vpast = static_cast<const T*>(a.pv) + (((int64_t)b * a.KV + kh) * a.cap + c0) * D;
-      fence_proxy_async_smem();  // the previous chunk's generic reads and writes come first
-      mbar_arrive_expect_tx(&bar_k, pbytes);
-      bulk_load(kbuf, kpast, pbytes, &bar_k);
-      mbar_arrive_expect_tx(&bar_v, pbytes);
-      bulk_load(vbuf, vpast, pbytes, &bar_v);
-    }
+    // ---- stage: past rows by bulk copies (issued here for every chunk after the first), new
+    // rows by plain loads
+    if (tid == 0 && c0 != k0) issue_chunk(c0);
     for (int i = tid; i < (nk - np) * kUnits; i += kClThreads) {
       const int k = np + i / kUnits, d = (i % kUnits) * 4;
       st4(kbuf + (size_t)k * D + d, ld4(key_row<T>(a, bg, b, kh, c0 + k, false) + d));
