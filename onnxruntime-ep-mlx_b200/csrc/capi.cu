@@ -16,7 +16,6 @@
 #include <cstring>
 #include <mutex>
 #include <string>
-#include <unordered_set>
 #include <vector>
 
 #include "b200_kernels.h"
@@ -198,22 +197,29 @@ int validate_host(const B200PagedAttentionParams* p, bool* duplicates) {
     }
   }
   const int64_t maxb = p->max_blocks_per_seq;
+  const uint32_t nblocks = (uint32_t)std::max(p->num_blocks, 0);
   for (int b = 0; b < B; ++b) {
     int64_t total = (int64_t)past[b] + cum[b + 1] - cum[b];
     if (total > INT32_MAX || total > maxb * p->block_size)
       return fail(B200_ERR_FAIL, "PagedAttention: sequence exceeds block table capacity");
-    int64_t needed = (total + p->block_size - 1) / p->block_size;
-    for (int64_t j = 0; j < needed; ++j) {
-      int32_t blk = bt[b * maxb + j];
-      if (blk < 0 || blk >= p->num_blocks)
-        return fail(B200_ERR_FAIL, "PagedAttention: block table contains an invalid physical block");
-    }
+    const int64_t needed = (total + p->block_size - 1) / p->block_size;
+    // Branch-free over the row (vectorised): a negative entry is a large unsigned value.
+    const int32_t* row = bt + b * maxb;
+    uint32_t bad_row = 0;
+    for (int64_t j = 0; j < needed; ++j) bad_row |= (uint32_t)((uint32_t)row[j] >= nblocks);
+    if (bad_row)
+      return fail(B200_ERR_FAIL, "PagedAttention: block table contains an invalid physical block");
     if (p->do_rotary && total > p->rotary_positions)
       return fail(B200_ERR_FAIL, "PagedAttention: rotary position exceeds the cos/sin cache");
   }
   if (duplicates) {
-    std::unordered_set<int64_t> seen;
-    seen.reserve((size_t)p->num_tokens * 2 + 1);
+    // Open-addressing set of the written slots (reused across calls on this thread).
+    thread_local std::vector<int64_t> table;
+    size_t cap = 16;
+    while (cap < (size_t)p->num_tokens * 2) cap <<= 1;
+    if (table.size() < cap) table.resize(cap);
+    std::fill(table.begin(), table.begin() + cap, (int64_t)-1);
+    const size_t mask = cap - 1;
     *duplicates = false;
     for (int b = 0; b < B && !*duplicates; ++b) {
       for (int t = cum[b]; t < cum[b + 1]; ++t) {
@@ -225,7 +231,13 @@ int validate_host(const B200PagedAttentionParams* p, bool* duplicates) {
           slot = (int64_t)bt[b * maxb + logical / p->block_size] * p->block_size + logical % p->block_size;
         }
         if (slot < 0) continue;
-        if (!seen.insert(slot).second) { *duplicates = true; break; }
+        size_t h = (size_t)((uint64_t)slot * 0x9e3779b97f4a7c15ull >> 17) & mask;
+        while (table[h] != -1 && table[h] != slot) h = (h + 1) & mask;
+        if (table[h] == slot) {
+          *duplicates = true;
+          break;
+        }
+        table[h] = slot;
       }
     }
   }
