@@ -51,6 +51,8 @@ def parse():
                     help="CPU work budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time the steps as eager C-ABI calls instead of CUDA-graph replays of the call")
     ap.add_argument("--seqs", type=int, default=B_PER_GPU, help="sequences per GPU (profiling runs use fewer)")
     ap.add_argument("--pool-blocks", type=int, default=NB_PER_GPU, help="KV pool blocks per GPU")
     ap.add_argument("--mixed-chunks", type=int, default=8, help="mixed workload: prefill chunks")
@@ -84,6 +86,54 @@ def make_metadata(n_gpus: int, seqs: int = B_PER_GPU, pool_blocks: int = NB_PER_
     cum = np.arange(B + 1, dtype=np.int32)
     past = (L - 1).astype(np.int32)
     return dict(B=B, L=L, NB=NB, maxb=maxb, bt=bt, cum=cum, past=past)
+
+
+def capture_call(capi, pp, p, dev):
+    """The C-ABI call captured once in a CUDA graph on `dev` (the NCCL all-gather stays outside
+    the graph).  Returns (graph, None) or (None, reason).  Host validation of the metadata runs
+    at capture; the replayed steps reuse the same metadata, as a serving loop with fixed
+    metadata buffers does."""
+    import ctypes
+
+    import torch
+    p.attention_event_begin = p.attention_event_end = None
+    g = torch.cuda.CUDAGraph()
+    try:
+        torch.cuda.synchronize(dev)
+        rc = 0
+        # thread-local capture: other threads (the NCCL watchdog) keep making CUDA calls
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
+            cs = torch.cuda.current_stream(dev)
+            rc = capi.LIB.b200_paged_attention(pp, ctypes.c_void_p(cs.cuda_stream))
+        if rc != 0:
+            raise RuntimeError(capi.LIB.b200_last_error().decode())
+        g.replay()
+        torch.cuda.synchronize(dev)
+        return g, None
+    except Exception as e:  # noqa: BLE001 - reported in the JSON line, eager timing stays
+        torch.cuda.synchronize(dev)
+        return None, f"unavailable: {e}"
+
+
+def graph_loop(graph, after, steps, stream, dist):
+    """Time `steps` replays of `graph`, each followed by `after()` (eager), max over ranks."""
+    import torch
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        graph.replay()
+        after()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if dist:
+        t = torch.tensor([ms], device=stream.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    return ms
 
 
 def decode_bytes(meta, kv_heads):
@@ -278,17 +328,30 @@ def run_b200(args):
     pp = ctypes.byref(p)
     gathered = torch.empty((n, B, qh * D), dtype=torch.bfloat16, device=dev) if n > 1 else None
 
-    def step():
-        _capi.check(_capi.LIB.b200_paged_attention(pp, sp))
+    def gather():
         if n > 1:
             # one NCCL all-gather of the head-sharded outputs, then the head permute
             dist.all_gather_into_tensor(gathered, out)
             return sharding.reassemble(gathered)
         return out
 
+    def step():
+        _capi.check(_capi.LIB.b200_paged_attention(pp, sp))
+        return gather()
+
     for _ in range(args.warmup):
         step()
     _capi.check(_capi.LIB.b200_read_status(pp, sp))
+    graph, graph_note = (None, "off (--no-graph)") if args.no_graph else capture_call(_capi, pp, p, dev)
+    if dist:  # every rank takes the same path (a failed capture anywhere means eager everywhere)
+        ok = torch.tensor([1 if graph is not None else 0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok[0]) == 0 and graph is not None:
+            graph, graph_note = None, "unavailable on another rank"
+    if graph is not None:
+        for _ in range(args.warmup):
+            graph.replay()
+            gather()
 
     # per-launch attention timing on the launch stream
     ev_pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -310,6 +373,7 @@ def run_b200(args):
             step()
         t_end.record(stream)
         torch.cuda.synchronize()
+        graph_ms = graph_loop(graph, gather, args.steps, stream, dist) if graph is not None else None
     p.attention_event_begin = p.attention_event_end = None
     launches = _capi.LIB.b200_launch_count() - launches0
     elapsed_ms = t_start.elapsed_time(t_end)
@@ -320,6 +384,10 @@ def run_b200(args):
         dist.barrier()
         elapsed_ms, attn_ms = float(t[0]), float(t[1])
     _capi.check(_capi.LIB.b200_read_status(pp, sp))
+    eager_ms_per_step = elapsed_ms / args.steps
+    if graph_ms is not None:
+        elapsed_ms = graph_ms
+        launches *= 2  # the graph loop replays the same kernels once more per step
     ms_per_step = elapsed_ms / args.steps
     value = B / (ms_per_step / 1e3)
 
@@ -395,7 +463,11 @@ def run_b200(args):
                        "global_batch": B, "num_blocks_per_gpu": NB, "kv_heads_per_gpu": kvh,
                        "l2": "inputs larger than L2 (KV pool 2 x %.1f GiB, %.2f GB read per step)" %
                              (kc.numel() * 2 / 2**30, kv_bytes / 1e9),
-                       "parallelism": f"kv-head shard x{n}" + (" + NCCL all-gather" if n > 1 else "")},
+                       "parallelism": f"kv-head shard x{n}" + (" + NCCL all-gather" if n > 1 else ""),
+                       "step": ("CUDA-graph replay of the C-ABI call (metadata validated at capture)"
+                                + (" + eager NCCL all-gather" if n > 1 else "")) if graph is not None
+                       else f"eager C-ABI call ({graph_note})",
+                       "eager_ms_per_step": eager_ms_per_step},
             "kv_read_gbs": kv_bytes / (attn_ms / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
@@ -408,6 +480,7 @@ def run_b200(args):
             "gpu_launches": int(launches),
         }
         print(json.dumps(line), flush=True)
+    graph = None  # released before the process group goes
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -746,16 +819,29 @@ def run_fp8(args):
     sp, pp = ctypes.c_void_p(stream.cuda_stream), ctypes.byref(p)
     gathered = torch.empty((n, B5, qh * D), dtype=torch.bfloat16, device=dev) if n > 1 else None
 
-    def step():
-        _capi.check(_capi.LIB.b200_paged_attention(pp, sp))
+    def gather():
         if n > 1:
             dist.all_gather_into_tensor(gathered, out)
             return sharding.reassemble(gathered)
         return out
 
+    def step():
+        _capi.check(_capi.LIB.b200_paged_attention(pp, sp))
+        return gather()
+
     for _ in range(max(args.warmup, 3)):
         step()
     _capi.check(_capi.LIB.b200_read_status(pp, sp))
+    graph, graph_note = (None, "off (--no-graph)") if args.no_graph else capture_call(_capi, pp, p, dev)
+    if dist:  # every rank takes the same path
+        ok = torch.tensor([1 if graph is not None else 0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok[0]) == 0 and graph is not None:
+            graph, graph_note = None, "unavailable on another rank"
+    if graph is not None:
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+            gather()
     steps = args.steps
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     for a_, b_ in ev:
@@ -774,6 +860,7 @@ def run_fp8(args):
             step()
         t1.record(stream)
         torch.cuda.synchronize()
+        graph_ms = graph_loop(graph, gather, steps, stream, dist) if graph is not None else None
     p.attention_event_begin = p.attention_event_end = None
     launches = _capi.LIB.b200_launch_count() - launches0
     elapsed_ms = t0.elapsed_time(t1)
@@ -814,6 +901,10 @@ def run_fp8(args):
         e2e = {"value": B5 / (e_ms / steps / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(hout.numel() * hout.element_size())}
     _capi.check(_capi.LIB.b200_read_status(pp, sp))
+    eager_ms_per_step = elapsed_ms / steps
+    if graph_ms is not None:
+        elapsed_ms = graph_ms
+        launches *= 2  # the graph loop replays the same kernels once more per step
     ms_per_step = elapsed_ms / steps
     kv_bytes = int(L.sum()) * kvh * D * 2 + int(need.sum()) * kvh * 4 * 2
     alg = kv_bytes + B5 * (qh + 2 * kvh) * D * 2 + B5 * qh * D * 2 + int(need.sum()) * 4
@@ -855,7 +946,11 @@ def run_fp8(args):
                                        "bs16, B=256, ctx U[4096,32768], per-(block, kv head) scales U(0.01,0.1)",
                            "kv_heads_per_gpu": kvh, "num_blocks": NB,
                            "l2": f"inputs larger than L2 ({kv_bytes / 1e9:.2f} GB of KV per step per GPU)",
-                           "parallelism": f"kv-head shard x{n}" + (" + NCCL all-gather" if n > 1 else "")},
+                           "parallelism": f"kv-head shard x{n}" + (" + NCCL all-gather" if n > 1 else ""),
+                           "step": ("CUDA-graph replay of the C-ABI call (metadata validated at capture)"
+                                    + (" + eager NCCL all-gather" if n > 1 else "")) if graph is not None
+                           else f"eager C-ABI call ({graph_note})",
+                           "eager_ms_per_step": eager_ms_per_step},
                 "kv_read_gbs": kv_bytes / (attn_ms / 1e3) / 1e9,
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                              "kernel": "attention section (paged_decode_kernel fp8, split-K combine fused in)",
@@ -864,6 +959,7 @@ def run_fp8(args):
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
+        graph = None  # released before the process group goes
         dist.destroy_process_group()
 
 
