@@ -91,3 +91,36 @@ def test_codec_byte_equations(bits, scale):
     np.testing.assert_array_equal(ref.quant_encode(values, s, bits, paged=False),
                                   GOLDEN[f"{key}/codes_gqa"])
     np.testing.assert_array_equal(ref.quant_decode(codes, s, bits, 16), GOLDEN[f"{key}/decoded"])
+
+
+# The C restatement (oracle/paged_ref.c, through oracle/cpu_oracle.py) is the checker of the
+# full-size GPU parity tests and the timed CPU baseline; it covers float caches without RoPE or
+# q/k norm, so it is pinned on those golden cases, in both output modes.
+C_CASES = [c for c in FLOAT_CASES if not any(k in cases.float_inputs(c) for k in ("cos", "q_norm"))]
+
+
+@pytest.mark.parametrize("case", C_CASES, ids=lambda c: c["name"])
+def test_c_oracle_matches_reference_float(case):
+    from oracle import cpu_oracle
+
+    feeds = cases.float_inputs(case)
+    name = case["name"]
+    kw = dict(case.get("ref_kwargs", {}))
+    sink = feeds.get("head_sink")
+    call = dict(slot_mapping=feeds.get("slot_mapping"), is_causal=kw.get("is_causal", True),
+                local_window_size=kw.get("local_window_size", -1),
+                head_sink=None if sink is None else sink.astype(np.float32), threads=2)
+    meta = [feeds[n] for n in ("cumulative_sequence_length", "past_seqlens", "block_table")]
+    want = GOLDEN[f"{name}/output"]
+    kc, vc = feeds["key_cache"].copy(), feeds["value_cache"].copy()
+    out32 = cpu_oracle.paged_attention(feeds["query"], feeds["key"], feeds["value"], kc, vc, *meta,
+                                       case["H"], case["KV"], fp32_out=True, **call)
+    # fp32 against fp32: only the summation order differs (eight-lane partial sums here)
+    np.testing.assert_allclose(out32, want, rtol=1e-4, atol=1e-4)
+    for tag, got, before in (("k", kc, feeds["key_cache"]), ("v", vc, feeds["value_cache"])):
+        expect = _apply_delta(before, GOLDEN[f"{name}/{tag}_slots"], GOLDEN[f"{name}/{tag}_rows"])
+        np.testing.assert_array_equal(got.view(np.uint16), expect.view(np.uint16))
+    # the rounded mode is the fp32 output rounded once to the activation dtype
+    out16 = cpu_oracle.paged_attention(feeds["query"], feeds["key"], feeds["value"], feeds["key_cache"].copy(),
+                                       feeds["value_cache"].copy(), *meta, case["H"], case["KV"], **call)
+    np.testing.assert_array_equal(out16, out32.astype(out16.dtype))
