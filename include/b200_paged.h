@@ -165,8 +165,21 @@ B200_API int b200_kv_append(const B200PagedAttentionParams* p, void* stream);
  * a device share the array (each call re-initialises what must start at zero), so calls that
  * overlap on the GPU race and must be serialised by the caller.  The first call on a device
  * resolves the array's address (cudaGetSymbolAddress) and should come before any stream
- * capture.  The call allocates nothing. */
+ * capture; the address is kept until exit, so cudaDeviceReset is not supported alongside this
+ * entry point.  The scratch need grows with the token count (RoPE / q-k norm rows), the batch
+ * and the SM count (decode partial rows: SMs x resident decode CTAs x 4 warps x 16 rows x
+ * head_size x 4 bytes, about 9.7 MB at head_size 256 on 148 SMs), so a num_sms override far
+ * above the device's count can push a call past the limit.  Without device_status the status
+ * word lives in the static array too: read it with b200_read_status_static_scratch.  The call
+ * allocates nothing. */
 B200_API int b200_paged_attention_static_scratch(const B200PagedAttentionParams* p, void* stream);
+
+/* b200_read_status for calls made through b200_paged_attention_static_scratch: reads
+ * p->device_status when set, otherwise the status word inside the current device's static
+ * scratch (so device-side metadata errors and timed-out waits reach callers that pass no
+ * status word).  Reads the last call's word, so calls that overlap on the GPU race here too.
+ * No counterpart in the reference; allocates nothing. */
+B200_API int b200_read_status_static_scratch(const B200PagedAttentionParams* p, void* stream);
 
 /* Synchronise `stream`, read and clear the device status word of the last call with these
  * params, and turn set bits into B200_ERR_FAIL / B200_ERR_DEVICE with the reference's

@@ -122,6 +122,10 @@ int encode_tensor_map_u8(CUtensorMap* map, int rank, const void* base, const uin
 
 cudaError_t launch_decode(const AttnArgs& a, const DecodePlan& plan, const DecodeMaps& maps, int num_sms,
                           cudaStream_t stream);
+// Resident decode CTAs per SM for this head size / dtype pair on the current device (at most
+// kDecodeMaxCtasPerSm): the decode grid is num_sms times this, and the workspace's partial rows
+// are sized from it.
+int decode_ctas_per_sm(int head_size, int act_dtype, int cache_dtype);
 struct PrefillMaps {
   CUtensorMap k_map;  // cache views, as DecodeMaps
   CUtensorMap v_map;

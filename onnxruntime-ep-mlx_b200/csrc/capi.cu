@@ -107,8 +107,10 @@ Layout make_layout(const B200PagedAttentionParams* p) {
     L.pf_total = take(sizeof(int64_t));
   }
   if (L.fast_decode || L.fast_prefill) {
-    // Stream-K decode: at most 2 partial slots of 8 rows per warp of the persistent grid.
-    const size_t max_warps = (size_t)device_sm_count(p) * b200::kDecodeMaxCtasPerSm * b200::kDecodeWarpsPerCta;
+    // Stream-K decode: at most 2 partial slots of 8 rows per warp of the persistent grid, whose
+    // size is SMs x resident decode CTAs per SM (the prefill kernel keeps no partials).
+    const int ctas = L.fast_decode ? b200::decode_ctas_per_sm(p->head_size, p->act_dtype, p->cache_dtype) : 1;
+    const size_t max_warps = (size_t)device_sm_count(p) * ctas * b200::kDecodeWarpsPerCta;
     const size_t part_rows = max_warps * 2 * b200::kDecodeRows;
     L.min_tiles_per_warp = p->decode_min_tiles_per_warp > 0 ? p->decode_min_tiles_per_warp : 4;
     L.total_tiles = take(sizeof(int64_t));

@@ -18,6 +18,10 @@
 //    without ordering) race on it and must be serialised by the caller;
 //  * the first call on a device resolves the array's device address with cudaGetSymbolAddress,
 //    which may load the module onto that device; make that first call before any stream capture.
+//    The address is kept for the life of the process, so cudaDeviceReset (which unloads the
+//    module and frees the array) is not supported while this entry point is in use;
+//  * without a caller-provided device_status the status word also lives in the array: read it
+//    with b200_read_status_static_scratch (b200_read_status sees no workspace and refuses).
 // The call itself allocates nothing: no cudaMalloc/cudaFree and no allocating library routine.
 #include <cuda_runtime.h>
 
@@ -39,28 +43,31 @@ constexpr int kMaxDevices = 64;
 void* g_scratch_ptr[kMaxDevices] = {nullptr};
 std::mutex g_scratch_mutex;
 
+// Device address of this device's static scratch; resolved once per device, with that device
+// current (the set-up step of the first call on it).
+int static_scratch_address(const char* who, void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return b200::set_error(B200_ERR_CUDA, std::string(who) + ": no current CUDA device");
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_ptr[dev]) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    if (e != cudaSuccess || !ptr)
+      return b200::set_error(B200_ERR_CUDA, std::string(who) + ": cudaGetSymbolAddress failed: " + cudaGetErrorString(e));
+    g_scratch_ptr[dev] = ptr;
+  }
+  *out = g_scratch_ptr[dev];
+  return B200_OK;
+}
+
 }  // namespace
 
 extern "C" int b200_paged_attention_static_scratch(const B200PagedAttentionParams* p, void* stream) {
   if (!p) return b200::set_error(B200_ERR_INVALID_ARGUMENT, "PagedAttention (static scratch): null params");
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-    return b200::set_error(B200_ERR_CUDA, "PagedAttention (static scratch): no current CUDA device");
-
-  // One-time set-up per device, with that device current.
   void* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_ptr[dev]) {
-      void* ptr = nullptr;
-      cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
-      if (e != cudaSuccess || !ptr)
-        return b200::set_error(B200_ERR_CUDA, std::string("PagedAttention (static scratch): cudaGetSymbolAddress failed: ") +
-                                                  cudaGetErrorString(e));
-      g_scratch_ptr[dev] = ptr;
-    }
-    scratch = g_scratch_ptr[dev];
-  }
+  int rc0 = static_scratch_address("PagedAttention (static scratch)", &scratch);
+  if (rc0 != B200_OK) return rc0;
 
   B200PagedAttentionParams q = *p;
   q.workspace = scratch;
@@ -88,4 +95,18 @@ extern "C" int b200_paged_attention_static_scratch(const B200PagedAttentionParam
                                " (32 MiB); use b200_paged_attention with a caller workspace");
   }
   return b200_paged_attention(&q, stream);
+}
+
+extern "C" int b200_read_status_static_scratch(const B200PagedAttentionParams* p, void* stream) {
+  if (!p) return b200::set_error(B200_ERR_INVALID_ARGUMENT, "PagedAttention (static scratch): null params");
+  if (p->device_status) return b200_read_status(p, stream);
+  void* scratch = nullptr;
+  int rc = static_scratch_address("PagedAttention (static scratch)", &scratch);
+  if (rc != B200_OK) return rc;
+  // The status word sits where b200_paged_attention_static_scratch put it: at the workspace
+  // layout's status offset inside this device's static array.
+  B200PagedAttentionParams q = *p;
+  q.workspace = scratch;
+  q.workspace_bytes = kStaticScratchBytes;
+  return b200_read_status(&q, stream);
 }

@@ -655,9 +655,12 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
 // ---------------------------------------------------------------------------------------
 // Launch
 // ---------------------------------------------------------------------------------------
+// Resident CTAs per SM of one decode instantiation on the current device (its shared-memory
+// need decides it), capped at kDecodeMaxCtasPerSm.  Cached per device; the first query also sets
+// the kernel's dynamic shared-memory limit.  The workspace sizing of the partial rows and the
+// launch grid both use it, so the grid never has more warps than the partial rows cover.
 template <typename T, int D, int STAGES, bool FP8 = false>
-static cudaError_t launch_decode_t(const AttnArgs& a, const DecodePlan& plan, const DecodeMaps& maps, int num_sms,
-                                   cudaStream_t stream) {
+static int decode_occupancy_t(cudaError_t* err) {
   using L = DecodeLayout<D, FP8>;
   constexpr size_t smem = (size_t)kDecodeWarps * STAGES * L::kStageBytes + 1024;
   static int occupancy[64] = {0};
@@ -667,14 +670,45 @@ static cudaError_t launch_decode_t(const AttnArgs& a, const DecodePlan& plan, co
   if (occupancy[dev] == 0) {
     cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<T, D, STAGES, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
-    if (e != cudaSuccess) return e;
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, paged_decode_kernel<T, D, STAGES, FP8>, 128, smem);
-    if (e != cudaSuccess) return e;
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, paged_decode_kernel<T, D, STAGES, FP8>, 128, smem);
+    if (e != cudaSuccess) {
+      if (err) *err = e;
+      return kDecodeMaxCtasPerSm;
+    }
     occupancy[dev] = occ < 1 ? 1 : (occ > kDecodeMaxCtasPerSm ? kDecodeMaxCtasPerSm : occ);
   }
-  paged_decode_kernel<T, D, STAGES, FP8><<<num_sms * occupancy[dev], 128, smem, stream>>>(a, maps, plan);
+  return occupancy[dev];
+}
+
+template <typename T, int D, int STAGES, bool FP8 = false>
+static cudaError_t launch_decode_t(const AttnArgs& a, const DecodePlan& plan, const DecodeMaps& maps, int num_sms,
+                                   cudaStream_t stream) {
+  using L = DecodeLayout<D, FP8>;
+  constexpr size_t smem = (size_t)kDecodeWarps * STAGES * L::kStageBytes + 1024;
+  cudaError_t e = cudaSuccess;
+  const int occ = decode_occupancy_t<T, D, STAGES, FP8>(&e);
+  if (e != cudaSuccess) return e;
+  paged_decode_kernel<T, D, STAGES, FP8><<<num_sms * occ, 128, smem, stream>>>(a, maps, plan);
   return cudaGetLastError();
+}
+
+int decode_ctas_per_sm(int head_size, int act_dtype, int cache_dtype) {
+  const bool bf = act_dtype == B200_DTYPE_BFLOAT16;
+  if (cache_dtype == B200_DTYPE_FLOAT8E4M3FN) {
+    switch (head_size) {
+      case 128: return decode_occupancy_t<__half, 128, 3, true>(nullptr);
+      case 256: return decode_occupancy_t<__half, 256, 2, true>(nullptr);
+      default: return kDecodeMaxCtasPerSm;
+    }
+  }
+  switch (head_size) {
+    case 64: return bf ? decode_occupancy_t<__nv_bfloat16, 64, 4>(nullptr) : decode_occupancy_t<__half, 64, 4>(nullptr);
+    case 128: return bf ? decode_occupancy_t<__nv_bfloat16, 128, 3>(nullptr) : decode_occupancy_t<__half, 128, 3>(nullptr);
+    case 256: return bf ? decode_occupancy_t<__nv_bfloat16, 256, 2>(nullptr) : decode_occupancy_t<__half, 256, 2>(nullptr);
+    default: return kDecodeMaxCtasPerSm;
+  }
 }
 
 cudaError_t launch_decode_plan(const AttnArgs& a, const DecodePlan& plan, cudaStream_t stream) {

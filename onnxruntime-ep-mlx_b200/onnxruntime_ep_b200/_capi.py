@@ -123,6 +123,7 @@ SIGNATURES = {
     "b200_paged_attention": (ctypes.c_int, [ctypes.POINTER(PagedAttentionParams), _vp]),
     "b200_kv_append": (ctypes.c_int, [ctypes.POINTER(PagedAttentionParams), _vp]),
     "b200_paged_attention_static_scratch": (ctypes.c_int, [ctypes.POINTER(PagedAttentionParams), _vp]),
+    "b200_read_status_static_scratch": (ctypes.c_int, [ctypes.POINTER(PagedAttentionParams), _vp]),
     "b200_read_status": (ctypes.c_int, [ctypes.POINTER(PagedAttentionParams), _vp]),
     "b200_selftest_tcgen05": (ctypes.c_int, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_paged_attention_claim": (
