@@ -293,6 +293,8 @@ typedef struct B200GqaNodeInfo {
       sliding_window_cache, smooth_softmax, qk_output, kv_cache_bit_width;
   int32_t has_causal, has_local_window_size, has_smooth_softmax; /* 0 = operator default   */
   float softcap;
+  int32_t has_scale;         /* 0 = attribute absent: 1/sqrt(head_size)                      */
+  float scale;
 } B200GqaNodeInfo;
 
 B200_API int b200_group_query_attention_claim(const B200GqaNodeInfo* node, char* reason, size_t reason_len);

@@ -1,4 +1,4 @@
-"""ctypes binding of ``include/b200_paged.h`` (the library's C ABI).
+"""ctypes binding of ``include/b200_paged.h`` and ``include/b200_ep.h`` (the library's C ABI).
 
 The library is loaded from this package folder.  A missing or stale library raises at import
 time: there is no CPU fallback for the claimed path.
@@ -106,11 +106,51 @@ class GqaNodeInfo(ctypes.Structure):
         ("do_rotary", _i64), ("rotary_interleaved", _i64), ("sliding_window_cache", _i64),
         ("smooth_softmax", _i64), ("qk_output", _i64), ("kv_cache_bit_width", _i64),
         ("has_causal", _i32), ("has_local_window_size", _i32), ("has_smooth_softmax", _i32),
-        ("softcap", _f32),
+        ("softcap", _f32), ("has_scale", _i32), ("scale", _f32),
     ]
 
 
-# Every entry point the header declares, with its ctypes signature.
+class EpOptions(ctypes.Structure):
+    """Mirror of ``B200EpOptions`` (include/b200_ep.h)."""
+
+    _fields_ = [("kv_pool_bytes", ctypes.c_uint64), ("has_kv_pool_bytes", _i32), ("num_gpus", _i32),
+                ("device_id", _i32), ("decode_min_tiles_per_warp", _i32), ("force_generic", _i32),
+                ("check_status", _i32)]
+
+
+class KvPoolDesc(ctypes.Structure):
+    """Mirror of ``B200KvPoolDesc``."""
+
+    _fields_ = [("device", _i32), ("block_size", _i32), ("kv_num_heads", _i32), ("head_size", _i32),
+                ("cache_dtype", _i32), ("num_blocks", _i32), ("budget_bytes", ctypes.c_uint64),
+                ("key_cache", _vp), ("value_cache", _vp), ("k_scale", _vp), ("v_scale", _vp)]
+
+
+class KvPoolInfo(ctypes.Structure):
+    """Mirror of ``B200KvPoolInfo``."""
+
+    _fields_ = [("key_cache", _vp), ("value_cache", _vp), ("k_scale", _vp), ("v_scale", _vp),
+                ("num_blocks", _i32), ("free_blocks", _i32), ("block_size", _i32), ("owns_memory", _i32),
+                ("block_bytes", ctypes.c_uint64), ("allocated_bytes", ctypes.c_uint64)]
+
+
+class PagedTensors(ctypes.Structure):
+    """Mirror of ``B200PagedTensors`` (one PagedAttention Compute's inputs and sizes)."""
+
+    _fields_ = [("query", _vp), ("key", _vp), ("value", _vp), ("key_cache", _vp), ("value_cache", _vp),
+                ("cumulative_sequence_length", _vp), ("past_seqlens", _vp), ("block_table", _vp),
+                ("cos_cache", _vp), ("sin_cache", _vp), ("slot_mapping", _vp), ("head_sink", _vp),
+                ("q_norm_weight", _vp), ("k_norm_weight", _vp), ("k_scale", _vp), ("v_scale", _vp),
+                ("output", _vp), ("host_cumulative_sequence_length", _vp), ("host_past_seqlens", _vp),
+                ("host_block_table", _vp), ("host_slot_mapping", _vp),
+                ("num_tokens", _i32), ("query_hidden", _i32), ("batch", _i32), ("num_blocks", _i32),
+                ("block_size", _i32), ("max_blocks_per_seq", _i32), ("rotary_positions", _i32),
+                ("rotary_half_dim", _i32), ("act_dtype", _i32), ("cache_dtype", _i32)]
+
+
+B200_ORT_OK, B200_ORT_INVALID_ARGUMENT, B200_ORT_EP_FAIL = 0, 1, 2
+
+# Every entry point the headers declare, with its ctypes signature.
 SIGNATURES = {
     "b200_version": (ctypes.c_int, []),
     "b200_params_size": (ctypes.c_size_t, []),
@@ -136,6 +176,26 @@ SIGNATURES = {
     "b200_group_query_attention_read_status": (ctypes.c_int, [ctypes.POINTER(GqaParams), _vp]),
     "b200_group_query_attention_claim": (
         ctypes.c_int, [ctypes.POINTER(GqaNodeInfo), ctypes.c_char_p, ctypes.c_size_t]),
+    # include/b200_ep.h
+    "b200_ep_options_parse": (ctypes.c_int, [ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_char_p),
+                                             ctypes.c_size_t, ctypes.POINTER(EpOptions)]),
+    "b200_ort_error_class": (ctypes.c_int, [ctypes.c_int]),
+    "b200_ep_struct_size": (ctypes.c_size_t, [_i32]),
+    "b200_kv_pool_block_bytes": (ctypes.c_int, [ctypes.POINTER(KvPoolDesc), ctypes.POINTER(ctypes.c_uint64)]),
+    "b200_kv_pool_create": (ctypes.c_int, [ctypes.POINTER(KvPoolDesc), ctypes.POINTER(_vp)]),
+    "b200_kv_pool_destroy": (ctypes.c_int, [_vp]),
+    "b200_kv_pool_info": (ctypes.c_int, [_vp, ctypes.POINTER(KvPoolInfo)]),
+    "b200_kv_pool_alloc": (ctypes.c_int, [_vp, _i32, ctypes.POINTER(_i32)]),
+    "b200_kv_pool_free": (ctypes.c_int, [_vp, ctypes.POINTER(_i32), _i32]),
+    "b200_kv_pool_blocks_for": (_i32, [_vp, _i64]),
+    "b200_ep_node_create_paged": (ctypes.c_int, [ctypes.POINTER(NodeInfo), ctypes.POINTER(EpOptions),
+                                                 ctypes.POINTER(_vp)]),
+    "b200_ep_node_create_gqa": (ctypes.c_int, [ctypes.POINTER(GqaNodeInfo), ctypes.POINTER(EpOptions),
+                                               ctypes.POINTER(_vp)]),
+    "b200_ep_node_destroy": (ctypes.c_int, [_vp]),
+    "b200_ep_node_compute_paged": (ctypes.c_int, [_vp, ctypes.POINTER(PagedTensors), _vp]),
+    "b200_ep_node_compute_gqa": (ctypes.c_int, [_vp, ctypes.POINTER(GqaParams), _vp]),
+    "b200_ep_node_stats": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
 }
 
 
@@ -170,6 +230,9 @@ def load() -> ctypes.CDLL:
         raise ImportError("libb200_paged.so: B200GqaParams layout differs from the binding")
     if lib.b200_gqa_node_info_size() != ctypes.sizeof(GqaNodeInfo):
         raise ImportError("libb200_paged.so: B200GqaNodeInfo layout differs from the binding")
+    for which, cls in enumerate((EpOptions, KvPoolDesc, KvPoolInfo, PagedTensors)):
+        if lib.b200_ep_struct_size(which) != ctypes.sizeof(cls):
+            raise ImportError(f"libb200_paged.so: {cls.__name__} layout differs from the binding")
     return lib
 
 

@@ -12,17 +12,18 @@ import pytest
 from onnxruntime_ep_b200 import _capi
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "b200_paged.h")
+HEADERS = [os.path.join(ROOT, "include", h) for h in sorted(os.listdir(os.path.join(ROOT, "include")))
+           if h.endswith(".h")]
 
 
 def declared_symbols():
-    text = open(HEADER).read()
+    text = "".join(open(h).read() for h in HEADERS)
     return sorted(set(re.findall(r"B200_API\s+[\w\s\*]+?\b(b200_\w+)\s*\(", text)))
 
 
 def test_every_declared_symbol_is_exported_and_bound():
     names = declared_symbols()
-    assert len(names) >= 8
+    assert len(names) >= 30
     for name in names:
         assert hasattr(_capi.LIB, name), name
         assert name in _capi.SIGNATURES, f"{name} lacks a ctypes signature"
