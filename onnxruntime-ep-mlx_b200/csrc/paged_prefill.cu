@@ -79,12 +79,13 @@ constexpr int kSmemK = kSmemQ + kQTiles * kTileBytes;       // kKStages K tiles
 constexpr int kSmemV = kSmemK + kKStages * kTileBytes;      // kVStages V tiles
 constexpr int kSmemBytes = kSmemV + kVStages * kTileBytes;  // 224 KB
 
-// Roles: warpgroups 0-1 softmax / epilogue of q tile 0 / 1; warpgroup 2 = warp 8 TMA producer,
-// warp 9 MMA issuer, warps 10-11 idle.
+// Roles: warpgroups 0-1 softmax / epilogue of q tile 0 / 1; warpgroup 2 = warp 8 TMA producer of
+// Q and K, warp 9 MMA issuer, warp 10 TMA producer of V, warp 11 idle.
 constexpr int kThreads = 384;
 constexpr int kWgThreads = 128;
-constexpr int kProducerWarp = 8;
+constexpr int kProducerWarp = 8;   // Q and K tiles
 constexpr int kMmaWarp = 9;
+constexpr int kVProducerWarp = 10; // V tiles: its own warp, so a V stage refills as soon as it frees
 constexpr int kSoftmaxRegs = 200;  // setmaxnreg split: 2 x 128 x 200 + 128 x 96 = 63488
 constexpr int kControlRegs = 96;
 constexpr int kSplitRegs = 2 * kWgThreads * kSoftmaxRegs + kWgThreads * kControlRegs;
@@ -94,6 +95,9 @@ struct Bars {
   uint64_t q_full[kQTiles], q_empty[kQTiles];
   uint64_t k_full[kKStages], k_empty[kKStages];
   uint64_t v_full[kVStages], v_empty[kVStages];
+  // o_done[w] completes once per item of q tile w, after its last P . V (the epilogue's wait).
+  // Within an item no O wait is needed: S_w(j) is issued after PV_w(j-1) and a commit covers all
+  // earlier MMAs, so s_full[w] for tile j also says that P . V of tile j-1 has landed in O.
   uint64_t s_full[kQTiles], p_full[kQTiles], o_done[kQTiles];
   uint64_t drain;
 };
@@ -218,58 +222,66 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   if (warp >= 2 * (kWgThreads / 32)) {
     // warpgroup 2: producer, MMA issuer and two idle warps give registers to the softmax
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));
-    if (warp == kProducerWarp) {
-      // ------------------------------------------------------------------ TMA producer
-      uint32_t qc0 = 0, qc1 = 0, kc = 0, vc = 0;  // loads issued per ring (scalars: no local memory)
+    if (warp == kProducerWarp || warp == kVProducerWarp) {
+      // ------------------------------------------------------------------ TMA producers
+      // Warp 8 loads Q and K tiles, warp 10 V tiles; each ring refills as soon as its stage frees.
+      // Lane l < 16 loads box (page l / 2, channel half l & 1) of each tile; its block id is
+      // loaded one tile ahead, so the block-table read never sits between a free stage and its copy.
+      const bool is_v = warp == kVProducerWarp;
+      const int stages = is_v ? kVStages : kKStages;
+      uint64_t* full_bar = is_v ? bars.v_full : bars.k_full;
+      uint64_t* empty_bar = is_v ? bars.v_empty : bars.k_empty;
+      const CUtensorMap* map = is_v ? &maps.v_map : &maps.k_map;
+      const uint32_t ring = sbase + (is_v ? kSmemV : kSmemK);
+      uint32_t qc0 = 0, qc1 = 0, c = 0;  // Q loads per buffer, tiles loaded on this ring (scalars: no local memory)
       const int64_t oob_z = (int64_t)a.num_blocks * a.block_size;  // past the cache: zero fill
-      // lane l loads box (page (l & 15) / 2, channel half l & 1) of K (l < 16) or V (l >= 16)
-      const int page = (lane & 15) >> 1, half = lane & 1, is_v = lane >> 4;
+      const int page = (lane & 15) >> 1, half = lane & 1;
+      const bool loader = lane < 16;
       bool ok = true;
       for (int64_t it = blockIdx.x; it < n_items && ok && !failed_warp(); it += gridDim.x) {
         const Item m = decode_item(a, plan, it);
         if (m.skip) continue;
-        for (int w = 0; w < kQTiles && ok; ++w) {
-          if (nkv_of(m, w) == 0) continue;
-          uint32_t& qc = w ? qc1 : qc0;
-          if (qc > 0 && !(ok = wait_warp(&bars.q_empty[w], qc - 1))) break;
-          if (lane == 0) mbar_arrive_expect_tx(&bars.q_full[w], kTileBytes);
-          __syncwarp();
-          if (lane < 2)
-            tma_load_3d(smem + kSmemQ + w * kTileBytes + lane * kBoxBytes, &maps.q_map, &bars.q_full[w], lane * 64,
-                        m.kh * g, m.c0 + m.q0 + w * TQ);
-          ++qc;
+        if (!is_v) {
+          for (int w = 0; w < kQTiles && ok; ++w) {
+            if (nkv_of(m, w) == 0) continue;
+            const uint32_t qc = w ? qc1 : qc0;
+            if (qc > 0 && !(ok = wait_warp(&bars.q_empty[w], qc - 1))) break;
+            if (lane == 0) mbar_arrive_expect_tx(&bars.q_full[w], kTileBytes);
+            __syncwarp();
+            if (lane < 2)
+              tma_load_3d(smem + kSmemQ + w * kTileBytes + lane * kBoxBytes, &maps.q_map, &bars.q_full[w], lane * 64,
+                          m.kh * g, m.c0 + m.q0 + w * TQ);
+            if (w) qc1 = qc + 1; else qc0 = qc + 1;
+          }
         }
         const int32_t* bt = a.block_table + (int64_t)m.b * a.max_blocks;
+        auto block_of = [&](int j) -> int32_t {
+          const int pos = m.kv_lo + j * kBN + page * kTile;
+          return loader && pos < m.total ? __ldg(bt + pos / a.block_size) : -1;
+        };
+        int32_t blk_next = m.n > 0 ? block_of(0) : -1;
         for (int j = 0; j < m.n && ok; ++j) {
           const int pos0 = m.kv_lo + j * kBN + page * kTile;
-          const int32_t blk = pos0 < m.total ? __ldg(bt + pos0 / a.block_size) : -1;
+          const int32_t blk = blk_next;
+          if (j + 1 < m.n) blk_next = block_of(j + 1);  // in flight during the stage wait below
           const bool blk_ok = blk >= 0 && blk < a.num_blocks;
-          if (!is_v && pos0 < m.total && !blk_ok) set_status(a.status, kStatusBadBlock);
+          if (!is_v && loader && pos0 < m.total && !blk_ok) set_status(a.status, kStatusBadBlock);
           const int z = blk_ok ? blk * a.block_size + pos0 % a.block_size : (int)oob_z;
-          const int off = half * kBoxBytes + page * (kTile * 128);
-          // K tile j
-          const int ks = kc % kKStages;
-          if (kc >= kKStages && !(ok = wait_warp(&bars.k_empty[ks], kc / kKStages - 1))) break;
-          if (lane == 0) mbar_arrive_expect_tx(&bars.k_full[ks], kTileBytes);
+          const int st = (int)(c % (uint32_t)stages);
+          if (c >= (uint32_t)stages && !(ok = wait_warp(&empty_bar[st], c / stages - 1))) break;
+          if (lane == 0) mbar_arrive_expect_tx(&full_bar[st], kTileBytes);
           __syncwarp();
-          if (!is_v) tma_load_3d(smem + kSmemK + ks * kTileBytes + off, &maps.k_map, &bars.k_full[ks], half * 64, m.kh, z);
-          if (lane == 0) PF_TRACE(kc * 16 + 12);
-          ++kc;
-          // V tile j
-          const int vs = vc % kVStages;
-          if (vc >= kVStages && !(ok = wait_warp(&bars.v_empty[vs], vc / kVStages - 1))) break;
-          if (lane == 0) mbar_arrive_expect_tx(&bars.v_full[vs], kTileBytes);
-          __syncwarp();
-          if (is_v) tma_load_3d(smem + kSmemV + vs * kTileBytes + off, &maps.v_map, &bars.v_full[vs], half * 64, m.kh, z);
-          if (lane == 0) PF_TRACE(vc * 16 + 13);
-          ++vc;
+          if (loader)
+            tma_load_3d(smem + (ring - sbase) + st * kTileBytes + half * kBoxBytes + page * (kTile * 128), map,
+                        &full_bar[st], half * 64, m.kh, z);
+          if (lane == 0) PF_TRACE(c * 16 + (is_v ? 13 : 12));
+          ++c;
         }
       }
       // Every issued copy lands before the CTA can exit (immediate on the normal path).
       if (qc0 > 0) drain_idx(&bars.q_full[0], qc0 - 1);
       if (qc1 > 0) drain_idx(&bars.q_full[1], qc1 - 1);
-      for (uint32_t i = (kc > kKStages ? kc - kKStages : 0); i < kc; ++i) drain_idx(&bars.k_full[i % kKStages], i / kKStages);
-      for (uint32_t i = (vc > kVStages ? vc - kVStages : 0); i < vc; ++i) drain_idx(&bars.v_full[i % kVStages], i / kVStages);
+      for (uint32_t i = (c > (uint32_t)stages ? c - stages : 0); i < c; ++i) drain_idx(&full_bar[i % stages], i / stages);
     } else if (warp == kMmaWarp) {
       // ------------------------------------------------------------------ MMA issuer
       // The whole warp runs the schedule (waits, counters, descriptors stay warp-uniform and in
@@ -298,10 +310,11 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
               tc::fence_after_sync();  // P was written to tensor memory by the softmax threads
               PF_TRACE(pc * 16 + 14 + w);
               const uint32_t pbuf = tmem + w * 128, obuf = tmem + 256 + w * 128;
-              const uint32_t vb = sbase + kSmemV + (vi % kVStages) * kTileBytes;
+              // one descriptor per stage; a K step of 16 keys adds 2048 B = 128 in the address field
+              const uint64_t vdesc0 = tc::smem_desc(sbase + kSmemV + (vi % kVStages) * kTileBytes, kBoxBytes, 1024);
 #pragma unroll
               for (int kk = 0; kk < kBN / 16; ++kk) {
-                const uint64_t vdesc = tc::smem_desc(vb + kk * 2048, kBoxBytes, 1024);
+                const uint64_t vdesc = vdesc0 + (uint64_t)(kk * (2048 >> 4));
                 // P of keys 16kk..16kk+15: hi at chunk kk/2's columns (kk%2)*8.., lo 16 columns on
                 const uint32_t pcol = pbuf + (kk >> 1) * 32 + (kk & 1) * 8;
                 if (leader) {
@@ -309,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
                   tc::mma_ts(obuf, pcol + 16, vdesc, kIdPV, 1u);
                 }
               }
-              if (leader) tc::commit(&bars.o_done[w]);
+              if (leader && j == nkv_of(m, w)) tc::commit(&bars.o_done[w]);  // the item's last P . V
               PF_TRACE(pc * 16 + 2 + w);
               if (w) pc1 = pc + 1; else pc0 = pc + 1;
             }
@@ -320,12 +333,13 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
                 k_ready = true;
               }
               if (j == 0 && !(ok = wait_warp(&bars.q_full[w], w ? qc1 : qc0))) break;
-              const uint32_t kb = sbase + kSmemK + (ki % kKStages) * kTileBytes;
-              const uint32_t qb = sbase + kSmemQ + w * kTileBytes;
+              // base descriptors once; the K step's byte offset goes straight into the address field
+              const uint64_t kdesc0 = tc::smem_desc(sbase + kSmemK + (ki % kKStages) * kTileBytes, 16, 1024);
+              const uint64_t qdesc0 = tc::smem_desc(sbase + kSmemQ + w * kTileBytes, 16, 1024);
 #pragma unroll
               for (int kk = 0; kk < kD / 16; ++kk) {
                 const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-                const uint64_t qdesc = tc::smem_desc(qb + off, 16, 1024), kdesc = tc::smem_desc(kb + off, 16, 1024);
+                const uint64_t qdesc = qdesc0 + (uint64_t)(off >> 4), kdesc = kdesc0 + (uint64_t)(off >> 4);
                 if (leader) tc::mma_ss(tmem + w * 128, qdesc, kdesc, kIdQK, kk > 0);
               }
               if (leader) tc::commit(&bars.s_full[w]);
@@ -358,7 +372,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t sbuf = tmem + w * 128 + lane_off, obuf = tmem + 256 + w * 128 + lane_off;
     const float qk_scale = a.softcap > 0.f ? a.scale : a.scale * kLog2eP;
-    uint32_t t = 0;  // tiles this warpgroup has processed
+    uint32_t t = 0;      // tiles this warpgroup has processed
+    uint32_t items = 0;  // items this warpgroup has finished (o_done completions)
     for (int64_t it = blockIdx.x; it < n_items && !failed_warp(); it += gridDim.x) {
       const Item m = decode_item(a, plan, it);
       if (m.skip || nkv_of(m, w) == 0) continue;
@@ -436,9 +451,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           m_run = m_new;
         }
         if (j > 0 && __any_sync(0xffffffffu, grow && alpha != 1.0f)) {
-          // O holds tiles < j: wait for PV of tile j-1, then scale this warp's rows in place.
-          if (!(ok = wait_warp(&bars.o_done[w], t - 1))) break;
-          tc::fence_after_sync();
+          // O holds tiles < j and P . V of tile j-1 has landed (s_full of tile j, waited above, covers
+          // it): scale this warp's rows in place.
 #pragma unroll 1
           for (int c = 0; c < kD / 16; ++c) {
             float r[16];
@@ -502,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
       }
       if (!ok) break;
       // ---- epilogue: last PV done -> normalise -> store this row
-      if (!wait_warp(&bars.o_done[w], t - 1)) break;
+      if (!wait_warp(&bars.o_done[w], items++)) break;
       tc::fence_after_sync();
       float L = l_run;
       if (a.head_sink) {  // l is relative to the reference max m_run; fold the sink in that frame
