@@ -170,7 +170,8 @@ typedef struct B200PagedTensors {
 B200_API int b200_ep_node_compute_paged(B200EpNode* node, const B200PagedTensors* tensors, void* stream);
 
 /* The tensors of one GroupQueryAttention Compute: B200GqaParams with the node's attribute fields
- * ignored (the node supplies them) and workspace fields ignored (the node owns one). */
+ * (heads, scale, causal, window, softcap, smooth_softmax, do_rotary, rotary_interleaved) ignored,
+ * as the node supplies them, and the workspace fields ignored (the node owns one). */
 B200_API int b200_ep_node_compute_gqa(B200EpNode* node, const B200GqaParams* tensors, void* stream);
 
 /* sizeof the structs above as compiled into the library, for binding layout checks:

@@ -40,6 +40,7 @@ extern "C" {
 #define B200_DTYPE_UINT8 2 /* int4 cache: two +8-biased nibbles per byte */
 #define B200_DTYPE_INT8 3
 #define B200_DTYPE_INT32 6
+#define B200_DTYPE_INT64 7
 #define B200_DTYPE_FLOAT16 10
 #define B200_DTYPE_BFLOAT16 16
 #define B200_DTYPE_FLOAT8E4M3FN 17
@@ -266,6 +267,20 @@ typedef struct B200GqaParams {
   void* workspace;
   size_t workspace_bytes;
   int32_t num_sms;               /* 0 = query the device                                 */
+  /* rotary embedding of the new query and key rows (attribute do_rotary, inputs 7-9,
+   * attention.rs:538-585, :668-681): the first rotary_dim channels of every head, rotate-half
+   * or interleaved pairs, in fp32, rounded once to dtype.  Row s of batch b sits at position
+   * query_past(b) + s without position_ids; with them, at position_ids[0] + s on a first prompt
+   * (total_sequence_length == seq) and at the flattened id b * seq + s otherwise. */
+  int32_t do_rotary;
+  int32_t rotary_interleaved;
+  int32_t rotary_dim;            /* 2 * cos_cache.shape[1], <= head_size                 */
+  int32_t rotary_positions;      /* cos_cache.shape[0]                                   */
+  const void* cos_cache;         /* [rotary_positions, rotary_dim / 2] in dtype          */
+  const void* sin_cache;
+  const int64_t* position_ids;   /* device int64 [batch, position_ids_width] or NULL     */
+  const int64_t* host_position_ids; /* host copy, required with position_ids (validation) */
+  int32_t position_ids_width;
 } B200GqaParams;
 
 B200_API int b200_gqa_params_size(void);
@@ -281,9 +296,9 @@ B200_API int b200_group_query_attention(const B200GqaParams* p, void* stream);
 B200_API int b200_group_query_attention_read_status(const B200GqaParams* p, void* stream);
 
 /* Claim predicate, restating group_query_attention_claim (attention.rs:2407-2754) over a
- * plain node description, plus this build's own declines (rotary, attention_bias,
- * qk_output, sliding_window_cache, integer caches, q/k norm, head size).  Returns 1 (claim)
- * or 0 (decline, reason written to `reason`). */
+ * plain node description, plus this build's own declines (attention_bias, qk_output,
+ * sliding_window_cache, integer caches, q/k norm, head size).  Returns 1 (claim) or 0
+ * (decline, reason written to `reason`). */
 typedef struct B200GqaNodeInfo {
   int32_t num_inputs;
   int32_t num_outputs;

@@ -43,6 +43,7 @@ const char* dtype_name(int dt) {
     case B200_DTYPE_UINT8: return "uint8";
     case B200_DTYPE_INT8: return "int8";
     case B200_DTYPE_INT32: return "int32";
+    case B200_DTYPE_INT64: return "int64";
     case B200_DTYPE_FLOAT16: return "float16";
     case B200_DTYPE_BFLOAT16: return "bfloat16";
     case B200_DTYPE_FLOAT8E4M3FN: return "float8e4m3fn";
@@ -348,6 +349,19 @@ void gqa_claim(const GView& v) {
           "seqlens_k must be [batch]");
   const B200TensorInfo* tot = v.in(6);
   REQUIRE(tot && (tot->rank == 0 || (tot->rank == 1 && tot->shape[0] == 1)), "total_sequence_length must be scalar or [1]");
+  if (do_rotary) {
+    const B200TensorInfo* cos = v.in(7);
+    const B200TensorInfo* sin = v.in(8);
+    REQUIRE(cos && sin && cos->rank == 2 && same_shape(cos, sin) && cos->shape[1] > 0 && 2 * cos->shape[1] <= head,
+            "rotary caches must have matching [positions,rotary_dim/2] shapes within the head");
+  }
+  if (v.in_present(9) && do_rotary) {
+    const B200TensorInfo* pos = v.in(9);
+    REQUIRE(pos->dtype == B200_DTYPE_INT64 && pos->rank == 2 &&
+                (pos->shape[0] < 0 || q->shape[0] < 0 || pos->shape[0] == q->shape[0]) &&
+                (pos->shape[1] < 0 || q->shape[1] < 0 || pos->shape[1] >= q->shape[1]),
+            "position_ids must be int64 [batch,>=sequence_length]");
+  }
   if (v.in_present(11)) {
     const B200TensorInfo* s = v.in(11);
     REQUIRE(s->dtype == out_type && s->rank == 1 && s->shape[0] == nh, "head_sink must be [num_heads] in activation dtype");
@@ -359,7 +373,6 @@ void gqa_claim(const GView& v) {
   REQUIRE(std::isfinite(n.softcap) && n.softcap >= 0.f, "softcap must be finite and non-negative");
   // Forms the reference accepts that this build does not implement (the node stays on ORT).
   REQUIRE(!sliding, "sliding_window_cache is not implemented on B200");
-  REQUIRE(!do_rotary, "rotary embedding inside GroupQueryAttention is not implemented on B200 (apply RoPE before the node)");
   REQUIRE(!has_bias, "attention_bias is not implemented on B200");
   REQUIRE(n.qk_output == 0, "qk_output diagnostics are not implemented on B200");
   REQUIRE(!quantized && n.kv_cache_bit_width == 0, "integer GroupQueryAttention caches are not implemented on B200");

@@ -777,6 +777,67 @@ __global__ void gqa_present_kernel(const GqaArgs a, int tail_only) {
   }
 }
 
+// ------------------------------------------------------------------ rotary embedding
+// RoPE of the node's new query and key rows (do_rotary=1), written to workspace rows that the
+// attention kernels then read (attention.rs:668-681: Q and K rotated at the query rows'
+// positions before K joins present).  One CTA per (batch, query row); fp32 arithmetic, one
+// rounding to the activation type (the reference oracle's _rotate, and gqa_rope_f32).
+struct GqaRope {
+  int H, KV, D, S, new_seq, half, interleaved, rows, first_prompt;
+  int64_t q_stride, k_stride;
+  const void* q;
+  const void* k;
+  const void* cos;
+  const void* sin;
+  const int32_t* seqlens;
+  const int64_t* pos_ids;  // NULL: positions query_past + s
+  void* q_out;             // [B * S, H * D]
+  void* k_out;             // [B * new_seq, KV * D]
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) gqa_rope_kernel(const GqaRope r) {
+  const int row = blockIdx.x;  // b * S + s
+  const int b = row / r.S, s = row % r.S;
+  int64_t pos;
+  if (r.pos_ids) pos = r.first_prompt ? r.pos_ids[0] + s : r.pos_ids[(int64_t)b * r.S + s];
+  else pos = max(r.seqlens[b] + 1 - r.S, 0) + s;
+  // the host rejected out-of-range positions before the launch; clamp so no read can stray
+  pos = pos < 0 ? 0 : (pos >= r.rows ? r.rows - 1 : pos);
+  const T* crow = static_cast<const T*>(r.cos) + pos * r.half;
+  const T* srow = static_cast<const T*>(r.sin) + pos * r.half;
+  const int rot = 2 * r.half;
+  const int nheads = r.H + (s < r.new_seq ? r.KV : 0);
+  for (int i = threadIdx.x; i < nheads * r.D; i += blockDim.x) {
+    const int h = i / r.D, d = i - h * r.D;
+    const bool is_k = h >= r.H;
+    const T* src = is_k ? static_cast<const T*>(r.k) + ((int64_t)b * r.new_seq + s) * r.k_stride + (int64_t)(h - r.H) * r.D
+                        : static_cast<const T*>(r.q) + (int64_t)row * r.q_stride + (int64_t)h * r.D;
+    T* dst = is_k ? static_cast<T*>(r.k_out) + ((int64_t)b * r.new_seq + s) * ((int64_t)r.KV * r.D) + (int64_t)(h - r.H) * r.D
+                  : static_cast<T*>(r.q_out) + (int64_t)row * ((int64_t)r.H * r.D) + (int64_t)h * r.D;
+    const float x = to_f<T>(src[d]);
+    float y = x;
+    if (d < rot) {
+      int j, partner;
+      bool first;
+      if (r.interleaved) {  // pairs (2j, 2j + 1)
+        j = d >> 1;
+        partner = d ^ 1;
+        first = (d & 1) == 0;
+      } else {  // rotate-half: (j, j + half)
+        j = d < r.half ? d : d - r.half;
+        partner = d < r.half ? d + r.half : d - r.half;
+        first = d < r.half;
+      }
+      const float c = to_f<T>(crow[j]), sn = to_f<T>(srow[j]), xp = to_f<T>(src[partner]);
+      // two products and one sum, each rounded (no fused multiply-add), as the reference's
+      // element-wise ops round them: fp32 caches match bit for bit
+      y = __fadd_rn(__fmul_rn(x, c), __fmul_rn(first ? -xp : xp, sn));
+    }
+    dst[d] = from_f<T>(y);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 int gfail(int code, const std::string& msg) { return set_error(code, msg); }
 
@@ -790,8 +851,10 @@ int sm_count(const B200GqaParams* p) {
 
 struct GqaPlan {
   int rows = kMaxRows, row_tiles = 1, splits = 1, fused = 0;
-  size_t status = 0, counters = 0, part_o = 0, part_ml = 0, total = 0;
+  size_t status = 0, counters = 0, part_o = 0, part_ml = 0, q_rot = 0, k_rot = 0, total = 0;
 };
+
+size_t act_size(int dtype) { return dtype == B200_DTYPE_FLOAT ? 4 : 2; }
 
 GqaPlan gqa_plan(const B200GqaParams* p) {
   GqaPlan P;
@@ -812,6 +875,10 @@ GqaPlan gqa_plan(const B200GqaParams* p) {
     return at;
   };
   P.status = take(sizeof(int));
+  if (p->do_rotary) {  // rotated query and key rows
+    P.q_rot = take(act_size(p->dtype) * (size_t)p->batch * p->seq * p->num_heads * p->head_size);
+    P.k_rot = take(act_size(p->dtype) * (size_t)p->batch * std::max(p->new_seq, 1) * p->kv_num_heads * p->head_size);
+  }
   if (P.splits > 1) {
     P.counters = take(sizeof(int) * groups);
     P.part_o = take(sizeof(float) * groups * P.splits * P.rows * p->head_size);
@@ -854,6 +921,15 @@ int check_gqa(const B200GqaParams* p) {
     if (!ok)
       return gfail(B200_ERR_INVALID_ARGUMENT,
                    "GroupQueryAttention: tensors must be aligned to 4 elements (16 bytes for float, 8 for 16-bit)");
+  }
+  if (p->do_rotary) {
+    if (!p->cos_cache || !p->sin_cache)
+      return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: do_rotary=1 requires cos_cache and sin_cache");
+    if (p->rotary_dim <= 0 || p->rotary_dim % 2 || p->rotary_dim > p->head_size || p->rotary_positions <= 0)
+      return gfail(B200_ERR_INVALID_ARGUMENT,
+                   "rotary caches must have matching [positions,rotary_dim/2] shapes within the head");
+    if (p->position_ids && !p->host_position_ids)
+      return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: position_ids need their host copy (host_position_ids)");
   }
   // attention.rs:992-997
   if (p->new_seq != p->seq && (p->new_seq != 0 || !p->past_key))
@@ -899,6 +975,34 @@ int validate_lengths(const B200GqaParams* p) {
     return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: present capacity must be max(cap, total_sequence_length)");
   if (p->present_key && p->present_key == p->past_key && p->present_cap != p->cap)
     return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: an in-place present must have the past's capacity");
+  return B200_OK;
+}
+
+// Rotary positions (gqa_rotary_rows, attention.rs:538-585; cos_sin_row :525-536): without
+// position_ids row s of batch b sits at query_past + s; with them, a first prompt (total ==
+// seq) uses only the first id as an offset, later calls the first batch * seq flattened ids.
+int validate_rotary(const B200GqaParams* p) {
+  if (!p->do_rotary) return B200_OK;
+  const int64_t rows = p->rotary_positions, seq = p->seq;
+  if (!p->position_ids) {
+    for (int b = 0; b < p->batch; ++b) {
+      const int64_t query_past = std::max<int64_t>((int64_t)p->host_seqlens_k[b] + 1 - seq, 0);
+      if (query_past > rows - seq)
+        return gfail(B200_ERR_FAIL, "RotaryEmbedding: requested positions exceed the supplied cache");
+    }
+    return B200_OK;
+  }
+  if (p->position_ids_width < p->seq)
+    return gfail(B200_ERR_FAIL, "GroupQueryAttention: position_ids must be int64 [batch,>=sequence]");
+  const int64_t* ids = p->host_position_ids;
+  if ((int64_t)p->total_sequence_length == seq) {
+    if (ids[0] < 0 || ids[0] > rows - seq)
+      return gfail(B200_ERR_FAIL, "GroupQueryAttention: position_ids exceed the supplied cache");
+    return B200_OK;
+  }
+  for (int64_t i = 0; i < (int64_t)p->batch * seq; ++i)
+    if (ids[i] < 0 || ids[i] >= rows)
+      return gfail(B200_ERR_FAIL, "GroupQueryAttention: position_ids exceed the supplied cache");
   return B200_OK;
 }
 
@@ -1082,6 +1186,8 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
     if (rc) return rc;
     rc = validate_lengths(p);
     if (rc) return rc;
+    rc = validate_rotary(p);
+    if (rc) return rc;
     const GqaPlan P = gqa_plan(p);
     if (!p->workspace || p->workspace_bytes < P.total)
       return gfail(B200_ERR_WORKSPACE, "GroupQueryAttention: workspace missing or smaller than b200_group_query_attention_workspace_size()");
@@ -1129,6 +1235,41 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     int launches = 0;
     cudaError_t e;
+    if (p->do_rotary) {  // rotate the new rows first; the attention kernels read the rotated copies
+      GqaRope r{};
+      r.H = a.H;
+      r.KV = a.KV;
+      r.D = a.D;
+      r.S = a.S;
+      r.new_seq = a.new_seq;
+      r.half = p->rotary_dim / 2;
+      r.interleaved = p->rotary_interleaved != 0;
+      r.rows = p->rotary_positions;
+      r.first_prompt = p->total_sequence_length == p->seq;
+      r.q_stride = a.q_stride;
+      r.k_stride = a.k_stride;
+      r.q = a.q;
+      r.k = a.k;
+      r.cos = p->cos_cache;
+      r.sin = p->sin_cache;
+      r.seqlens = p->seqlens_k;
+      r.pos_ids = p->position_ids;
+      r.q_out = ws + P.q_rot;
+      r.k_out = ws + P.k_rot;
+      const dim3 grid((unsigned)(a.B * a.S));
+      if (a.dtype == B200_DTYPE_FLOAT) gqa_rope_kernel<float><<<grid, 256, 0, stream>>>(r);
+      else if (a.dtype == B200_DTYPE_FLOAT16) gqa_rope_kernel<__half><<<grid, 256, 0, stream>>>(r);
+      else gqa_rope_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(r);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return gfail(B200_ERR_CUDA, std::string("GroupQueryAttention: CUDA error: ") + cudaGetErrorString(e));
+      add_launches(1);
+      a.q = r.q_out;
+      a.q_stride = (int64_t)a.H * a.D;
+      if (a.new_seq > 0) {
+        a.k = r.k_out;
+        a.k_stride = (int64_t)a.KV * a.D;
+      }
+    }
     // Rows past some batch's length exist in present only when a length is below its capacity.
     bool tail_rows = false;
     for (int b = 0; b < p->batch; ++b) tail_rows |= p->host_seqlens_k[b] + 1 < a.pcap;

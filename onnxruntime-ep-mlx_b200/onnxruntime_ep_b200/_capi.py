@@ -24,6 +24,7 @@ DTYPE_FLOAT = 1
 DTYPE_UINT8 = 2
 DTYPE_INT8 = 3
 DTYPE_INT32 = 6
+DTYPE_INT64 = 7
 DTYPE_FLOAT16 = 10
 DTYPE_BFLOAT16 = 16
 DTYPE_FLOAT8E4M3FN = 17
@@ -93,6 +94,9 @@ class GqaParams(ctypes.Structure):
         ("present_key", _vp), ("present_value", _vp), ("seqlens_k", _vp), ("host_seqlens_k", _vp),
         ("head_sink", _vp), ("output", _vp), ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("num_sms", _i32),
+        ("do_rotary", _i32), ("rotary_interleaved", _i32), ("rotary_dim", _i32), ("rotary_positions", _i32),
+        ("cos_cache", _vp), ("sin_cache", _vp), ("position_ids", _vp), ("host_position_ids", _vp),
+        ("position_ids_width", _i32),
     ]
 
 

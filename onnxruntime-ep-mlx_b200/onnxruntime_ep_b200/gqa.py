@@ -41,8 +41,13 @@ def _workspace(device, nbytes):
 def build_params(query, key, value, past_key, past_value, seqlens_k, total_sequence_length,
                  head_sink=None, *, num_heads, kv_num_heads, scale=0.0, causal=1,
                  local_window_size=-1, softcap=0.0, smooth_softmax=-1, present_key=None,
-                 present_value=None, with_present=True, host_seqlens_k=None, output=None):
-    """Fill a ``B200GqaParams``.  Returns ``(params, keepalive, output, present_key, present_value)``."""
+                 present_value=None, with_present=True, host_seqlens_k=None, output=None,
+                 do_rotary=0, rotary_interleaved=0, cos_cache=None, sin_cache=None, position_ids=None):
+    """Fill a ``B200GqaParams``.  Returns ``(params, keepalive, output, present_key, present_value)``.
+
+    ``do_rotary=1`` takes ``cos_cache``/``sin_cache`` ``[positions, rotary_dim/2]`` (inputs 7 and
+    8) and optionally ``position_ids`` int64 ``[batch, >=seq]`` (input 9; a host copy is made for
+    the reference's bounds checks)."""
     H, KV = int(num_heads), int(kv_num_heads)
     packed = key is None and value is None  # packed QKV in query (inputs 1 and 2 absent)
     B, S = int(query.shape[0]), int(query.shape[1])
@@ -95,12 +100,29 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
     p.host_seqlens_k = host_seqlens_k.ctypes.data_as(ctypes.c_void_p)
     p.head_sink = _ptr(head_sink)
     p.output = _ptr(output)
+    host_ids = None
+    if do_rotary:
+        p.do_rotary = 1
+        p.rotary_interleaved = int(rotary_interleaved)
+        p.rotary_dim = int(cos_cache.shape[1]) * 2
+        p.rotary_positions = int(cos_cache.shape[0])
+        p.cos_cache, p.sin_cache = _ptr(cos_cache), _ptr(sin_cache)
+        if position_ids is not None:
+            ids = torch.as_tensor(position_ids)
+            host_ids = np.ascontiguousarray(ids.detach().to("cpu", torch.int64).numpy())
+            if ids.device.type != "cuda":
+                ids = ids.to(dev)
+            position_ids = ids.contiguous()
+            p.position_ids = _ptr(position_ids)
+            p.host_position_ids = host_ids.ctypes.data_as(ctypes.c_void_p)
+            p.position_ids_width = int(host_ids.shape[1]) if host_ids.ndim == 2 else int(host_ids.size)
     nbytes = ctypes.c_size_t(0)
     check(LIB.b200_group_query_attention_workspace_size(ctypes.byref(p), ctypes.byref(nbytes)))
     ws = _workspace(dev, nbytes.value)
     p.workspace = _ptr(ws)
     p.workspace_bytes = ws.numel()
-    keep = (query, key, value, past_key, past_value, seqlens_k, head_sink, host_seqlens_k, ws)
+    keep = (query, key, value, past_key, past_value, seqlens_k, head_sink, host_seqlens_k, ws, cos_cache, sin_cache,
+            position_ids, host_ids)
     return p, keep, output, present_key, present_value
 
 

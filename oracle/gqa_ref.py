@@ -15,7 +15,9 @@ Semantics:
   ``[start, end)`` with ``end = min(past + i + 1, length)`` (causal) or ``length``, and
   ``start = max(0, end - window)`` for ``window > 0``; scores in fp32; softcap
   ``cap * tanh(s / cap)``; a sink joins only the softmax denominator;
-* ``smooth_softmax == 1`` is a zero sink in every head (attention.rs:1311-1312).
+* ``smooth_softmax == 1`` is a zero sink in every head (attention.rs:1311-1312);
+* rotary embedding of the new query / key rows before K joins present, positions as
+  gqa_rotary_rows (attention.rs:538-585) and the oracle's ``_rotate`` (:71-85).
 
 Parity pinning: ``tests/golden/make_gqa_golden.py`` runs the reference's ``_reference`` on
 seeded inputs and commits its outputs (``gqa_golden.npz``); ``tests/test_gqa_oracle.py``
@@ -27,14 +29,48 @@ from __future__ import annotations
 import numpy as np
 
 
+def rotate(x, cos, sin, positions, interleaved):
+    """Rotary embedding of ``x [heads, seq, D]`` at ``positions [seq]`` over the first
+    ``2 * cos.shape[1]`` channels, in fp32, rounded back to ``x.dtype``
+    (tests/ops/test_gqa_position_cache.py:71-85)."""
+    half = cos.shape[1]
+    part = x[..., :2 * half].astype(np.float32)
+    c, s = cos[positions].astype(np.float32), sin[positions].astype(np.float32)
+    if interleaved:
+        partner = np.empty_like(part)
+        partner[..., 0::2], partner[..., 1::2] = -part[..., 1::2], part[..., 0::2]
+        c, s = np.repeat(c, 2, -1), np.repeat(s, 2, -1)
+    else:
+        partner = np.concatenate([-part[..., half:], part[..., :half]], -1)
+        c, s = np.tile(c, (1, 2)), np.tile(s, (1, 2))
+    out = x.copy()
+    out[..., :2 * half] = (part * c[None] + partner * s[None]).astype(x.dtype)
+    return out
+
+
+def rotary_positions(b, seq, query_past, total, position_ids):
+    """Positions of batch row ``b``'s query rows (attention.rs:538-585): ``query_past + s``
+    without ids; with ids, the first id as an offset on a first prompt (``total == seq``),
+    else the flattened ids ``b * seq .. b * seq + seq``."""
+    if position_ids is None:
+        return query_past + np.arange(seq)
+    ids = np.asarray(position_ids).reshape(-1)
+    if total == seq:
+        return int(ids[0]) + np.arange(seq)
+    return ids[b * seq:(b + 1) * seq]
+
+
 def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_heads, kv_num_heads,
                           scale=None, causal=True, window=-1, softcap=0.0, sink=None,
-                          smooth_softmax=-1):
+                          smooth_softmax=-1, cos=None, sin=None, position_ids=None, interleaved=False,
+                          out_dtype=None):
     """Returns ``(output [B,S,H*D], present_k, present_v [B,KV,max(cap,total),D])``.
 
     ``q`` [B,S,H*D]; ``k``/``v`` [B,new_seq,KV*D] (new_seq may be 0); ``past_k``/``past_v``
-    [B,KV,cap,D] or None.  Arrays keep their dtype; math is fp32, the output is rounded to
-    the activation dtype."""
+    [B,KV,cap,D] or None; ``cos``/``sin`` [positions, rotary_dim/2] turn on the rotary
+    embedding of the new query and key rows (``position_ids`` [B, >=S] optional).  Arrays keep
+    their dtype; math is fp32, the output is rounded to the activation dtype (or kept in
+    ``out_dtype``, e.g. fp32 for tolerance checks)."""
     B, S, hidden = q.shape
     H, KV = int(num_heads), int(kv_num_heads)
     D = hidden // H
@@ -47,7 +83,7 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
     scale = 1.0 / np.sqrt(D) if not scale else float(scale)
     pk = np.zeros((B, KV, pcap, D), dt)
     pv = np.zeros((B, KV, pcap, D), dt)
-    out = np.empty((B, S, H * D), dt)
+    out = np.empty((B, S, H * D), out_dtype or dt)
     if sink is None and smooth_softmax == 1:
         sink = np.zeros(H, np.float32)
     for b in range(B):
@@ -61,12 +97,19 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
             if length < cap:
                 pk[b, :, length:cap] = past_k[b, :, length:cap]
                 pv[b, :, length:cap] = past_v[b, :, length:cap]
+        kb = None if not new_seq else k[b].reshape(new_seq, KV, D).transpose(1, 0, 2)  # [KV, new_seq, D]
+        qb = q[b].reshape(S, H, D).transpose(1, 0, 2)                                      # [H, S, D]
+        if cos is not None:
+            ids = rotary_positions(b, S, query_past, total, position_ids)
+            qb = rotate(qb, cos, sin, ids, interleaved)
+            if new_seq:
+                kb = rotate(kb, cos, sin, ids, interleaved)
         if rows:
-            pk[b, :, past:length] = k[b, :rows].reshape(rows, KV, D).transpose(1, 0, 2)
+            pk[b, :, past:length] = kb[:, :rows]
             pv[b, :, past:length] = v[b, :rows].reshape(rows, KV, D).transpose(1, 0, 2)
         keys = np.repeat(pk[b, :, :length].astype(np.float32), g, 0)   # [H, length, D]
         vals = np.repeat(pv[b, :, :length].astype(np.float32), g, 0)
-        qh = q[b].reshape(S, H, D).transpose(1, 0, 2).astype(np.float32)  # [H, S, D]
+        qh = qb.astype(np.float32)  # [H, S, D]
         scores = qh @ keys.transpose(0, 2, 1) * np.float32(scale)
         if softcap > 0:
             scores = softcap * np.tanh(scores / softcap)
@@ -80,5 +123,5 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
             logits = np.concatenate([logits, np.broadcast_to(s, (H, S, 1))], -1)
         e = np.exp(logits - logits.max(-1, keepdims=True))
         probs = (e / e.sum(-1, keepdims=True))[..., :length]
-        out[b] = (probs @ vals).transpose(1, 0, 2).reshape(S, H * D).astype(dt)
+        out[b] = (probs @ vals).transpose(1, 0, 2).reshape(S, H * D).astype(out.dtype)
     return out, pk, pv

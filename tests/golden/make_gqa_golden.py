@@ -4,8 +4,9 @@ Usage (build container only; the reference checkout does not travel to GPU boxes
 
     python tests/golden/make_gqa_golden.py --reference <path to the reference checkout>
 
-``_reference`` (tests/ops/test_gqa_position_cache.py:88-134, pinned there to ORT v1.31.0) is
-taken from the test file with ``ast`` and executed in a private namespace holding ``numpy``;
+``_reference`` (tests/ops/test_gqa_position_cache.py:88-134, pinned there to ORT v1.31.0) and
+its ``_rotate`` (:71-85) are taken from the test file with ``ast`` and executed in a private
+namespace holding ``numpy``;
 the test module itself imports onnx helpers that are absent here.  Its geometry is fixed at
 4 q heads, 2 kv heads, head size 32, scale 1/sqrt(32); composed cases use softcap 0.7 and the
 feed ``sink``.  Inputs are seeded numpy (``default_rng(365 + case index)``) and stored with
@@ -40,6 +41,28 @@ CASES = [
 ]
 HEADS, KV, HEAD = 4, 2, 32
 
+# rotary cases (the reference oracle's cos / sin / pos paths, test_gqa_position_cache.py:71-104):
+# name -> (half, interleaved, position ids or None).  A first prompt (total == seq) uses only the
+# first id as an offset; later calls the first batch * seq flattened ids.
+ROTARY = {
+    "rot_prefill_first": (16, False, [[2, 7, 7, 7]]),
+    "rot_decode_ids": (16, False, [[5, 9], [6, 8]]),
+    "rot_no_ids": (16, False, None),
+    "rot_interleaved_partial": (8, True, [[3, 4, 5]]),
+    "rot_partial_ids": (8, False, [[1, 2, 3], [4, 5, 6]]),
+    "rot_fp16": (16, True, None),
+    "rot_past_only": (16, False, [[4], [5]]),
+}
+CASES += [
+    ("rot_prefill_first", "float32", 1, 3, 3, 8, [3], 3, True, -1, False),
+    ("rot_decode_ids", "float32", 2, 1, 1, 8, [5, 7], 7, True, -1, False),
+    ("rot_no_ids", "float32", 2, 2, 2, 8, [4, 6], 6, True, -1, False),
+    ("rot_interleaved_partial", "float32", 1, 2, 2, 6, [5], 5, True, -1, False),
+    ("rot_partial_ids", "float32", 2, 2, 2, 8, [5, 8], 8, True, 3, False),
+    ("rot_fp16", "float16", 2, 2, 2, 8, [6, 8], 8, True, -1, True),
+    ("rot_past_only", "float32", 2, 1, 0, 6, [4, 6], 6, True, -1, False),
+]
+
 
 def load_reference(path):
     with open(path) as f:
@@ -69,6 +92,16 @@ def make_feeds(index, dtype, batch, seq, new_seq, cap, lengths, total, composed)
     return feeds
 
 
+def add_rotary(feeds, index, half, ids, dtype):
+    rng = np.random.default_rng(1365 + index)
+    dt = np.dtype(dtype)
+    feeds["cos"] = rng.uniform(0.5, 1.5, (64, half)).astype(dt)
+    feeds["sin"] = rng.uniform(-0.5, 0.5, (64, half)).astype(dt)
+    if ids is not None:
+        feeds["pos"] = np.asarray(ids, np.int64)
+    return feeds
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
@@ -77,14 +110,19 @@ def main():
     arrays, meta = {}, []
     for i, (name, dtype, batch, seq, new_seq, cap, lengths, total, causal, window, composed) in enumerate(CASES):
         feeds = make_feeds(i, dtype, batch, seq, new_seq, cap, lengths, total, composed)
-        out, pk, pv = ref(feeds, causal=causal, window=window, composed=composed)
+        interleaved = False
+        if name in ROTARY:
+            half, interleaved, ids = ROTARY[name]
+            add_rotary(feeds, i, half, ids, dtype)
+        out, pk, pv = ref(feeds, causal=causal, window=window, composed=composed, interleaved=interleaved)
         for key, val in feeds.items():
             arrays[f"{name}/in/{key}"] = val
         arrays[f"{name}/out/output"] = out
         arrays[f"{name}/out/present_k"] = pk
         arrays[f"{name}/out/present_v"] = pv
         meta.append(dict(name=name, dtype=dtype, batch=batch, seq=seq, new_seq=new_seq, cap=cap,
-                         total=total, causal=causal, window=window, composed=composed))
+                         total=total, causal=causal, window=window, composed=composed,
+                         interleaved=bool(interleaved)))
     arrays["meta"] = np.frombuffer(json.dumps(meta).encode(), np.uint8)
     np.savez_compressed(os.path.join(HERE, "gqa_golden.npz"), **arrays)
     print(f"wrote {len(meta)} cases to gqa_golden.npz")

@@ -102,10 +102,38 @@ def test_reference_declines(mutate, reason):
     assert ok == 0 and why.startswith(reason), why
 
 
+def rotary(n, half=64, rows=4096, dt=F32, pos=None):
+    n.num_inputs = 10 if pos is not None else 9
+    n.do_rotary = 1
+    tensor(n.inputs[7], dt, [rows, half])
+    tensor(n.inputs[8], dt, [rows, half])
+    if pos is not None:
+        tensor(n.inputs[9], pos[0], pos[1])
+    return n
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(half=32), dict(pos=(_capi.DTYPE_INT64, [1, 1])),
+                                dict(pos=(_capi.DTYPE_INT64, [1, 5]))])
+def test_rotary_nodes_are_claimed(kw):
+    assert claim(rotary(gnode(), **kw)) == (1, "")
+
+
 @pytest.mark.parametrize("mutate,reason", [
-    (lambda n: (setattr(n, "num_inputs", 9), setattr(n, "do_rotary", 1),
-                tensor(n.inputs[7], F32, [4096, 64]), tensor(n.inputs[8], F32, [4096, 64])),
-     "rotary embedding inside GroupQueryAttention is not implemented on B200"),
+    (lambda n: rotary(n, half=65), "rotary caches must have matching [positions,rotary_dim/2] shapes within the head"),
+    (lambda n: (rotary(n), tensor(n.inputs[8], F32, [2048, 64])),
+     "rotary caches must have matching [positions,rotary_dim/2] shapes"),
+    (lambda n: rotary(n, pos=(I32, [1, 1])), "position_ids must be int64 [batch,>=sequence_length]"),
+    (lambda n: rotary(n, pos=(_capi.DTYPE_INT64, [2, 1])), "position_ids must be int64 [batch,>=sequence_length]"),
+    (lambda n: rotary(n, dt=F16), "input 7 must have output dtype float32, got float16"),
+])
+def test_reference_rotary_declines(mutate, reason):
+    n = gnode()
+    mutate(n)
+    ok, why = claim(n)
+    assert ok == 0 and why.startswith(reason), why
+
+
+@pytest.mark.parametrize("mutate,reason", [
     (lambda n: (setattr(n, "num_inputs", 11), tensor(n.inputs[10], F32, [1, 1, 1, 2049])),
      "attention_bias is not implemented on B200"),
     (lambda n: (tensor(n.inputs[3], I8, [1, 8, 2048, 128]), tensor(n.inputs[4], I8, [1, 8, 2048, 128]),
@@ -168,3 +196,51 @@ def test_workspace_size_is_shape_only():
     n = ctypes.c_size_t(0)
     assert _capi.LIB.b200_group_query_attention_workspace_size(ctypes.byref(p), ctypes.byref(n)) == 0
     assert n.value >= 256
+
+
+# ---- rotary positions, checked on the host before any launch (attention.rs:525-585) ----------
+def rotary_params(lengths, total, S, rows=64, ids=None, width=None):
+    """`lengths` are seqlens_k values (length - 1), as in ``params``."""
+    p, host = params(lengths, total, S=S, new_seq=S, cap=64)
+    keep = [host]
+    cos = ctypes.c_void_p(0x3000)
+    p.do_rotary, p.rotary_dim, p.rotary_positions = 1, 64, rows
+    p.cos_cache = p.sin_cache = cos
+    if ids is not None:
+        ids = np.ascontiguousarray(ids, np.int64)
+        keep.append(ids)
+        p.position_ids = ctypes.c_void_p(0x4000)
+        p.host_position_ids = ids.ctypes.data
+        p.position_ids_width = ids.shape[1] if width is None else width
+    return p, keep
+
+
+def gqa_call(p):
+    return _capi.LIB.b200_group_query_attention(ctypes.byref(p), None)
+
+
+def test_rotary_positions_past_the_cache_without_ids():
+    p, keep = rotary_params([63], 64, S=1, rows=63)  # length 64: query_past 63 needs 64 rows
+    assert gqa_call(p) == _capi.B200_ERR_FAIL
+    assert "RotaryEmbedding: requested positions exceed the supplied cache" in _capi.LIB.b200_last_error().decode()
+
+
+@pytest.mark.parametrize("bad", [-1, 64, 2**32, 2**63 - 1])
+def test_rotary_position_ids_out_of_range(bad):
+    # later call: the first batch * seq flattened ids must all be inside the cache
+    p, keep = rotary_params([4, 5], 6, S=2, ids=[[1, bad], [2, 3]])
+    assert gqa_call(p) == _capi.B200_ERR_FAIL
+    assert "position_ids exceed the supplied cache" in _capi.LIB.b200_last_error().decode()
+
+
+def test_rotary_first_prompt_offset_span():
+    # total == seq: only the first id counts, and offset + seq must stay inside the cache
+    p, keep = rotary_params([2], 3, S=3, ids=[[62, 0, 0]])
+    assert gqa_call(p) == _capi.B200_ERR_FAIL
+    assert "position_ids exceed the supplied cache" in _capi.LIB.b200_last_error().decode()
+
+
+def test_rotary_position_ids_too_narrow():
+    p, keep = rotary_params([4, 5], 6, S=2, ids=[[1], [2]])
+    assert gqa_call(p) == _capi.B200_ERR_FAIL
+    assert "position_ids must be int64 [batch,>=sequence]" in _capi.LIB.b200_last_error().decode()

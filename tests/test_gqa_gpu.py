@@ -68,6 +68,9 @@ def test_golden_cases(case, in_place):
     sink = dev(f["sink"]) if "sink" in f else None
     if in_place:
         kw.update(present_key=pk, present_value=pv)
+    if "cos" in f:  # rotary: cos / sin caches, optional position ids (host copy for validation)
+        kw.update(do_rotary=1, rotary_interleaved=int(case.get("interleaved", False)), cos_cache=dev(f["cos"]),
+                  sin_cache=dev(f["sin"]), position_ids=f.get("pos"))
     out, ok, ov = gqa.group_query_attention(q, k, v, pk, pv, lengths, int(f["total"][0]), sink, check_status=True, **kw)
     torch.cuda.synchronize()
     check(host(out), GOLDEN[f"{name}/out/output"], case["dtype"])
@@ -77,7 +80,7 @@ def test_golden_cases(case, in_place):
 
 def run_case(rng, *, dtype="bfloat16", B=1, S=1, H=32, KV=8, D=128, cap=2048, lengths=None, total=None,
              causal=1, window=-1, softcap=0.0, sink=False, smooth=-1, packed=False, new_rows=True, past=True,
-             in_place=False):
+             in_place=False, rotary=None):
     npdt = np.float32
     lengths = [cap + S] * B if lengths is None else lengths
     B = len(lengths)
@@ -95,13 +98,31 @@ def run_case(rng, *, dtype="bfloat16", B=1, S=1, H=32, KV=8, D=128, cap=2048, le
     qt, kt, vt, pkt, pvt, skt = map(to, (q, k, v, pkn, pvn, sk))
     back = lambda t: None if t is None else t.float().cpu().numpy()
     qn, kn, vn, pkr, pvr, skr = map(back, (qt, kt, vt, pkt, pvt, skt))
+    rot = {}
+    kw_rot = {}
+    if rotary is not None:  # (half, interleaved, position ids or None), cos / sin in the activation type
+        half, inter, ids = rotary
+        rows = max(lengths) + 8
+        cos = rng.uniform(0.5, 1.5, (rows, half)).astype(npdt)
+        sin = rng.uniform(-0.5, 0.5, (rows, half)).astype(npdt)
+        ct, st = to(cos), to(sin)
+        rot = dict(cos=back(ct), sin=back(st), position_ids=ids, interleaved=inter)
+        kw_rot = dict(do_rotary=1, rotary_interleaved=int(inter), cos_cache=ct, sin_cache=st, position_ids=ids)
+        if dtype != "float32":
+            # the oracle sees the activation type, so its rotated rows are rounded like the kernel's
+            import ml_dtypes
+            ndt = np.float16 if dtype == "float16" else ml_dtypes.bfloat16
+            cast = lambda a: None if a is None else a.astype(ndt)
+            qn, kn, vn, pkr, pvr, skr = map(cast, (qn, kn, vn, pkr, pvr, skr))
+            rot.update(cos=cast(rot["cos"]), sin=cast(rot["sin"]))
     want, wk, wv = gqa_ref.group_query_attention(
         qn, kn if new_rows else None, vn if new_rows else None, pkr, pvr, np.asarray(lengths) - 1, total,
         num_heads=H, kv_num_heads=KV, causal=bool(causal), window=window, softcap=softcap, sink=skr,
-        smooth_softmax=smooth)
+        smooth_softmax=smooth, out_dtype=np.float32, **rot)
+    want, wk, wv = (np.asarray(x, np.float32) for x in (want, wk, wv))
     lens = torch.tensor(np.asarray(lengths) - 1, dtype=torch.int32, device=DEV)
     kw = dict(num_heads=H, kv_num_heads=KV, causal=causal, local_window_size=window, softcap=softcap,
-              smooth_softmax=smooth)
+              smooth_softmax=smooth, **kw_rot)
     if in_place:
         kw.update(present_key=pkt, present_value=pvt)
     if packed:
@@ -167,3 +188,30 @@ def test_past_only_decode():
 
 def test_in_place_shared_buffer():
     run_case(np.random.default_rng(15), S=2, cap=1024, lengths=[600, 1000], in_place=True)
+
+
+# ---- rotary embedding inside the node (do_rotary=1) ------------------------------------------
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_config1_with_rotary(dtype):
+    """Config-1 shapes with RoPE on the new rows at position query_past (no position_ids)."""
+    run_case(np.random.default_rng(21), dtype=dtype, cap=2048, lengths=[2049], rotary=(64, False, None))
+
+
+@pytest.mark.parametrize("half,inter", [(64, False), (64, True), (32, False), (16, True)])
+def test_rotary_forms_with_position_ids(half, inter):
+    ids = np.array([[40], [77]], np.int64)  # later call: the first batch * seq flattened ids
+    run_case(np.random.default_rng(22 + half), dtype="float16", H=16, KV=4, cap=300, lengths=[301, 120],
+             rotary=(half, inter, ids))
+
+
+def test_rotary_first_prompt_offset_and_packed():
+    # total == seq: only the first id is used, as an offset for every batch row
+    ids = np.array([[3, 99, 99, 99, 99, 99, 99, 99]], np.int64)
+    run_case(np.random.default_rng(23), S=8, cap=0, past=False, lengths=[8], total=8, H=8, KV=2, packed=True,
+             rotary=(64, False, ids))
+
+
+def test_rotary_prefill_rows_and_past_only():
+    run_case(np.random.default_rng(24), S=40, cap=64, lengths=[104, 45], H=8, KV=2, rotary=(32, True, None))
+    run_case(np.random.default_rng(25), S=1, cap=500, lengths=[500, 321], new_rows=False,
+             rotary=(64, False, np.array([[499], [320]], np.int64)))
