@@ -181,6 +181,22 @@ B200_API size_t b200_ep_struct_size(int32_t which);
 /* Bytes of device workspace the node currently holds, and computes run so far. */
 B200_API int b200_ep_node_stats(const B200EpNode* node, uint64_t* workspace_bytes, uint64_t* computes);
 
+/* ---- device memory, copies and streams for the ORT glue ---------------------------------------
+ * What the EP's OrtAllocator, OrtDataTransferImpl and Compute need from CUDA, so the glue itself
+ * is compiled against ONNX Runtime's headers alone (the reference's allocator and transfer are
+ * rust/src/device.rs:409-640).  `device` is the CUDA ordinal. */
+B200_API int b200_ep_device_alloc(int32_t device, size_t bytes, void** out);
+B200_API int b200_ep_device_free(int32_t device, void* ptr);
+/* Copy `bytes` between any two of host and device memory (the direction is read from the
+ * pointers).  stream NULL: synchronous; otherwise ordered on `stream`. */
+B200_API int b200_ep_copy(int32_t device, void* dst, const void* src, size_t bytes, void* stream);
+/* *out = 1 when the kernels can read `ptr` directly (device or managed memory), else 0. */
+B200_API int b200_ep_is_device_pointer(const void* ptr, int32_t* out);
+/* A non-blocking stream on `device`; synchronise; destroy (NULL is a no-op). */
+B200_API int b200_ep_stream_create(int32_t device, void** stream);
+B200_API int b200_ep_stream_sync(void* stream);
+B200_API int b200_ep_stream_destroy(int32_t device, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -608,3 +608,80 @@ int b200_ep_node_compute_gqa(B200EpNode* n, const B200GqaParams* t, void* stream
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// device memory, copies and streams for the ORT glue
+// ---------------------------------------------------------------------------------------------
+extern "C" {
+
+int b200_ep_device_alloc(int32_t device, size_t bytes, void** out) {
+  if (!out) return fail(B200_ERR_INVALID_ARGUMENT, "B200 allocator: null output");
+  *out = nullptr;
+  DeviceScope scope(device);
+  if (scope.err != cudaSuccess) return cuda_fail(scope.err, "B200 allocator: cudaSetDevice");
+  if (bytes == 0) return B200_OK;
+  cudaError_t e = cudaMalloc(out, bytes);
+  if (e != cudaSuccess) {
+    *out = nullptr;
+    return cuda_fail(e, "B200 allocator: cudaMalloc of " + std::to_string(bytes) + " bytes");
+  }
+  return B200_OK;
+}
+
+int b200_ep_device_free(int32_t device, void* ptr) {
+  if (!ptr) return B200_OK;
+  DeviceScope scope(device);
+  if (scope.err != cudaSuccess) return cuda_fail(scope.err, "B200 allocator: cudaSetDevice");
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? B200_OK : cuda_fail(e, "B200 allocator: cudaFree");
+}
+
+int b200_ep_copy(int32_t device, void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return B200_OK;
+  if (!dst || !src) return fail(B200_ERR_INVALID_ARGUMENT, "B200 copy: null pointer");
+  DeviceScope scope(device);
+  if (scope.err != cudaSuccess) return cuda_fail(scope.err, "B200 copy: cudaSetDevice");
+  cudaError_t e = stream ? cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream))
+                         : cudaMemcpy(dst, src, bytes, cudaMemcpyDefault);
+  return e == cudaSuccess ? B200_OK : cuda_fail(e, "B200 copy of " + std::to_string(bytes) + " bytes");
+}
+
+int b200_ep_is_device_pointer(const void* ptr, int32_t* out) {
+  if (!out) return fail(B200_ERR_INVALID_ARGUMENT, "B200: null output");
+  *out = 0;
+  if (!ptr) return B200_OK;
+  cudaPointerAttributes attr{};
+  cudaError_t e = cudaPointerGetAttributes(&attr, ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // plain host memory on old runtimes; not sticky
+    return B200_OK;
+  }
+  *out = attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
+  return B200_OK;
+}
+
+int b200_ep_stream_create(int32_t device, void** stream) {
+  if (!stream) return fail(B200_ERR_INVALID_ARGUMENT, "B200: null output");
+  *stream = nullptr;
+  DeviceScope scope(device);
+  if (scope.err != cudaSuccess) return cuda_fail(scope.err, "B200 stream: cudaSetDevice");
+  cudaStream_t s = nullptr;
+  cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  if (e != cudaSuccess) return cuda_fail(e, "B200 stream: cudaStreamCreateWithFlags");
+  *stream = s;
+  return B200_OK;
+}
+
+int b200_ep_stream_sync(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? B200_OK : cuda_fail(e, "B200 stream: cudaStreamSynchronize");
+}
+
+int b200_ep_stream_destroy(int32_t device, void* stream) {
+  if (!stream) return B200_OK;
+  DeviceScope scope(device);
+  cudaError_t e = cudaStreamDestroy(static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? B200_OK : cuda_fail(e, "B200 stream: cudaStreamDestroy");
+}
+
+}  // extern "C"

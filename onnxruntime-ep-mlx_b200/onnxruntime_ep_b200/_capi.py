@@ -200,6 +200,13 @@ SIGNATURES = {
     "b200_ep_node_compute_paged": (ctypes.c_int, [_vp, ctypes.POINTER(PagedTensors), _vp]),
     "b200_ep_node_compute_gqa": (ctypes.c_int, [_vp, ctypes.POINTER(GqaParams), _vp]),
     "b200_ep_node_stats": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
+    "b200_ep_device_alloc": (ctypes.c_int, [_i32, ctypes.c_size_t, ctypes.POINTER(_vp)]),
+    "b200_ep_device_free": (ctypes.c_int, [_i32, _vp]),
+    "b200_ep_copy": (ctypes.c_int, [_i32, _vp, _vp, ctypes.c_size_t, _vp]),
+    "b200_ep_is_device_pointer": (ctypes.c_int, [_vp, ctypes.POINTER(_i32)]),
+    "b200_ep_stream_create": (ctypes.c_int, [_i32, ctypes.POINTER(_vp)]),
+    "b200_ep_stream_sync": (ctypes.c_int, [_vp]),
+    "b200_ep_stream_destroy": (ctypes.c_int, [_i32, _vp]),
 }
 
 
