@@ -178,8 +178,10 @@ def test_gqa_compute_config1_shapes(ep, seqlens_on_device):
         for k, v in dev.items():
             _bind(ctx, f"gqa.{k}", v, oh.F32)
         meta = dict(seqlens_k=lens.copy(), total=total.copy())
+        if seqlens_on_device:
+            meta = {k: to_dev(v) for k, v in meta.items()}  # kept alive until Compute has run
         for k, v in meta.items():
-            _bind(ctx, f"gqa.{k}", to_dev(v) if seqlens_on_device else v, oh.I32)
+            _bind(ctx, f"gqa.{k}", v, oh.I32)
         out = torch.empty((1, 1, Hg * Dg), device="cuda")
         pk = torch.empty((1, KVg, cap, Dg), device="cuda")
         pv = torch.empty_like(pk)
