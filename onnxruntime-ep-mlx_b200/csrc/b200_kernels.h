@@ -79,6 +79,7 @@ struct AttnArgs {
   // means every sequence runs on the generic kernel.
   int* route;
   int decode_on;   // decode kernel enabled for this call (shape supported)
+  int decode_tile; // tokens per decode tile: kTile, or 2 * kTile for fp8 caches
   int prefill_tq;  // query tokens per prefill work item (2 x 128 rows / group) or 0 = prefill kernel off
 };
 
@@ -86,6 +87,11 @@ enum Route : int { kRouteDecode = 0, kRoutePrefill = 1, kRouteGeneric = 2 };
 
 constexpr int kDecodeRows = 8;   // q rows (query x head-in-group) one decode unit covers
 constexpr int kTile = 16;        // tokens per decode tile (one mma M tile)
+// Half-tiles of kTile tokens per fp8 decode tile (1 or 2).  Two halve the per-tile fixed costs
+// but double the shared memory of a stage; on B200 both settle near 0.61-0.64 of HBM on
+// config 5 (the kernel is bound by dependent-latency chains at 8-12 resident warps per SM), and
+// one with two stages was the best measured.
+constexpr int kFp8HalfTiles = 1;
 
 cudaError_t launch_generic(const AttnArgs& a, cudaStream_t stream);
 

@@ -529,6 +529,7 @@ int b200_paged_attention(const B200PagedAttentionParams* p, void* stream_ptr) {
       plan.pf_total = reinterpret_cast<int64_t*>(ws + L.pf_total);
       a.route = reinterpret_cast<int*>(ws + L.route);
       a.decode_on = L.fast_decode;
+      a.decode_tile = p->cache_dtype == B200_DTYPE_FLOAT8E4M3FN ? b200::kFp8HalfTiles * b200::kTile : b200::kTile;
       a.prefill_tq = L.fast_prefill ? b200::prefill_tokens_per_item(group) : 0;
       if ((rc = encode_cache_map(&maps.k_map, p->key_cache, p))) return rc;
       if ((rc = encode_cache_map(&maps.v_map, p->value_cache, p))) return rc;

@@ -22,8 +22,10 @@
 //    mma.m16n8k16 (K from ldmatrix, Q fragments in registers), so every K/V byte is read once
 //    per kv head, not once per query head as in the reference kernel;
 //  * online softmax on the accumulator fragments (exp2 domain), P^T moved into the B operand
-//    with movmatrix.trans, O^T[d x 8 rows] += V_tile^T . P^T with ldmatrix.trans; P is carried
-//    as a hi + lo pair of 16-bit values so the PV product keeps ~16 mantissa bits;
+//    with movmatrix.trans, O^T[d x 8 rows] += V_tile^T . P^T with ldmatrix.trans; for 16-bit
+//    caches P is carried as a hi + lo pair of 16-bit values so the PV product keeps ~16
+//    mantissa bits; fp8 tiles (converted to fp16 in registers) use one fp16 P, a lazily moved
+//    running max (P <= 2^8) and a V unit that keeps P's scale near 1;
 //  * a (sequence, kv head) segment that lies inside one warp's range is written directly;
 //    a segment cut by range boundaries leaves one fp32 partial (m, l, o) per warp, and the last
 //    warp to finish it merges them (fused split-K combine, no extra launch).  A warp writes at
@@ -81,7 +83,7 @@ __device__ __forceinline__ int route_of(const AttnArgs& a, int b, int& dtiles, i
                      total <= (int64_t)a.max_blocks * a.block_size;
   if (!valid) return kRouteGeneric;  // the generic kernel guards invalid metadata itself
   if (a.decode_on && nq * a.group <= kDecodeRows) {
-    dtiles = (int)((total + kTile - 1) / kTile);
+    dtiles = (int)((total + a.decode_tile - 1) / a.decode_tile);
     return kRouteDecode;
   }
   if (a.prefill_tq > 0) {
@@ -122,13 +124,20 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(AttnArgs a, DecodePla
 // ---------------------------------------------------------------------------------------
 // Decode kernel
 // ---------------------------------------------------------------------------------------
+// A decode tile is kHalves half-tiles of kTile (16) tokens: one for 16-bit caches,
+// kFp8HalfTiles for fp8 caches (two give 32 tokens per stage and per softmax step).  A half-tile
+// never crosses a cache block (block_size % 16 == 0), so each has its own block id, TMA boxes
+// and fp8 scales.
 template <int D, bool FP8>
 struct DecodeLayout {
   static constexpr int kElem = FP8 ? 1 : 2;              // stored bytes per element
   static constexpr int kBoxCols = 128 / kElem;           // elements per 128-byte TMA box row
-  static constexpr int kBoxes = D / kBoxCols;            // TMA boxes per tile row
+  static constexpr int kBoxes = D / kBoxCols;            // TMA boxes per half-tile row
   static constexpr int kBoxBytes = kTile * 128;          // 16 rows x 128 B
-  static constexpr int kTileBytes = kTile * D * kElem;   // one tensor, one tile, as stored
+  static constexpr int kHalves = FP8 ? kFp8HalfTiles : 1;
+  static constexpr int kTileRows = kTile * kHalves;      // tokens per tile
+  static constexpr int kHalfBytes = kTile * D * kElem;   // one tensor, one half-tile, as stored
+  static constexpr int kTileBytes = kHalves * kHalfBytes;
   static constexpr int kStageBytes = 2 * kTileBytes;     // K + V
 };
 
@@ -242,9 +251,45 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
   auto issue = [&](int s, int slot, int t) {
     if (lane != 0) return;
     const Piece& u = myring[slot];
+    uint64_t* bar = &bars[warp][s];
+    if constexpr (FP8) {
+      // Half-tiles past the sequence load nothing (their tokens are masked); a half-tile with an
+      // invalid block id loads nothing and reports it.
+      int z[L::kHalves];
+      uint32_t bytes = 0;
+#pragma unroll
+      for (int h = 0; h < L::kHalves; ++h) {
+        const int pos = t * L::kTileRows + h * kTile;
+        z[h] = -1;
+        if (pos >= u.total) continue;
+        const int32_t blk = a.block_table[(int64_t)u.b * a.max_blocks + pos / a.block_size];
+        if (blk < 0 || blk >= a.num_blocks) {
+          set_status(a.status, kStatusBadBlock);
+          continue;
+        }
+        z[h] = blk * a.block_size + pos % a.block_size;
+        bytes += 2 * L::kHalfBytes;
+      }
+      if (bytes == 0) {
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+        return;
+      }
+      uint8_t* kdst = wbase + s * L::kStageBytes;
+      uint8_t* vdst = kdst + L::kTileBytes;
+      mbar_arrive_expect_tx(bar, bytes);
+#pragma unroll
+      for (int h = 0; h < L::kHalves; ++h) {
+        if (z[h] < 0) continue;
+#pragma unroll
+        for (int hb = 0; hb < L::kBoxes; ++hb) {
+          tma_load_3d(kdst + h * L::kHalfBytes + hb * L::kBoxBytes, &maps.k_map, bar, hb * L::kBoxCols, u.kh, z[h]);
+          tma_load_3d(vdst + h * L::kHalfBytes + hb * L::kBoxBytes, &maps.v_map, bar, hb * L::kBoxCols, u.kh, z[h]);
+        }
+      }
+      return;
+    }
     const int pos0 = t * kTile;
     const int32_t blk = a.block_table[(int64_t)u.b * a.max_blocks + pos0 / a.block_size];
-    uint64_t* bar = &bars[warp][s];
     if (blk < 0 || blk >= a.num_blocks) {
       set_status(a.status, kStatusBadBlock);
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -329,201 +374,352 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
     float o[KSTEPS][4];
 #pragma unroll
     for (int mt = 0; mt < KSTEPS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    // fp8: o is kept in units of vref, a V scale of the piece (P carries v_scale / vref, which
+    // stays near 1 so the fp16 P keeps its precision); 16-bit caches: 1.
+    float vref = FP8 ? 0.f : 1.f;
 
-    // Tile metadata in windows of 32 tiles: lane i holds tile wb + i's physical block (and, for
-    // fp8 caches, its K and V scales).  The next window's block entries are loaded when a
-    // window starts and its scales 8 tiles later, so no tile waits on a dependent global load.
-    auto tile_block = [&](int t) -> int32_t {
-      return t < u.t1 ? __ldg(a.block_table + (int64_t)u.b * a.max_blocks + (t * kTile) / a.block_size) : -1;
-    };
-    auto block_scale = [&](const float* sc, int32_t blk) -> float {
-      return blk >= 0 && blk < a.num_blocks ? __ldg(sc + (int64_t)blk * KV + u.kh) : 1.f;
-    };
-    int wb = ct;
-    int32_t w_blk = tile_block(wb + lane), n_blk = -1;
-    float w_ks = 1.f, w_vs = 1.f, n_ks = 1.f, n_vs = 1.f;
     if constexpr (FP8) {
-      w_ks = block_scale(a.k_scale, w_blk);
-      w_vs = block_scale(a.v_scale, w_blk);
-    }
-    // A tile needs no per-position mask when it lies inside the sequence, before every query's
-    // causal limit and after every query's window start.
-    const int full_end = a.is_causal ? min(u.total, u.past + 1) : u.total;
-    const int full_begin = a.window > 0 ? u.past + u.nq - a.window : 0;
+      // Half-tile metadata in windows of 32 half-tiles (kWin tiles): lane i holds half-tile
+      // kHalves * wb + i's block id and K / V scales; the next window's ids are loaded when a
+      // window starts and its scales 4 tiles later.
+      constexpr int kWin = 32 / L::kHalves;
+      auto half_block = [&](int hidx) -> int32_t {
+        const int t = hidx / L::kHalves, pos = t * L::kTileRows + (hidx % L::kHalves) * kTile;
+        return t < u.t1 && pos < u.total
+                   ? __ldg(a.block_table + (int64_t)u.b * a.max_blocks + pos / a.block_size)
+                   : -1;
+      };
+      auto block_scale = [&](const float* sc, int32_t blk) -> float {
+        return blk >= 0 && blk < a.num_blocks ? __ldg(sc + (int64_t)blk * KV + u.kh) : 0.f;
+      };
+      int wb = ct;
+      int32_t w_blk = half_block(L::kHalves * wb + lane), n_blk = -1;
+      float w_ks = block_scale(a.k_scale, w_blk), w_vs = block_scale(a.v_scale, w_blk);
+      float n_ks = 0.f, n_vs = 0.f;
+      const int full_end = a.is_causal ? min(u.total, u.past + 1) : u.total;
+      const int full_begin = a.window > 0 ? u.past + u.nq - a.window : 0;
 
-    for (; ct < u.t1; ++ct) {
-      const int s = consumed % STAGES;
-      const int pos0 = ct * kTile;
-      int wi = ct - wb;
-      if (wi == 32) {
-        wb = ct;
-        wi = 0;
-        w_blk = n_blk;
-        w_ks = n_ks;
-        w_vs = n_vs;
-      }
-      if (wi == 0) n_blk = tile_block(wb + 32 + lane);
-      if constexpr (FP8) {
-        if (wi == 8) {
+      for (; ct < u.t1; ++ct) {
+        const int s = consumed % STAGES;
+        const int pos0 = ct * L::kTileRows;
+        int wi = ct - wb;
+        if (wi == kWin) {
+          wb = ct;
+          wi = 0;
+          w_blk = n_blk;
+          w_ks = n_ks;
+          w_vs = n_vs;
+        }
+        if (wi == 0) n_blk = half_block(L::kHalves * (wb + kWin) + lane);
+        if (wi == 4) {
           n_ks = block_scale(a.k_scale, n_blk);
           n_vs = block_scale(a.v_scale, n_blk);
         }
-      }
-      if (!mbar_wait(&bars[warp][s], (phase >> s) & 1u)) {
-        if (lane == 0) set_status(a.status, kStatusTimeout);
-        failed = true;
-        // One more bounded wait for the loads still in flight before the warp stops.
-        for (int s2 = 0; s2 < STAGES; ++s2)
-          if ((pending >> s2) & 1u) mbar_wait(&bars[warp][s2], (phase >> s2) & 1u);
-        pending = 0;
-        break;
-      }
-      phase ^= 1u << s;
-      pending &= ~(1u << s);
-      const int32_t blk = __shfl_sync(0xffffffffu, w_blk, wi);
-      const bool blk_ok = blk >= 0 && blk < a.num_blocks;
-      const bool full = blk_ok && pos0 >= full_begin && pos0 + kTile <= full_end;
-      uint32_t kbase = wbase_u32 + s * L::kStageBytes;
-      uint32_t vbase = kbase + L::kTileBytes;
-      float k_sc = 1.f, v_sc = 1.f;
-      if constexpr (FP8) {
-        k_sc = __shfl_sync(0xffffffffu, w_ks, wi);
-        v_sc = __shfl_sync(0xffffffffu, w_vs, wi);
-      }
-
-      // Overlay: tile rows at positions >= past hold the sequence's own new K/V rows (16-bit
-      // caches; an fp8 cache is read whole, new rows included, as encoded caches are).
-      const bool overlay = !FP8 && pos0 + kTile > u.past;
-      if (overlay) {
-        constexpr int CH = D / 8;  // 16-byte chunks per row
-        for (int idx = lane; idx < kTile * CH; idx += 32) {
-          const int row = idx / CH, chunk = idx % CH;
-          const int pos = pos0 + row;
-          if (pos >= u.total) {
-            // rows past the sequence: V becomes zeros (P is 0 there; 0 x NaN from an unused slot
-            // would still poison O)
-            *reinterpret_cast<uint4*>(wbase + (vbase - wbase_u32) + swz(row, chunk)) = make_uint4(0u, 0u, 0u, 0u);
-            continue;
-          }
-          if (pos < u.past) continue;
-          const int64_t tok = u.c0 + (pos - u.past);
-          const uint4 kv = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) + tok * a.k_stride +
-                                                           (int64_t)u.kh * D + chunk * 8);
-          const uint4 vv = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) + tok * a.v_stride +
-                                                           (int64_t)u.kh * D + chunk * 8);
-          *reinterpret_cast<uint4*>(wbase + (kbase - wbase_u32) + swz(row, chunk)) = kv;
-          *reinterpret_cast<uint4*>(wbase + (vbase - wbase_u32) + swz(row, chunk)) = vv;
+        if (!mbar_wait(&bars[warp][s], (phase >> s) & 1u)) {
+          if (lane == 0) set_status(a.status, kStatusTimeout);
+          failed = true;
+          for (int s2 = 0; s2 < STAGES; ++s2)
+            if ((pending >> s2) & 1u) mbar_wait(&bars[warp][s2], (phase >> s2) & 1u);
+          pending = 0;
+          break;
         }
-        __syncwarp();
-      }
-
-      // S^T = K_tile . Q^T (two accumulators halve the dependent MMA chain)
-      float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
-      {
-        const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int half = lane >> 4;
+        phase ^= 1u << s;
+        pending &= ~(1u << s);
+        int32_t blk[L::kHalves];
+        float k_sc[L::kHalves], v_sc[L::kHalves];
+        bool blk_ok[L::kHalves];
 #pragma unroll
-        for (int kk = 0; kk < KSTEPS; kk += 2) {
-          uint32_t af[4], bf[4];
-          if constexpr (FP8) {
-            // 16-byte chunks kk, kk+1 = channel blocks of k-steps kk, kk+1
-            uint32_t d0, d1, d2, d3;
-            ldsm_x4(kbase + swz(row, kk + half), d0, d1, d2, d3);
-            e4m3x4_to_f16x2x2(d0, af[0], af[2]);
-            e4m3x4_to_f16x2x2(d1, af[1], af[3]);
-            e4m3x4_to_f16x2x2(d2, bf[0], bf[2]);
-            e4m3x4_to_f16x2x2(d3, bf[1], bf[3]);
-          } else {
-            ldsm_x4(kbase + swz(row, kk * 2 + half), af[0], af[1], af[2], af[3]);
-            ldsm_x4(kbase + swz(row, kk * 2 + 2 + half), bf[0], bf[1], bf[2], bf[3]);
-          }
-          MMA::run(c, af, qf[kk][0], qf[kk][1]);
-          MMA::run(c2, bf, qf[kk + 1][0], qf[kk + 1][1]);
+        for (int h = 0; h < L::kHalves; ++h) {
+          blk[h] = __shfl_sync(0xffffffffu, w_blk, L::kHalves * wi + h);
+          k_sc[h] = __shfl_sync(0xffffffffu, w_ks, L::kHalves * wi + h);
+          v_sc[h] = __shfl_sync(0xffffffffu, w_vs, L::kHalves * wi + h);
+          blk_ok[h] = blk[h] >= 0 && blk[h] < a.num_blocks;
         }
+        bool full = pos0 >= full_begin && pos0 + L::kTileRows <= full_end;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) c[e] += c2[e];
-      }
+        for (int h = 0; h < L::kHalves; ++h) full = full && blk_ok[h];
+        const uint32_t kbase = wbase_u32 + s * L::kStageBytes;
+        const uint32_t vbase = kbase + L::kTileBytes;
 
-      // Masks, scale (log2 domain), online softmax per q-row column.
-      float sc[4];
-      const float ksq = k_sc * qk_scale;
+        // S^T per half-tile = K_half . Q^T; two accumulators per half halve the MMA chains.
+        float c[L::kHalves][2][4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int tok = (lane >> 2) + ((e >> 1) << 3);
-        const int col = col0 + (e & 1);
-        const int qi = (e & 1) ? qi1 : qi0;
-        const int pos = pos0 + tok;
-        bool vis = col < rows;
-        if (!full) {
-          vis = vis && blk_ok && pos < u.total;
-          if (a.is_causal) vis = vis && pos <= u.past + qi;
-          if (a.window > 0) vis = vis && pos >= u.past + qi - a.window + 1;
-        }
-        float x = c[e] * ksq;
-        if (a.softcap > 0.f) x = a.softcap * tanhf(x / a.softcap) * kLog2e;
-        sc[e] = vis ? x : -INFINITY;
-      }
-      float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+        for (int h = 0; h < L::kHalves; ++h)
 #pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-      }
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float mu0 = mn0 == -INFINITY ? 0.f : mn0, mu1 = mn1 == -INFINITY ? 0.f : mn1;
-      const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
-      const float p0 = exp2f(sc[0] - mu0), p1 = exp2f(sc[1] - mu1);
-      const float p2 = exp2f(sc[2] - mu0), p3 = exp2f(sc[3] - mu1);
-      l0 = l0 * al0 + p0 + p2;
-      l1 = l1 * al1 + p1 + p3;
-      m0 = mn0;
-      m1 = mn1;
+          for (int j = 0; j < 2; ++j) c[h][j][0] = c[h][j][1] = c[h][j][2] = c[h][j][3] = 0.f;
+        {
+          const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int half = lane >> 4;
 #pragma unroll
-      for (int mt = 0; mt < KSTEPS; ++mt) {
-        o[mt][0] *= al0; o[mt][2] *= al0;
-        o[mt][1] *= al1; o[mt][3] *= al1;
-      }
-
-      // P^T -> B fragments (hi + lo 16-bit split); an fp8 tile's V scale rides on P.
-      const float q0 = p0 * v_sc, q1 = p1 * v_sc, q2 = p2 * v_sc, q3 = p3 * v_sc;
-      const uint32_t x0 = MMA::pack(q0, q1), x1 = MMA::pack(q2, q3);
-      const float2 h0 = MMA::unpack(x0), h1 = MMA::unpack(x1);
-      const uint32_t y0 = MMA::pack(q0 - h0.x, q1 - h0.y), y1 = MMA::pack(q2 - h1.x, q3 - h1.y);
-      const uint32_t bh0 = movm_t(x0), bh1 = movm_t(x1), bl0 = movm_t(y0), bl1 = movm_t(y1);
-
-      // O^T += V_tile^T . P^T
-      {
-        const int jm = lane >> 3;
-        const int row = (lane & 7) + (jm >> 1) * 8;
-        const int sub = jm & 1;
-        if constexpr (FP8) {
-          // tokens 2t, 2t+1 (and +8) of this lane; tokens past the sequence (or of an invalid
-          // block) read as zeros: P is 0 there, and 0 x NaN from an unused slot would poison O
-          // byte masks on the fp8 register [t0 c0, t0 c1, t1 c0, t1 c1] (tokens 2t, 2t+1)
-          // The byte permute [t0 c0, t0 c1, t1 c0, t1 c1] -> [t0 c0, t1 c0, t0 c1, t1 c1] (selector
-          // 0x3120) regroups the bytes per channel; a masked token's bytes select the zero operand
-          // (selector nibble 4) instead.
-          const int t2 = (lane & 3) * 2;
-          auto perm_sel = [&](int p) -> uint32_t {
-            const bool ok0 = full || (blk_ok && pos0 + p < u.total);
-            const bool ok1 = full || (blk_ok && pos0 + p + 1 < u.total);
-            return (ok0 ? 0x0100u : 0x0404u) | (ok1 ? 0x3020u : 0x4040u);
-          };
-          const uint32_t sel_lo = perm_sel(t2), sel_hi = perm_sel(t2 + 8);
+          for (int kk = 0; kk < KSTEPS; kk += 2) {
 #pragma unroll
-          for (int mt = 0; mt < KSTEPS; mt += 2) {
-            uint32_t d[4];
-            ldsm_x4_t(vbase + swz(row, mt + sub), d[0], d[1], d[2], d[3]);
-#pragma unroll
-            for (int blk2 = 0; blk2 < 2; ++blk2) {  // channel blocks mt, mt+1
-              uint32_t af[4];
-              e4m3x4_to_f16x2x2(__byte_perm(d[blk2], 0u, sel_lo), af[0], af[1]);
-              e4m3x4_to_f16x2x2(__byte_perm(d[blk2 + 2], 0u, sel_hi), af[2], af[3]);
-              MMA::run(o[mt + blk2], af, bh0, bh1);
-              MMA::run(o[mt + blk2], af, bl0, bl1);
+            for (int h = 0; h < L::kHalves; ++h) {
+              // 16-byte chunks kk, kk+1 = channel blocks of k-steps kk, kk+1
+              uint32_t af[4], bf[4], d0, d1, d2, d3;
+              ldsm_x4(kbase + h * L::kHalfBytes + swz(row, kk + half), d0, d1, d2, d3);
+              e4m3x4_to_f16x2x2(d0, af[0], af[2]);
+              e4m3x4_to_f16x2x2(d1, af[1], af[3]);
+              e4m3x4_to_f16x2x2(d2, bf[0], bf[2]);
+              e4m3x4_to_f16x2x2(d3, bf[1], bf[3]);
+              MMA::run(c[h][0], af, qf[kk][0], qf[kk][1]);
+              MMA::run(c[h][1], bf, qf[kk + 1][0], qf[kk + 1][1]);
             }
           }
-        } else {
+        }
+
+        // Masks, scale (log2 domain), online softmax per q-row column over the 32 tokens.
+        float sc[L::kHalves][4];
+#pragma unroll
+        for (int h = 0; h < L::kHalves; ++h) {
+          const float ksq = k_sc[h] * qk_scale;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int tok = h * kTile + (lane >> 2) + ((e >> 1) << 3);
+            const int col = col0 + (e & 1);
+            const int qi = (e & 1) ? qi1 : qi0;
+            const int pos = pos0 + tok;
+            bool vis = col < rows;
+            if (!full) {
+              vis = vis && blk_ok[h] && pos < u.total;
+              if (a.is_causal) vis = vis && pos <= u.past + qi;
+              if (a.window > 0) vis = vis && pos >= u.past + qi - a.window + 1;
+            }
+            float x = (c[h][0][e] + c[h][1][e]) * ksq;
+            if (a.softcap > 0.f) x = a.softcap * tanhf(x / a.softcap) * kLog2e;
+            sc[h][e] = vis ? x : -INFINITY;
+          }
+        }
+        float mx0 = fmaxf(sc[0][0], sc[0][2]), mx1 = fmaxf(sc[0][1], sc[0][3]);
+#pragma unroll
+        for (int h = 1; h < L::kHalves; ++h) {
+          mx0 = fmaxf(mx0, fmaxf(sc[h][0], sc[h][2]));
+          mx1 = fmaxf(mx1, fmaxf(sc[h][1], sc[h][3]));
+        }
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+        }
+        // Lazy rescale: the running max moves only when a score exceeds it by more than 2^8, so
+        // P stays <= 256 (exact in fp16) and most tiles skip the O rescale.  The decision is
+        // warp-uniform.
+        if (__any_sync(0xffffffffu, mx0 > m0 + 8.f || mx1 > m1 + 8.f)) {
+          const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+          const float al0 = exp2f(m0 - (mn0 == -INFINITY ? 0.f : mn0));
+          const float al1 = exp2f(m1 - (mn1 == -INFINITY ? 0.f : mn1));
+          l0 *= al0;
+          l1 *= al1;
+#pragma unroll
+          for (int mt = 0; mt < KSTEPS; ++mt) {
+            o[mt][0] *= al0; o[mt][2] *= al0;
+            o[mt][1] *= al1; o[mt][3] *= al1;
+          }
+          m0 = mn0;
+          m1 = mn1;
+        }
+        // The V unit moves when a half-tile's V scale exceeds it 64-fold (then P <= 256 * 64
+        // stays inside fp16); the first tile with a nonzero scale sets it.
+        float vmax = v_sc[0];
+#pragma unroll
+        for (int h = 1; h < L::kHalves; ++h) vmax = fmaxf(vmax, v_sc[h]);
+        if (vmax > vref * 64.f) {  // warp-uniform: the scales are shuffled values
+          const float f = vref / vmax;
+#pragma unroll
+          for (int mt = 0; mt < KSTEPS; ++mt) {
+            o[mt][0] *= f; o[mt][1] *= f; o[mt][2] *= f; o[mt][3] *= f;
+          }
+          vref = vmax;
+        }
+        const float mu0 = m0 == -INFINITY ? 0.f : m0, mu1 = m1 == -INFINITY ? 0.f : m1;
+        const float inv_vref = vref > 0.f ? 1.f / vref : 0.f;
+        uint32_t bp[L::kHalves][2];  // P^T B-fragments per half-tile (fp16, V scale / vref folded in)
+#pragma unroll
+        for (int h = 0; h < L::kHalves; ++h) {
+          const float p0 = exp2f(sc[h][0] - mu0), p1 = exp2f(sc[h][1] - mu1);
+          const float p2 = exp2f(sc[h][2] - mu0), p3 = exp2f(sc[h][3] - mu1);
+          l0 += p0 + p2;
+          l1 += p1 + p3;
+          const float vr = v_sc[h] * inv_vref;
+          bp[h][0] = movm_t(MMA::pack(p0 * vr, p1 * vr));
+          bp[h][1] = movm_t(MMA::pack(p2 * vr, p3 * vr));
+        }
+
+        // O^T += V_half^T . P_half^T for both half-tiles
+        {
+          const int jm = lane >> 3;
+          const int row = (lane & 7) + (jm >> 1) * 8;
+          const int sub = jm & 1;
+          // tokens 2t, 2t+1 (and +8) of this lane; tokens past the sequence or of an invalid
+          // block read as zeros (P is 0 there, and 0 x NaN from an unused slot would poison
+          // O).  The byte permute [t0 c0, t0 c1, t1 c0, t1 c1] -> [t0 c0, t1 c0, t0 c1, t1 c1]
+          // (selector 0x3120) regroups the bytes per channel; a masked token selects zeros.
+          const int t2 = (lane & 3) * 2;
+          auto perm_sel = [&](int h, int p) -> uint32_t {
+            const int pos = pos0 + h * kTile + p;
+            const bool ok0 = full || (blk_ok[h] && pos < u.total);
+            const bool ok1 = full || (blk_ok[h] && pos + 1 < u.total);
+            return (ok0 ? 0x0100u : 0x0404u) | (ok1 ? 0x3020u : 0x4040u);
+          };
+          uint32_t sel_lo[L::kHalves], sel_hi[L::kHalves];
+#pragma unroll
+          for (int h = 0; h < L::kHalves; ++h) {
+            sel_lo[h] = perm_sel(h, t2);
+            sel_hi[h] = perm_sel(h, t2 + 8);
+          }
+#pragma unroll
+          for (int mt = 0; mt < KSTEPS; mt += 2) {
+#pragma unroll
+            for (int h = 0; h < L::kHalves; ++h) {
+              uint32_t d[4];
+              ldsm_x4_t(vbase + h * L::kHalfBytes + swz(row, mt + sub), d[0], d[1], d[2], d[3]);
+#pragma unroll
+              for (int blk2 = 0; blk2 < 2; ++blk2) {  // channel blocks mt, mt+1
+                uint32_t af[4];
+                e4m3x4_to_f16x2x2(__byte_perm(d[blk2], 0u, sel_lo[h]), af[0], af[1]);
+                e4m3x4_to_f16x2x2(__byte_perm(d[blk2 + 2], 0u, sel_hi[h]), af[2], af[3]);
+                MMA::run(o[mt + blk2], af, bp[h][0], bp[h][1]);
+              }
+            }
+          }
+        }
+        __syncwarp();
+        ++consumed;
+        produce();  // refill the stage just freed (possibly with the next piece's first tile)
+        __syncwarp();
+      }
+    } else {
+      // Tile metadata in windows of 32 tiles: lane i holds tile wb + i's physical block; the
+      // next window's entries are loaded when a window starts, so no tile waits on a dependent
+      // global load.
+      auto tile_block = [&](int t) -> int32_t {
+        return t < u.t1 ? __ldg(a.block_table + (int64_t)u.b * a.max_blocks + (t * kTile) / a.block_size) : -1;
+      };
+      int wb = ct;
+      int32_t w_blk = tile_block(wb + lane), n_blk = -1;
+      // A tile needs no per-position mask when it lies inside the sequence, before every
+      // query's causal limit and after every query's window start.
+      const int full_end = a.is_causal ? min(u.total, u.past + 1) : u.total;
+      const int full_begin = a.window > 0 ? u.past + u.nq - a.window : 0;
+
+      for (; ct < u.t1; ++ct) {
+        const int s = consumed % STAGES;
+        const int pos0 = ct * kTile;
+        int wi = ct - wb;
+        if (wi == 32) {
+          wb = ct;
+          wi = 0;
+          w_blk = n_blk;
+        }
+        if (wi == 0) n_blk = tile_block(wb + 32 + lane);
+        if (!mbar_wait(&bars[warp][s], (phase >> s) & 1u)) {
+          if (lane == 0) set_status(a.status, kStatusTimeout);
+          failed = true;
+          // One more bounded wait for the loads still in flight before the warp stops.
+          for (int s2 = 0; s2 < STAGES; ++s2)
+            if ((pending >> s2) & 1u) mbar_wait(&bars[warp][s2], (phase >> s2) & 1u);
+          pending = 0;
+          break;
+        }
+        phase ^= 1u << s;
+        pending &= ~(1u << s);
+        const int32_t blk = __shfl_sync(0xffffffffu, w_blk, wi);
+        const bool blk_ok = blk >= 0 && blk < a.num_blocks;
+        const bool full = blk_ok && pos0 >= full_begin && pos0 + kTile <= full_end;
+        const uint32_t kbase = wbase_u32 + s * L::kStageBytes;
+        const uint32_t vbase = kbase + L::kTileBytes;
+
+        // Overlay: tile rows at positions >= past hold the sequence's own new K/V rows.
+        const bool overlay = pos0 + kTile > u.past;
+        if (overlay) {
+          constexpr int CH = D / 8;  // 16-byte chunks per row
+          for (int idx = lane; idx < kTile * CH; idx += 32) {
+            const int row = idx / CH, chunk = idx % CH;
+            const int pos = pos0 + row;
+            if (pos >= u.total) {
+              // rows past the sequence: V becomes zeros (P is 0 there; 0 x NaN from an unused
+              // slot would still poison O)
+              *reinterpret_cast<uint4*>(wbase + (vbase - wbase_u32) + swz(row, chunk)) = make_uint4(0u, 0u, 0u, 0u);
+              continue;
+            }
+            if (pos < u.past) continue;
+            const int64_t tok = u.c0 + (pos - u.past);
+            const uint4 kv = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) + tok * a.k_stride +
+                                                             (int64_t)u.kh * D + chunk * 8);
+            const uint4 vv = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) + tok * a.v_stride +
+                                                             (int64_t)u.kh * D + chunk * 8);
+            *reinterpret_cast<uint4*>(wbase + (kbase - wbase_u32) + swz(row, chunk)) = kv;
+            *reinterpret_cast<uint4*>(wbase + (vbase - wbase_u32) + swz(row, chunk)) = vv;
+          }
+          __syncwarp();
+        }
+
+        // S^T = K_tile . Q^T (two accumulators halve the dependent MMA chain)
+        float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+          const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int half = lane >> 4;
+#pragma unroll
+          for (int kk = 0; kk < KSTEPS; kk += 2) {
+            uint32_t af[4], bf[4];
+            ldsm_x4(kbase + swz(row, kk * 2 + half), af[0], af[1], af[2], af[3]);
+            ldsm_x4(kbase + swz(row, kk * 2 + 2 + half), bf[0], bf[1], bf[2], bf[3]);
+            MMA::run(c, af, qf[kk][0], qf[kk][1]);
+            MMA::run(c2, bf, qf[kk + 1][0], qf[kk + 1][1]);
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) c[e] += c2[e];
+        }
+
+        // Masks, scale (log2 domain), online softmax per q-row column.
+        float sc[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int tok = (lane >> 2) + ((e >> 1) << 3);
+          const int col = col0 + (e & 1);
+          const int qi = (e & 1) ? qi1 : qi0;
+          const int pos = pos0 + tok;
+          bool vis = col < rows;
+          if (!full) {
+            vis = vis && blk_ok && pos < u.total;
+            if (a.is_causal) vis = vis && pos <= u.past + qi;
+            if (a.window > 0) vis = vis && pos >= u.past + qi - a.window + 1;
+          }
+          float x = c[e] * qk_scale;
+          if (a.softcap > 0.f) x = a.softcap * tanhf(x / a.softcap) * kLog2e;
+          sc[e] = vis ? x : -INFINITY;
+        }
+        float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+        }
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float mu0 = mn0 == -INFINITY ? 0.f : mn0, mu1 = mn1 == -INFINITY ? 0.f : mn1;
+        const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
+        const float p0 = exp2f(sc[0] - mu0), p1 = exp2f(sc[1] - mu1);
+        const float p2 = exp2f(sc[2] - mu0), p3 = exp2f(sc[3] - mu1);
+        l0 = l0 * al0 + p0 + p2;
+        l1 = l1 * al1 + p1 + p3;
+        m0 = mn0;
+        m1 = mn1;
+#pragma unroll
+        for (int mt = 0; mt < KSTEPS; ++mt) {
+          o[mt][0] *= al0; o[mt][2] *= al0;
+          o[mt][1] *= al1; o[mt][3] *= al1;
+        }
+
+        // P^T -> B fragments (hi + lo 16-bit split, about 16 mantissa bits of P)
+        const uint32_t x0 = MMA::pack(p0, p1), x1 = MMA::pack(p2, p3);
+        const float2 h0 = MMA::unpack(x0), h1 = MMA::unpack(x1);
+        const uint32_t y0 = MMA::pack(p0 - h0.x, p1 - h0.y), y1 = MMA::pack(p2 - h1.x, p3 - h1.y);
+        const uint32_t bh0 = movm_t(x0), bh1 = movm_t(x1), bl0 = movm_t(y0), bl1 = movm_t(y1);
+
+        // O^T += V_tile^T . P^T
+        {
+          const int jm = lane >> 3;
+          const int row = (lane & 7) + (jm >> 1) * 8;
+          const int sub = jm & 1;
 #pragma unroll
           for (int mt = 0; mt < KSTEPS; ++mt) {
             uint32_t af[4];
@@ -532,12 +728,12 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
             MMA::run(o[mt], af, bl0, bl1);
           }
         }
+        __syncwarp();
+        if (overlay) fence_proxy_async_smem();
+        ++consumed;
+        produce();  // refill the stage just freed (possibly with the next piece's first tile)
+        __syncwarp();
       }
-      __syncwarp();
-      if (overlay) fence_proxy_async_smem();
-      ++consumed;
-      produce();  // refill the stage just freed (possibly with the next piece's first tile)
-      __syncwarp();
     }
     if (failed) break;
 
@@ -562,7 +758,7 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
           f = M == -INFINITY ? 0.f : exp2f(M - M2);
           Ls = Ls * f + exp2f(sink - M2);
         }
-        const float inv = Ls > 0.f ? f / Ls : 0.f;
+        const float inv = Ls > 0.f ? f / Ls * vref : 0.f;
         T* orow = reinterpret_cast<T*>(a.out) + (int64_t)(u.c0 + qi) * H * D + (int64_t)(u.kh * g + hl) * D;
 #pragma unroll
         for (int mt = 0; mt < KSTEPS; ++mt) {
@@ -586,8 +782,8 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
         }
 #pragma unroll
         for (int mt = 0; mt < KSTEPS; ++mt) {
-          po[out_channel(FP8, mt, dr, 0)] = o[mt][e];
-          po[out_channel(FP8, mt, dr, 1)] = o[mt][e + 2];
+          po[out_channel(FP8, mt, dr, 0)] = o[mt][e] * vref;
+          po[out_channel(FP8, mt, dr, 1)] = o[mt][e + 2] * vref;
         }
       }
       __threadfence();
@@ -698,7 +894,7 @@ int decode_ctas_per_sm(int head_size, int act_dtype, int cache_dtype) {
   const bool bf = act_dtype == B200_DTYPE_BFLOAT16;
   if (cache_dtype == B200_DTYPE_FLOAT8E4M3FN) {
     switch (head_size) {
-      case 128: return decode_occupancy_t<__half, 128, 3, true>(nullptr);
+      case 128: return decode_occupancy_t<__half, 128, 2, true>(nullptr);
       case 256: return decode_occupancy_t<__half, 256, 2, true>(nullptr);
       default: return kDecodeMaxCtasPerSm;
     }
@@ -721,7 +917,7 @@ cudaError_t launch_decode(const AttnArgs& a, const DecodePlan& plan, const Decod
   const bool bf = a.act_dtype == B200_DTYPE_BFLOAT16;
   if (a.cache_dtype == B200_DTYPE_FLOAT8E4M3FN) {
     switch (a.head_size) {
-      case 128: return launch_decode_t<__half, 128, 3, true>(a, plan, maps, num_sms, stream);
+      case 128: return launch_decode_t<__half, 128, 2, true>(a, plan, maps, num_sms, stream);
       case 256: return launch_decode_t<__half, 256, 2, true>(a, plan, maps, num_sms, stream);
       default: return cudaErrorInvalidValue;
     }
