@@ -50,6 +50,13 @@ extern "C" {
  * outputs and attributes (reference claim rust/src/ops/attention.rs:4384-4645, op
  * :3857-4382).  Zero-initialise and fill what is present.
  */
+/* Largest head_size the kernels take (head sizes above 256 and LATENT layouts run on the generic
+ * kernel; the fast decode and prefill kernels cover 64 / 128 / 256 and 128). */
+#define B200_MAX_HEAD_SIZE 640
+/* Shared memory the append prologue may stage per token when it rotates / normalises rows or
+ * encodes an integer or fp8 cache: 4 bytes x head_size x (num_heads + 2 kv_num_heads). */
+#define B200_MAX_PROLOGUE_STAGE_BYTES (227 * 1024)
+
 typedef struct B200PagedAttentionParams {
   /* attributes */
   int32_t num_heads;          /* H                                                        */
@@ -122,6 +129,13 @@ typedef struct B200PagedAttentionParams {
    * the last attention kernel of the call (decode + combine + prefill), for live timing */
   void* attention_event_begin;
   void* attention_event_end;
+
+  /* kv_cache_layout LATENT (attention.rs:3862-3867, :4058-4062, :4210-4212): one kv head; value,
+   * value_cache (and their outputs) are absent; every value row is the first v_head_size
+   * channels of the key row (after RoPE / norm), read from the key cache; the output is
+   * [nt, H*v_head_size].  16-bit caches only; such calls run on the generic kernel. */
+  int32_t kv_cache_latent;
+  int32_t v_head_size;        /* LATENT: value channels (0 -> head_size), <= head_size     */
 } B200PagedAttentionParams;
 
 /* Library version (major * 10000 + minor * 100 + patch). */

@@ -36,6 +36,7 @@ struct PrologueArgs {
   int act_dtype, cache_dtype, k_per_channel, v_per_channel;
   int do_norm, do_rotary, rotary_interleaved, rotary_offset, rotary_dim, rotary_positions;
   int kv_only;  // append alone: skip Q processing
+  int latent;   // LATENT layout: no value rows or value cache (key rows only)
   float norm_eps;
   int64_t query_stride, key_stride, value_stride;
   const void* query; const void* key; const void* value;
@@ -78,6 +79,8 @@ struct AttnArgs {
   // Per-sequence route (kRoute*), written by the plan kernel and refined by the prologue; null
   // means every sequence runs on the generic kernel.
   int* route;
+  int v_head;      // value channels per head and output channels per head (head_size, or the
+                   // LATENT v_head_size; LATENT values are read from the key rows)
   int decode_on;   // decode kernel enabled for this call (shape supported)
   int decode_tile; // tokens per decode tile: kTile, or 2 * kTile for fp8 caches
   int prefill_tq;  // query tokens per prefill work item (2 x 128 rows / group) or 0 = prefill kernel off

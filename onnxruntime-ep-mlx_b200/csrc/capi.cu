@@ -68,12 +68,14 @@ struct Layout {
   size_t total = 0;
 };
 
+// LATENT layouts (values are key-row prefixes) run on the generic kernel.
 bool fast_decode_enabled(const B200PagedAttentionParams* p) {
-  return !p->force_generic && b200::decode_supported(p->head_size, p->block_size, p->act_dtype, p->cache_dtype);
+  return !p->force_generic && !p->kv_cache_latent &&
+         b200::decode_supported(p->head_size, p->block_size, p->act_dtype, p->cache_dtype);
 }
 
 bool fast_prefill_enabled(const B200PagedAttentionParams* p) {
-  return !p->force_generic && p->kv_num_heads > 0 &&
+  return !p->force_generic && !p->kv_cache_latent && p->kv_num_heads > 0 &&
          b200::prefill_supported(p->head_size, p->block_size, p->num_heads / p->kv_num_heads, p->act_dtype,
                                  p->cache_dtype);
 }
@@ -129,8 +131,8 @@ int check_params(const B200PagedAttentionParams* p, bool kv_only) {
   if (p->num_heads <= 0 || p->kv_num_heads <= 0 || p->num_heads % p->kv_num_heads != 0)
     return fail(B200_ERR_INVALID_ARGUMENT, "PagedAttention: bad num_heads/kv_num_heads");
   if (p->head_size <= 0) return fail(B200_ERR_INVALID_ARGUMENT, "PagedAttention: head_size must be positive");
-  if (p->head_size > 256)
-    return fail(B200_ERR_UNSUPPORTED, "PagedAttention: head_size above 256 is not implemented");
+  if (p->head_size > B200_MAX_HEAD_SIZE)
+    return fail(B200_ERR_UNSUPPORTED, "PagedAttention: head_size above 640 is not implemented");
   if (p->num_blocks <= 0 || p->block_size <= 0)
     return fail(B200_ERR_INVALID_ARGUMENT, "PagedAttention: caches require matching positive block geometry");
   if (!is_act(p->act_dtype))
@@ -146,9 +148,27 @@ int check_params(const B200PagedAttentionParams* p, bool kv_only) {
     return fail(B200_ERR_INVALID_ARGUMENT, "PagedAttention: negative token or block-table size");
   if ((int64_t)p->num_blocks * p->block_size > INT32_MAX)
     return fail(B200_ERR_UNSUPPORTED, "PagedAttention: cache slot count exceeds int32");
-  if (!p->key || !p->value || !p->key_cache || !p->value_cache || !p->cumulative_sequence_length ||
-      !p->past_seqlens || !p->block_table)
+  const bool latent = p->kv_cache_latent != 0;
+  if (latent) {  // attention.rs:4426-4535
+    if (p->kv_num_heads != 1) return fail(B200_ERR_INVALID_ARGUMENT, "LATENT layout requires kv_num_heads=1");
+    if (cd != p->act_dtype)
+      return fail(B200_ERR_INVALID_ARGUMENT, "quantized LATENT cache contract is not supported");
+    if (p->value || p->value_cache)
+      return fail(B200_ERR_INVALID_ARGUMENT,
+                  "LATENT layout aliases value to key and requires absent value/value_cache");
+    if (p->v_head_size < 0 || p->v_head_size > p->head_size)
+      return fail(B200_ERR_INVALID_ARGUMENT, "LATENT v_head_size must not exceed head_size");
+  }
+  if (!p->key || (!latent && !p->value) || !p->key_cache || (!latent && !p->value_cache) ||
+      !p->cumulative_sequence_length || !p->past_seqlens || !p->block_table)
     return fail(B200_ERR_INVALID_ARGUMENT, "PagedAttention: missing required input");
+  // rows the append prologue stages in shared memory (rotary / norm, or an encoded cache)
+  if (p->do_rotary || p->q_norm_weight || cd != p->act_dtype) {
+    const size_t rows = (size_t)((p->do_rotary || p->q_norm_weight) ? p->num_heads : 0) + 2 * (size_t)p->kv_num_heads;
+    if (sizeof(float) * (size_t)p->head_size * rows > B200_MAX_PROLOGUE_STAGE_BYTES)
+      return fail(B200_ERR_UNSUPPORTED,
+                  "PagedAttention: rotary / norm / encoded rows of one token exceed the prologue's shared memory");
+  }
   if (!kv_only && (!p->query || !p->output))
     return fail(B200_ERR_INVALID_ARGUMENT, "PagedAttention: missing query or output");
   if (p->do_rotary) {
@@ -298,6 +318,7 @@ b200::PrologueArgs prologue_args(const B200PagedAttentionParams* p, const Layout
   a.rotary_dim = p->rotary_dim;
   a.rotary_positions = p->do_rotary ? p->rotary_positions : 0;
   a.kv_only = kv_only;
+  a.latent = p->kv_cache_latent != 0;
   a.norm_eps = p->q_norm_weight ? p->qk_norm_epsilon : 0.f;
   a.query_stride = q_stride(p);
   a.key_stride = k_stride(p);
@@ -510,8 +531,16 @@ int b200_paged_attention(const B200PagedAttentionParams* p, void* stream_ptr) {
       a.k_new = p->key;
       a.k_stride = k_stride(p);
     }
-    a.v_new = p->value;
-    a.v_stride = v_stride(p);
+    if (p->kv_cache_latent) {  // values are the first v_head channels of the key rows
+      a.v_head = p->v_head_size > 0 ? p->v_head_size : p->head_size;
+      a.value_cache = p->key_cache;
+      a.v_new = a.k_new;
+      a.v_stride = a.k_stride;
+    } else {
+      a.v_head = p->head_size;
+      a.v_new = p->value;
+      a.v_stride = v_stride(p);
+    }
 
     b200::DecodePlan plan{};
     b200::DecodeMaps maps;

@@ -4,9 +4,10 @@
 // Restates paged_attention_claim (rust/src/ops/attention.rs:4384-4645) and the integer cache
 // claim it calls (rust/src/ops/kv_cache.rs:16-108), decline messages included, so an EP shell
 // can decide in GetCapability exactly as the reference does.  Two additions: forms this build
-// does not implement (LATENT layout, head size above 256) are declined with a reason, and an
-// fp8 e4m3 cache (extension: per-block, per-kv-head fp32 scales [NB, KV]) is accepted when
-// k/v_cache_dtype say "float8e4m3".
+// does not implement (head size above B200_MAX_HEAD_SIZE, rows the append prologue cannot stage,
+// an fp8 LATENT cache) are declined with a reason, and an fp8 e4m3 cache (extension:
+// per-block, per-kv-head fp32 scales [NB, KV]) is accepted when k/v_cache_dtype say
+// "float8e4m3".
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -244,8 +245,16 @@ void paged_claim(const View& v) {
       REQUIRE(v.out(idx)->dtype == v.dtype_of(idx + 2), "cache output %d must retain cache storage dtype", idx);
   }
   // Forms the reference accepts that this build does not implement.
-  REQUIRE(!latent, "LATENT cache layout is not implemented by the B200 kernels");
-  REQUIRE(head <= 256, "head_size above 256 is not implemented by the B200 kernels");
+  REQUIRE(head <= B200_MAX_HEAD_SIZE, "head_size above %d is not implemented by the B200 kernels", B200_MAX_HEAD_SIZE);
+  REQUIRE(!latent || !v.in(3) || v.in(3)->dtype == out_dt, "fp8 LATENT caches are not implemented by the B200 kernels");
+  const bool process = n->do_rotary || v.in_present(12);
+  const bool encoded = v.in(3) && v.in(3)->dtype != out_dt;
+  if (process || encoded) {
+    const int64_t rows = (process ? num_heads : 0) + 2 * kv_heads;
+    REQUIRE(4 * head * rows <= B200_MAX_PROLOGUE_STAGE_BYTES,
+            "rotary / norm / encoded rows of one token (%lld heads of %lld channels) exceed the B200 append "
+            "prologue's shared memory", (long long)rows, (long long)head);
+  }
 }
 
 // ---------------------------------------------------------------------------------------

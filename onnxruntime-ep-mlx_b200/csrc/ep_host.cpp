@@ -497,7 +497,10 @@ int b200_ep_node_compute_paged(B200EpNode* n, const B200PagedTensors* t, void* s
     const B200NodeInfo& a = n->paged;
     B200PagedAttentionParams p{};
     const int H = (int)a.num_heads, KV = (int)a.kv_num_heads;
-    const bool packed = !t->key && !t->value;
+    const bool latent = fixed_str(a.kv_cache_layout, sizeof a.kv_cache_layout) == "LATENT";
+    const bool packed = !latent && !t->key && !t->value;
+    p.kv_cache_latent = latent;
+    p.v_head_size = latent ? (int32_t)a.v_head_size : 0;
     p.num_heads = H;
     p.kv_num_heads = KV;
     const int heads_in_query = packed ? H + 2 * KV : H;

@@ -522,19 +522,22 @@ void ComputeInfo::run_paged(OrtKernelContext* kctx, void* stream) {
   Bound in[17];
   for (size_t i = 0; i < 17; ++i) in[i] = input(kctx, i);
   const Bound &q = in[0], &kc = in[3], &vc = in[4];
-  if (!q.present || !kc.present || !vc.present || !in[5].present || !in[6].present || !in[7].present)
+  // LATENT (attention.rs:3862-3867): one kv head, no value / value cache; values are key prefixes
+  const bool latent = std::strncmp(paged.kv_cache_layout, "LATENT", sizeof paged.kv_cache_layout) == 0;
+  if (!q.present || !kc.present || (!latent && !vc.present) || !in[5].present || !in[6].present || !in[7].present)
     raise(ORT_INVALID_ARGUMENT, "PagedAttention: query, caches and positional inputs 5-7 must be present");
   if (q.shape.size() != 2 || kc.shape.size() != 4 || in[6].shape.size() != 1 || in[7].shape.size() != 2)
     raise(ORT_INVALID_ARGUMENT, "PagedAttention: query must be rank 2, caches rank 4, past_seqlens rank 1 and "
                                 "block_table rank 2");
   const int64_t H = paged.num_heads, KV = paged.kv_num_heads;
-  const bool packed = !in[1].present && !in[2].present;
+  const bool packed = !latent && !in[1].present && !in[2].present;
   const int64_t heads_in_query = packed ? H + 2 * KV : H;
   if (heads_in_query <= 0 || q.dim(1) % heads_in_query)
     raise(ORT_INVALID_ARGUMENT, "PagedAttention: query hidden size does not match the head count");
   const int64_t D = q.dim(1) / heads_in_query;
+  const int64_t DV = latent && paged.v_head_size > 0 ? paged.v_head_size : D;
 
-  Bound out0 = output(kctx, 0, {q.dim(0), H * D});
+  Bound out0 = output(kctx, 0, {q.dim(0), H * DV});
   Bound out1 = output(kctx, 1, kc.shape);
   Bound out2 = output(kctx, 2, vc.shape);
 

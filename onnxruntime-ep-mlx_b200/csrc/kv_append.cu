@@ -284,8 +284,8 @@ __global__ void __launch_bounds__(32 * kCopyTokensPerCta) kv_append_fused_kernel
 }
 
 bool append_fused_eligible(const PrologueArgs& a) {
-  return a.kv_only && a.slot_mapping != nullptr && !(a.do_norm || a.do_rotary) && a.cache_dtype == a.act_dtype &&
-         a.num_tokens > 0 && a.num_tokens <= kAppendFusedMaxTokens && a.route == nullptr;
+  return a.kv_only && !a.latent && a.slot_mapping != nullptr && !(a.do_norm || a.do_rotary) &&
+         a.cache_dtype == a.act_dtype && a.num_tokens > 0 && a.num_tokens <= kAppendFusedMaxTokens && a.route == nullptr;
 }
 
 cudaError_t launch_append_fused(const PrologueArgs& a, cudaStream_t stream) {
@@ -324,7 +324,7 @@ __global__ void kv_prologue_kernel(PrologueArgs a) {
     qs[j] = load_act(a.query, (int64_t)t * a.query_stride + j, dt);
   for (int j = tid; j < KV * d; j += nthreads) {
     ks[j] = load_act(a.key, (int64_t)t * a.key_stride + j, dt);
-    vs[j] = load_act(a.value, (int64_t)t * a.value_stride + j, dt);
+    if (!a.latent) vs[j] = load_act(a.value, (int64_t)t * a.value_stride + j, dt);
   }
   __syncthreads();
 
@@ -372,7 +372,7 @@ __global__ void kv_prologue_kernel(PrologueArgs a) {
   }
   if (!write) return;
   const int warp = tid >> 5, lane = tid & 31, nwarps = nthreads >> 5;
-  for (int hh = warp; hh < 2 * KV; hh += nwarps) {
+  for (int hh = warp; hh < (a.latent ? KV : 2 * KV); hh += nwarps) {  // LATENT: key rows only
     bool is_key = hh < KV;
     int kh = is_key ? hh : hh - KV;
     write_cache_row(a, is_key, slot, kh, (is_key ? ks : vs) + (int64_t)kh * d, lane, 32);
@@ -389,7 +389,7 @@ void launch_meta_check(const PrologueArgs& a, cudaStream_t stream) {
 
 size_t prologue_smem_bytes(const PrologueArgs& a) {
   const bool process = a.do_norm || a.do_rotary;
-  if (!process && a.cache_dtype == a.act_dtype) return 0;
+  if (!process && a.cache_dtype == a.act_dtype && !a.latent) return 0;  // kv_copy_kernel stages nothing
   int qheads = process && !a.kv_only ? a.num_heads : 0;
   return sizeof(float) * (size_t)a.head_size * (qheads + 2 * a.kv_heads);
 }
@@ -401,7 +401,7 @@ cudaError_t launch_prologue(const PrologueArgs& a, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(kv_prologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  if (!(a.do_norm || a.do_rotary) && a.cache_dtype == a.act_dtype) {
+  if (!(a.do_norm || a.do_rotary) && a.cache_dtype == a.act_dtype && !a.latent) {
     kv_copy_kernel<<<(a.num_tokens + kCopyTokensPerCta - 1) / kCopyTokensPerCta, 32 * kCopyTokensPerCta, 0, stream>>>(a);
     return cudaGetLastError();
   }

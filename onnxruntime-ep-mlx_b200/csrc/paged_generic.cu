@@ -1,5 +1,5 @@
-// Generic paged attention: every form the claim accepts, any head size up to 256, any block
-// size, float / int8 / int4 / fp8 caches.  One CTA (4 warps) per (query token, query head);
+// Generic paged attention: every form the claim accepts, any head size up to 640, any block
+// size, float / int8 / int4 / fp8 caches, SEPARATE or LATENT layout.  One CTA (4 warps) per (query token, query head);
 // the warps split the visible keys and merge their online-softmax states in shared memory.
 //
 // Semantics (rust/src/ops/attention.rs:4124-4320, oracle test_paged_attention.py:119-157):
@@ -9,7 +9,10 @@
 //    [past, total) from the sequence's own new rows; integer / fp8 caches read every key from
 //    the decoded cache (attention.rs:4190-4192);
 //  * scores = scale * q.k, optional softcap * tanh(s / softcap), fp32 softmax with an optional
-//    per-head sink in the denominator (attention.rs:99-118), fp32 accumulation, output in T.
+//    per-head sink in the denominator (attention.rs:99-118), fp32 accumulation, output in T;
+//  * LATENT layout (attention.rs:4058-4062, :4210-4212): one kv head, and the values are the
+//    first v_head channels of the key rows (the host points the value views at the key rows);
+//    the output has v_head channels per head.
 // This kernel is the reference-semantics path used for prefill rows and for shapes the fast
 // kernels do not cover.
 #include "b200_common.cuh"
@@ -30,7 +33,7 @@ __global__ void __launch_bounds__(128) generic_attention_kernel(AttnArgs a) {
   const int c0 = a.cum[b];
   const int nq = a.cum[b + 1] - c0;
   if (a.route && a.route[b] != kRouteGeneric) return;  // another kernel owns this sequence
-  const int D = a.head_size;
+  const int D = a.head_size, VD = a.v_head;
   const int i = t - c0;
   const int past = a.past[b];
   // invalid metadata (flagged by the check kernel): never index outside the new rows
@@ -90,7 +93,7 @@ __global__ void __launch_bounds__(128) generic_attention_kernel(AttnArgs a) {
     for (int e = 0; e < EPL; ++e) {
       int d = lane + 32 * e;
       float vv = 0.f;
-      if (d < D)
+      if (d < VD)
         vv = from_new ? load_act(a.v_new, new_row * a.v_stride + (int64_t)kh * D + d, a.act_dtype)
                       : cache_value(vc, slot, a.kv_heads, kh, d, D, a.block_size);
       o[e] = o[e] * alpha + p * vv;
@@ -120,11 +123,11 @@ __global__ void __launch_bounds__(128) generic_attention_kernel(AttnArgs a) {
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
     int d = lane + 32 * e;
-    if (d >= D) continue;
+    if (d >= VD) continue;
     float acc = 0.f;
     for (int w = 0; w < kWarps; ++w) acc += red_o[w][d] * f[w];
     float y = L > 0.f ? acc / L : 0.f;
-    store_act(a.out, (int64_t)t * a.num_heads * D + (int64_t)h * D + d, y, a.act_dtype);
+    store_act(a.out, (int64_t)t * a.num_heads * VD + (int64_t)h * VD + d, y, a.act_dtype);
   }
 }
 
@@ -136,6 +139,9 @@ cudaError_t launch_generic(const AttnArgs& a, cudaStream_t stream) {
   else if (epl <= 2) generic_attention_kernel<2><<<grid, 128, 0, stream>>>(a);
   else if (epl <= 4) generic_attention_kernel<4><<<grid, 128, 0, stream>>>(a);
   else if (epl <= 8) generic_attention_kernel<8><<<grid, 128, 0, stream>>>(a);
+  else if (epl <= 12) generic_attention_kernel<12><<<grid, 128, 0, stream>>>(a);
+  else if (epl <= 16) generic_attention_kernel<16><<<grid, 128, 0, stream>>>(a);
+  else if (epl <= 20) generic_attention_kernel<20><<<grid, 128, 0, stream>>>(a);
   else return cudaErrorInvalidValue;
   return cudaGetLastError();
 }

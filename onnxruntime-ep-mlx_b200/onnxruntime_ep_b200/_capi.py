@@ -55,6 +55,7 @@ class PagedAttentionParams(ctypes.Structure):
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t), ("device_status", _vp),
         ("decode_min_tiles_per_warp", _i32), ("force_generic", _i32), ("num_sms", _i32),
         ("attention_event_begin", _vp), ("attention_event_end", _vp),
+        ("kv_cache_latent", _i32), ("v_head_size", _i32),
     ]
 
 

@@ -64,12 +64,16 @@ def build_params(query, key, value, key_cache, value_cache, cum, past, block_tab
                  is_causal=1, local_window_size=-1, softcap=0.0, do_rotary=0, rotary_interleaved=0,
                  rotary_offset=0, qk_norm_epsilon=1e-6, k_quant_type="NONE", v_quant_type="NONE",
                  output=None, host_metadata=None, min_tiles_per_warp=0, force_generic=False,
-                 kv_only=False):
-    """Fill a ``B200PagedAttentionParams``.  Returns ``(params, keepalive, output)``."""
+                 kv_only=False, kv_cache_layout="SEPARATE", v_head_size=0):
+    """Fill a ``B200PagedAttentionParams``.  Returns ``(params, keepalive, output)``.
+
+    ``kv_cache_layout="LATENT"``: one kv head, ``value`` and ``value_cache`` are ``None``, and the
+    values are the first ``v_head_size`` channels of the key rows (output ``[nt, H*v_head_size]``)."""
     device = key_cache.device
     H, KV = int(num_heads), int(kv_num_heads)
     keep = []
-    packed = key is None and value is None
+    latent = kv_cache_layout == "LATENT"
+    packed = key is None and value is None and not latent
     if query is None:
         raise _capi.B200Error(_capi.B200_ERR_INVALID_ARGUMENT, "PagedAttention: query is required")
     nt = query.shape[0]
@@ -101,8 +105,14 @@ def build_params(query, key, value, key_cache, value_cache, cum, past, block_tab
         p.key_row_stride = p.value_row_stride = query.stride(0)
     else:
         p.key, p.value = _ptr(key), _ptr(value)
-        p.key_row_stride, p.value_row_stride = key.stride(0), value.stride(0)
+        p.key_row_stride = key.stride(0)
+        p.value_row_stride = value.stride(0) if value is not None else 0
     p.key_cache, p.value_cache = _ptr(key_cache), _ptr(value_cache)
+    dv = d
+    if latent:
+        p.kv_cache_latent = 1
+        p.v_head_size = int(v_head_size)
+        dv = int(v_head_size) or d
 
     cum_d, cum_h = _i32(cum, device)
     past_d, past_h = _i32(past, device)
@@ -154,7 +164,7 @@ def build_params(query, key, value, key_cache, value_cache, cum, past, block_tab
         p.k_scale, p.v_scale = _ptr(k_scale), _ptr(v_scale)
     if not kv_only:
         if output is None:
-            output = torch.empty((nt, H * d), dtype=query.dtype, device=device)
+            output = torch.empty((nt, H * dv), dtype=query.dtype, device=device)
         p.output = _ptr(output)
     p.decode_min_tiles_per_warp = int(min_tiles_per_warp)
     p.force_generic = int(bool(force_generic))

@@ -238,7 +238,7 @@ def paged_attention(q, k, v, key_cache, value_cache, cum, past, block_table,
                     cos=None, sin=None, interleaved=False, rotary_offset=0,
                     q_norm=None, k_norm=None, norm_eps=1e-6,
                     kquant: QuantSpec | None = None, vquant: QuantSpec | None = None,
-                    fp8_scales=None, head_size=None, round_activations=True):
+                    fp8_scales=None, head_size=None, round_activations=True, latent_v_head=None):
     """Reference PagedAttention forward.
 
     Returns ``(output fp32 [nt, H*d], key_cache', value_cache')``; the caches are copies
@@ -249,6 +249,9 @@ def paged_attention(q, k, v, key_cache, value_cache, cum, past, block_table,
     ``round_activations`` rounds the normalised / rotated Q and K rows back to the activation
     dtype after each step, as the reference's MLX ops do (their outputs carry dtype T); the
     reference test oracle keeps them in fp32, which differs only within tolerance.
+    ``latent_v_head`` selects the LATENT layout (attention.rs:4058-4062, :4210-4212,
+    test_paged_attention.py:669-764): one kv head, ``v``/``value_cache`` ``None``, and every
+    value row is the first ``latent_v_head`` channels of the (rotated / normalised) key row.
     """
     H, KV = int(num_heads), int(kv_num_heads)
     q = np.asarray(q)
@@ -267,7 +270,7 @@ def paged_attention(q, k, v, key_cache, value_cache, cum, past, block_table,
     rnd = (lambda a: a.astype(act).astype(np.float32)) if (round_activations and act != np.float32) else (lambda a: a)
     qf = to_f32(q).reshape(nt, H, d)
     kf = to_f32(k).reshape(nt, KV, d)
-    vf = to_f32(v).reshape(nt, KV, -1)
+    vf = to_f32(v).reshape(nt, KV, -1) if latent_v_head is None else None
     if q_norm is not None:
         qf = rnd(rms_norm(qf, to_f32(q_norm), np.float32(norm_eps)).astype(np.float32))
         kf = rnd(rms_norm(kf, to_f32(k_norm), np.float32(norm_eps)).astype(np.float32))
@@ -280,6 +283,8 @@ def paged_attention(q, k, v, key_cache, value_cache, cum, past, block_table,
             pos = np.arange(int(past[b]), int(past[b]) + s1 - s0)
             qf[s0:s1] = rnd(apply_rope(qf[s0:s1], cosf, sinf, pos, interleaved, rotary_offset))
             kf[s0:s1] = rnd(apply_rope(kf[s0:s1], cosf, sinf, pos, interleaved, rotary_offset))
+    if latent_v_head is not None:
+        vf = kf[:, :, :int(latent_v_head)]
 
     pairs = write_slots(cum, past, block_table, slot_mapping, bs)
     if fp8_scales is not None:
@@ -313,7 +318,7 @@ def paged_attention(q, k, v, key_cache, value_cache, cum, past, block_table,
             vals = fp8_decode(vc[blocks, offs], v8[blocks][:, :, None])
         else:
             keys = to_f32(kc[blocks, offs])
-            vals = to_f32(vc[blocks, offs])
+            vals = to_f32(vc[blocks, offs]) if vc is not None else keys[:, :, :vf.shape[-1]]
         if not quantized:
             keys = np.concatenate([keys, kf[s0:s1]], 0)
             vals = np.concatenate([vals, vf[s0:s1]], 0)

@@ -329,3 +329,26 @@ def quant_inputs(case):
         feeds["k_scale"][:] = 1
         feeds["v_scale"][:] = 1
     return feeds
+
+
+# ----------------------------------------------------------------------------------------
+# LATENT layout (test_paged_attention.py:669-764): one kv head, values are the first vd channels
+# of the rotated keys, rotary over channels [offset, offset + rot), explicit scale.
+# ----------------------------------------------------------------------------------------
+LATENT = dict(name="latent_rotary_offset", H=2, KV=1, d=16, vd=8, rot=8, nb=3, blk=4, nt=2, past=3,
+              offset=8, scale=0.2, seed=291)
+
+
+def latent_inputs(case=LATENT):
+    """The reference test's seeded inputs (same draws in the same order)."""
+    h, kv, d, nb, blk, nt = case["H"], case["KV"], case["d"], case["nb"], case["blk"], case["nt"]
+    rng = np.random.default_rng(case["seed"])
+    q = (rng.standard_normal((nt, h * d)) * 0.2).astype(F16)
+    k = (rng.standard_normal((nt, d)) * 0.2).astype(F16)
+    kc = (rng.standard_normal((nb, blk, kv, d)) * 0.2).astype(F16)
+    half = case["rot"] // 2
+    inv = 1.0 / (10000.0 ** (np.arange(half) / half))
+    angles = np.arange(nb * blk)[:, None] * inv[None, :]
+    return dict(query=q, key=k, key_cache=kc, cumulative_sequence_length=np.array([0, nt], I32),
+                past_seqlens=np.array([case["past"]], I32), block_table=np.array([[1, 0, 2]], I32),
+                cos=np.cos(angles).astype(F16), sin=np.sin(angles).astype(F16))

@@ -9,7 +9,7 @@ The reference's oracles live in its test files, which also import onnxruntime / 
 ``ast``, takes only the pure-numpy oracle functions by name and executes them in a private
 namespace holding ``numpy`` and ``math``:
 
-* tests/ops/test_paged_attention.py: ``_rotate_half``, ``_apply_rope``, ``_paged_ref``
+* tests/ops/test_paged_attention.py: ``_rotate_half``, ``_apply_rope``, ``_apply_rope_offset``, ``_paged_ref``
   (:27-158) and ``_inputs`` (:182-209, the reference's seeded input generator);
 * tests/ops/test_quantized_kv.py: ``_encode``, ``_decode``, ``_scores``, ``_scales``,
   ``_paged_ref`` (:22-78, :395-450);
@@ -81,7 +81,7 @@ def main() -> None:
     ops = os.path.join(args.reference, "tests", "ops")
 
     paged = load_functions(os.path.join(ops, "test_paged_attention.py"),
-                           ["_rotate_half", "_apply_rope", "_paged_ref", "_inputs"])
+                           ["_rotate_half", "_apply_rope", "_apply_rope_offset", "_paged_ref", "_inputs"])
     gqa = load_functions(os.path.join(ops, "test_gqa_position_cache.py"), ["_rotate"])
     quant = load_functions(os.path.join(ops, "test_quantized_kv.py"),
                            ["_encode", "_decode", "_scores", "_scales", "_paged_ref"],
@@ -136,6 +136,37 @@ def main() -> None:
         store[f"{name}/pk"] = pk
         store[f"{name}/pv"] = pv
         print(f"{name}: output {out.shape}")
+
+    # LATENT layout (test_paged_attention.py:669-764): the reference's _apply_rope_offset on the
+    # new rows, then the test's own expectation (values = the first vd channels of the keys).
+    lat = cases.LATENT
+    feeds = cases.latent_inputs()
+    h, kv, d, vd, nt, past_len = lat["H"], lat["KV"], lat["d"], lat["vd"], lat["nt"], lat["past"]
+    cos32, sin32 = feeds["cos"].astype(np.float32), feeds["sin"].astype(np.float32)
+    positions = np.arange(past_len, past_len + nt)
+    qh = paged["_apply_rope_offset"](feeds["query"].reshape(nt, h, d).astype(np.float32), cos32, sin32, positions, 0,
+                                     lat["offset"])
+    kh_new = paged["_apply_rope_offset"](feeds["key"].reshape(nt, kv, d).astype(np.float32), cos32, sin32, positions,
+                                         0, lat["offset"])
+    kc, bt, blk = feeds["key_cache"], feeds["block_table"], lat["blk"]
+    expected_cache = kc.copy()
+    for i in range(nt):
+        logical = past_len + i
+        expected_cache[bt[0, logical // blk], logical % blk, 0] = kh_new[i, 0].astype(np.float16)
+    keys = np.empty((past_len + nt, d), dtype=np.float32)
+    for logical in range(past_len):
+        keys[logical] = kc[bt[0, logical // blk], logical % blk, 0]
+    keys[past_len:] = kh_new[:, 0]
+    scores = np.einsum("thd,kd->htk", qh, keys) * lat["scale"]
+    cols = np.arange(past_len + nt)[None, :]
+    rows = (past_len + np.arange(nt))[:, None]
+    scores = np.where((cols > rows)[None], -np.inf, scores)
+    probs = np.exp(scores - scores.max(-1, keepdims=True))
+    probs /= probs.sum(-1, keepdims=True)
+    store["latent/digest"] = np.array(digest(cases.input_arrays(feeds)))
+    store["latent/output"] = np.einsum("htk,kv->thv", probs, keys[:, :vd]).reshape(nt, h * vd).astype(np.float32)
+    store["latent/key_cache"] = expected_cache
+    print(f"latent: output {store['latent/output'].shape}")
 
     # Byte-equation known answers (test_quantized_kv.py:479-494 values, both bit widths).
     values = np.array([-1024, -128.5, -8.5, -7.5, -2.5, -1.5, -0.5, 0.5,

@@ -10,6 +10,7 @@ from onnxruntime_ep_b200 import _capi
 
 F16, BF16, F32, I32, I8, U8 = (_capi.DTYPE_FLOAT16, _capi.DTYPE_BFLOAT16, _capi.DTYPE_FLOAT,
                                _capi.DTYPE_INT32, _capi.DTYPE_INT8, _capi.DTYPE_UINT8)
+F8 = _capi.DTYPE_FLOAT8E4M3FN
 
 
 def tensor(info, dtype, shape):
@@ -114,11 +115,55 @@ def test_integer_cache_claim():
 
 
 def test_forms_not_implemented_are_declined_with_reason():
-    n = node(d=320)
+    n = node(d=1024)
     ok, why = claim(n)
-    assert ok == 0 and "head_size above 256" in why
-    n = node(KV=1, H=2)
+    assert ok == 0 and "head_size above 640" in why
+    # the append prologue stages 4 bytes x head x (heads + 2 kv heads) per token for RoPE
+    n = node(H=128, KV=1, d=512)
+    n.do_rotary = 1
+    tensor(n.inputs[8], F16, [4096, 32])
+    tensor(n.inputs[9], F16, [4096, 32])
+    n.num_inputs = 10
+    ok, why = claim(n)
+    assert ok == 0 and "prologue's shared memory" in why
+    assert claim(latent_node(cache_dt=F8))[0] == 0  # encoded LATENT caches stay with ORT
+
+
+def latent_node(H=2, d=16, vd=8, cache_dt=None, nb=3, bs=4, maxb=3):
+    """The reference's LATENT case (test_paged_attention.py:669-764): one kv head, value and
+    value_cache absent, v_head_size < head_size with an explicit scale."""
+    n = node(H=H, KV=1, d=d, nb=nb, bs=bs, B=1, maxb=maxb, cache_dt=cache_dt)
     n.kv_cache_layout = b"LATENT"
     n.inputs[2].present = n.inputs[4].present = 0
+    n.v_head_size = vd
+    n.has_scale, n.scale = 1, 0.2
+    tensor(n.outputs[0], F16, [-1, H * vd])
+    if cache_dt == F8:
+        n.k_cache_dtype = b"float8e4m3"
+        tensor(n.inputs[14], F32, [nb, 1])
+        n.num_inputs = 16
+    return n
+
+
+def test_latent_layout_is_claimed():
+    assert claim(latent_node()) == (1, "")
+    n = latent_node()
+    n.do_rotary, n.rotary_offset = 1, 8
+    tensor(n.inputs[8], F16, [12, 4])
+    tensor(n.inputs[9], F16, [12, 4])
+    n.num_inputs = 10
+    assert claim(n) == (1, "")
+    # MLA-like geometry: 576-channel keys, 512-channel values, 16 heads
+    assert claim(latent_node(H=16, d=576, vd=512))[0] == 1
+
+
+@pytest.mark.parametrize("mutate,reason", [
+    (lambda n: setattr(n, "kv_num_heads", 2), "LATENT layout requires kv_num_heads=1"),
+    (lambda n: setattr(n, "has_scale", 0), "asymmetric value heads requires an explicit scale"),
+    (lambda n: setattr(n, "v_head_size", 32), "LATENT v_head_size must not exceed head_size"),
+])
+def test_latent_layout_rules(mutate, reason):
+    n = latent_node()
+    mutate(n)
     ok, why = claim(n)
-    assert ok == 0 and "LATENT" in why
+    assert ok == 0 and reason in why, why

@@ -222,3 +222,51 @@ def test_data_transfer_round_trip(ep):
     torch.cuda.synchronize()
     assert ep.copy(oh.F32, (4096,), d.data_ptr(), a.nbytes, (4096,), back.ctypes.data, a.nbytes) == 0
     assert np.array_equal(back, 2 * a)
+
+
+def test_latent_node_through_the_glue(ep):
+    """The reference's LATENT case (test_paged_attention.py:669-764) as ORT would hand it over:
+    value / value_cache absent, a key_cache_out output, output [nt, H * v_head_size]."""
+    import cases
+
+    golden = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden",
+                                                "paged_golden.npz"))
+    lat = cases.LATENT
+    feeds = cases.latent_inputs()
+    H, d, vd, nt = lat["H"], lat["d"], lat["vd"], lat["nt"]
+    g = oh.Graph()
+    ctx = oh.KernelContext()
+    try:
+        n = g.node("PagedAttention", "lat")
+        n.input("lat.q", oh.F16, (-1, H * d)).input("lat.k", oh.F16, (-1, d)).input(None)
+        n.input("lat.kc", oh.F16, feeds["key_cache"].shape).input(None)
+        n.input("lat.cum", oh.I32, (2,)).input("lat.past", oh.I32, (1,)).input("lat.bt", oh.I32, (1, 3))
+        n.input("lat.cos", oh.F16, feeds["cos"].shape).input("lat.sin", oh.F16, feeds["sin"].shape)
+        n.output("lat.out", oh.F16, (-1, H * vd)).output("lat.kc_out", oh.F16, feeds["key_cache"].shape)
+        for k, v in dict(num_heads=H, kv_num_heads=1, v_head_size=vd, kv_cache_layout="LATENT", do_rotary=1,
+                         rotary_offset=lat["offset"], scale=float(lat["scale"])).items():
+            n.attr(k, v)
+        rc, claimed, _ = ep.capability(g)
+        assert rc == 0 and claimed == [0], ep.report()
+        idx = ep.compile(g, 0)
+        assert idx >= 0, oh.last_error()
+        dev = {k: to_dev(v) for k, v in feeds.items()}
+        for name, key, dt in (("q", "query", oh.F16), ("k", "key", oh.F16), ("kc", "key_cache", oh.F16),
+                              ("cum", "cumulative_sequence_length", oh.I32), ("past", "past_seqlens", oh.I32),
+                              ("bt", "block_table", oh.I32), ("cos", "cos", oh.F16), ("sin", "sin", oh.F16)):
+            _bind(ctx, f"lat.{name}", dev[key], dt)
+        out = torch.empty((nt, H * vd), dtype=torch.float16, device="cuda")
+        kco = torch.empty_like(dev["key_cache"])
+        ctx.output("lat.out", oh.F16, (nt, H * vd), out.data_ptr(), out.numel() * 2)
+        ctx.output("lat.kc_out", oh.F16, tuple(kco.shape), kco.data_ptr(), kco.numel() * 2)
+        rc = ep.compute(idx, ctx)
+        assert rc == 0, oh.last_error()
+        assert ctx.requested("lat.out") == (nt, H * vd)
+        want_cache = golden["latent/key_cache"].view(np.uint16)
+        assert np.array_equal(kco.cpu().numpy().view(np.uint16), want_cache)
+        assert np.array_equal(dev["key_cache"].cpu().numpy().view(np.uint16), want_cache)
+        rep = tolerance.report(out.float().cpu().numpy(), golden["latent/output"], bits=11)
+        assert rep["max_excess"] <= 2e-3, rep
+    finally:
+        ctx.close()
+        g.close()

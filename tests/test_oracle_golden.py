@@ -124,3 +124,22 @@ def test_c_oracle_matches_reference_float(case):
     out16 = cpu_oracle.paged_attention(feeds["query"], feeds["key"], feeds["value"], feeds["key_cache"].copy(),
                                        feeds["value_cache"].copy(), *meta, case["H"], case["KV"], **call)
     np.testing.assert_array_equal(out16, out32.astype(out16.dtype))
+
+
+def latent_oracle(feeds, case=cases.LATENT):
+    return ref.paged_attention(
+        feeds["query"], feeds["key"], None, feeds["key_cache"], None, feeds["cumulative_sequence_length"],
+        feeds["past_seqlens"], feeds["block_table"], case["H"], case["KV"], scale=case["scale"],
+        cos=feeds["cos"], sin=feeds["sin"], rotary_offset=case["offset"], latent_v_head=case["vd"])
+
+
+def test_oracle_matches_reference_latent():
+    """LATENT layout (test_paged_attention.py:669-764): values are the first vd channels of the
+    rotated keys; the appended key rows are bit-exact, the output within the activation rounding
+    of the rotated rows (the reference test keeps them in fp32)."""
+    feeds = cases.latent_inputs()
+    assert digest(cases.input_arrays(feeds)) == str(GOLDEN["latent/digest"])
+    out, kc, vc = latent_oracle(feeds)
+    assert vc is None
+    np.testing.assert_array_equal(kc.view(np.uint16), GOLDEN["latent/key_cache"].view(np.uint16))
+    np.testing.assert_allclose(out, GOLDEN["latent/output"], rtol=2e-3, atol=2e-3)
