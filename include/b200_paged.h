@@ -295,6 +295,12 @@ typedef struct B200GqaParams {
   const int64_t* position_ids;   /* device int64 [batch, position_ids_width] or NULL     */
   const int64_t* host_position_ids; /* host copy, required with position_ids (validation) */
   int32_t position_ids_width;
+  /* attention_bias (input 10, attention.rs:637-652, :746-755): added to the (soft-capped)
+   * scores of the visible keys, element [bias_batch == 1 ? 0 : b, bias_heads == 1 ? 0 : h, s,
+   * key], in dtype; NULL = none.  Shape [bias_batch (1 or batch), bias_heads (1 or num_heads),
+   * bias_seq (== seq), bias_total (== total_sequence_length)], row-major. */
+  const void* attention_bias;
+  int32_t bias_batch, bias_heads, bias_seq, bias_total;
 } B200GqaParams;
 
 B200_API int b200_gqa_params_size(void);
@@ -310,8 +316,8 @@ B200_API int b200_group_query_attention(const B200GqaParams* p, void* stream);
 B200_API int b200_group_query_attention_read_status(const B200GqaParams* p, void* stream);
 
 /* Claim predicate, restating group_query_attention_claim (attention.rs:2407-2754) over a
- * plain node description, plus this build's own declines (attention_bias, qk_output,
- * sliding_window_cache, integer caches, q/k norm, head size).  Returns 1 (claim) or 0
+ * plain node description, plus this build's own declines (qk_output, sliding_window_cache,
+ * integer caches, q/k norm, head size).  Returns 1 (claim) or 0
  * (decline, reason written to `reason`). */
 typedef struct B200GqaNodeInfo {
   int32_t num_inputs;

@@ -315,6 +315,8 @@ void gqa_claim(const GView& v) {
     if (!t) deny("input %d lacks tensor type/shape info", idx);
     REQUIRE(t->dtype == out_type, "input %d must have output dtype %s, got %s", idx, dtype_name(out_type), dtype_name(t->dtype));
   }
+  if (has_bias)  // attention.rs:2546-2560
+    REQUIRE(v.in(10)->rank == 4, "attention_bias (input 10) must have rank 4, got rank %d", v.in(10)->rank);
   for (int idx = 1; idx < std::min(n.num_outputs, 3); ++idx) {
     if (!v.out_present(idx)) continue;
     const int want = v.in(idx + 2) ? v.in(idx + 2)->dtype : out_type;
@@ -382,7 +384,6 @@ void gqa_claim(const GView& v) {
   REQUIRE(std::isfinite(n.softcap) && n.softcap >= 0.f, "softcap must be finite and non-negative");
   // Forms the reference accepts that this build does not implement (the node stays on ORT).
   REQUIRE(!sliding, "sliding_window_cache is not implemented on B200");
-  REQUIRE(!has_bias, "attention_bias is not implemented on B200");
   REQUIRE(n.qk_output == 0, "qk_output diagnostics are not implemented on B200");
   REQUIRE(!quantized && n.kv_cache_bit_width == 0, "integer GroupQueryAttention caches are not implemented on B200");
   REQUIRE(!v.in_present(14), "q/k RMS norm inside GroupQueryAttention is not implemented on B200");

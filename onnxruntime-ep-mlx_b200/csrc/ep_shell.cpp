@@ -640,8 +640,9 @@ void ComputeInfo::run_gqa(OrtKernelContext* kctx, void* stream) {
   Bound out1 = output(kctx, 1, {B, KV, pcap, D});
   Bound out2 = output(kctx, 2, {B, KV, pcap, D});
 
-  staging.plan({&in[0], &in[1], &in[2], &in[3], &in[4], &in[5], &in[7], &in[8], &in[9], &in[11], &out0, &out1, &out2});
-  for (int i : {0, 1, 2, 3, 4, 5, 7, 8, 9, 11}) staging.place(&in[i], true, false, stream);
+  staging.plan({&in[0], &in[1], &in[2], &in[3], &in[4], &in[5], &in[7], &in[8], &in[9], &in[10], &in[11], &out0, &out1,
+                &out2});
+  for (int i : {0, 1, 2, 3, 4, 5, 7, 8, 9, 10, 11}) staging.place(&in[i], true, false, stream);
   staging.place(&out0, false, true, stream);
   staging.place(&out1, false, true, stream);
   staging.place(&out2, false, true, stream);
@@ -674,6 +675,15 @@ void ComputeInfo::run_gqa(OrtKernelContext* kctx, void* stream) {
   if (static_cast<int64_t>(seqlens.size()) < B)
     raise(ORT_INVALID_ARGUMENT, "GroupQueryAttention: seqlens_k must hold batch_size values");
   p.head_sink = in[11].dev;
+  if (in[10].present) {  // attention_bias [1|B, 1|H, S, total]
+    if (in[10].shape.size() != 4)
+      raise(ORT_EP_FAIL, "GroupQueryAttention: attention_bias must broadcast to [batch,heads,sequence,total]");
+    p.attention_bias = in[10].dev;
+    p.bias_batch = in[10].dim32(0);
+    p.bias_heads = in[10].dim32(1);
+    p.bias_seq = in[10].dim32(2);
+    p.bias_total = in[10].dim32(3);
+  }
   p.output = out0.dev;
   if (gqa.do_rotary && in[7].present) {
     p.rotary_dim = 2 * in[7].dim32(1);

@@ -56,6 +56,8 @@ struct GqaArgs {
   void* ov;
   const int32_t* seqlens;
   const void* sink;
+  const void* bias;                       // attention_bias [Bb, Hb, S, total] or null
+  int64_t bias_bstride, bias_hstride;     // 0 for a broadcast (size-1) dimension
   void* out;
   int row_tiles, splits, fused_copy, present_separate;
   float* part_o;   // [groups][splits][R][D]
@@ -149,6 +151,7 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
   __shared__ float m_run[R], l_run[R], alpha_s[R];
   __shared__ int row_pos[R];  // absolute position of each row, or -1 (padding row)
   __shared__ int row_end[R], row_start[R];
+  __shared__ int64_t row_bias[R];  // attention_bias offset of each row's [total] bias row
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int idx = blockIdx.x;
@@ -183,6 +186,7 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
       row_pos[tid] = pos;
       row_end[tid] = end;
       row_start[tid] = a.window > 0 ? max(0, end - a.window) : 0;
+      row_bias[tid] = b * a.bias_bstride + (int64_t)(kh * g + rho % g) * a.bias_hstride + (int64_t)(rho / g) * a.total;
     } else {
       row_pos[tid] = -1;
       row_end[tid] = 0;
@@ -264,6 +268,7 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
         if (row_pos[r] >= 0 && pos >= row_start[r] && pos < row_end[r]) {
           s = acc[r];
           if (a.softcap > 0.f) s = a.softcap * tanhf(s * a.scale / a.softcap) * kLog2e;
+          if (a.bias) s += to_f(static_cast<const T*>(a.bias)[row_bias[r] + pos]) * kLog2e;
         }
         sc[r][kk] = s;
       }
@@ -477,6 +482,7 @@ __global__ void __launch_bounds__(kClThreads) gqa_cluster_kernel(const GqaArgs a
   extern __shared__ __align__(16) uint8_t cl_smem[];
   __shared__ float m_run[R], l_run[R], alpha_s[R];
   __shared__ int row_pos[R], row_end[R];
+  __shared__ int64_t row_bias[R];  // attention_bias offset of each row's [total] bias row
   __shared__ __align__(8) uint64_t bar_k, bar_v;
 
   // Scores: LPK lanes per key, each holding the q values of UPL 4-channel units (units
@@ -505,6 +511,7 @@ __global__ void __launch_bounds__(kClThreads) gqa_cluster_kernel(const GqaArgs a
       const int pos = bg.query_past + tid / g;
       row_pos[tid] = pos;
       row_end[tid] = a.causal ? min(pos + 1, bg.length) : bg.length;
+      row_bias[tid] = b * a.bias_bstride + (int64_t)(kh * g + tid % g) * a.bias_hstride + (int64_t)(tid / g) * a.total;
     } else {
       row_pos[tid] = -1;
       row_end[tid] = 0;
@@ -624,6 +631,7 @@ __global__ void __launch_bounds__(kClThreads) gqa_cluster_kernel(const GqaArgs a
           if (row_pos[r] >= 0 && pos < row_end[r]) {
             s = acc[r];
             if (a.softcap > 0.f) s = a.softcap * tanhf(s * a.scale / a.softcap) * kLog2e;
+            if (a.bias) s += to_f(static_cast<const T*>(a.bias)[row_bias[r] + pos]) * kLog2e;
           }
           sc[r * kc + k] = s;
         }
@@ -931,6 +939,11 @@ int check_gqa(const B200GqaParams* p) {
     if (p->position_ids && !p->host_position_ids)
       return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: position_ids need their host copy (host_position_ids)");
   }
+  // attention.rs:637-652
+  if (p->attention_bias &&
+      ((p->bias_batch != 1 && p->bias_batch != p->batch) || (p->bias_heads != 1 && p->bias_heads != p->num_heads) ||
+       p->bias_seq != p->seq || p->bias_total != p->total_sequence_length))
+    return gfail(B200_ERR_FAIL, "GroupQueryAttention: attention_bias must broadcast to [batch,heads,sequence,total]");
   // attention.rs:992-997
   if (p->new_seq != p->seq && (p->new_seq != 0 || !p->past_key))
     return gfail(B200_ERR_FAIL, "GroupQueryAttention: K/V must match Q sequence or be empty with paired non-sliding past");
@@ -1220,6 +1233,12 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
     a.ov = p->present_value;
     a.seqlens = p->seqlens_k;
     a.sink = p->head_sink;
+    if (p->attention_bias) {
+      a.bias = p->attention_bias;
+      const int64_t plane = (int64_t)p->seq * p->bias_total;
+      a.bias_hstride = p->bias_heads == 1 ? 0 : plane;
+      a.bias_bstride = p->bias_batch == 1 ? 0 : plane * p->bias_heads;
+    }
     a.out = p->output;
     a.row_tiles = P.row_tiles;
     a.splits = P.splits;

@@ -98,6 +98,8 @@ class GqaParams(ctypes.Structure):
         ("do_rotary", _i32), ("rotary_interleaved", _i32), ("rotary_dim", _i32), ("rotary_positions", _i32),
         ("cos_cache", _vp), ("sin_cache", _vp), ("position_ids", _vp), ("host_position_ids", _vp),
         ("position_ids_width", _i32),
+        ("attention_bias", _vp), ("bias_batch", _i32), ("bias_heads", _i32), ("bias_seq", _i32),
+        ("bias_total", _i32),
     ]
 
 

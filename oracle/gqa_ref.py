@@ -63,12 +63,14 @@ def rotary_positions(b, seq, query_past, total, position_ids):
 def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_heads, kv_num_heads,
                           scale=None, causal=True, window=-1, softcap=0.0, sink=None,
                           smooth_softmax=-1, cos=None, sin=None, position_ids=None, interleaved=False,
-                          out_dtype=None):
+                          out_dtype=None, bias=None):
     """Returns ``(output [B,S,H*D], present_k, present_v [B,KV,max(cap,total),D])``.
 
     ``q`` [B,S,H*D]; ``k``/``v`` [B,new_seq,KV*D] (new_seq may be 0); ``past_k``/``past_v``
     [B,KV,cap,D] or None; ``cos``/``sin`` [positions, rotary_dim/2] turn on the rotary
-    embedding of the new query and key rows (``position_ids`` [B, >=S] optional).  Arrays keep
+    embedding of the new query and key rows (``position_ids`` [B, >=S] optional).  ``bias``
+    [1|B, 1|H, S, total] is added to the (soft-capped) scores of the visible keys
+    (test_gqa_position_cache.py:119-121, attention.rs:746-755).  Arrays keep
     their dtype; math is fp32, the output is rounded to the activation dtype (or kept in
     ``out_dtype``, e.g. fp32 for tolerance checks)."""
     B, S, hidden = q.shape
@@ -113,6 +115,8 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
         scores = qh @ keys.transpose(0, 2, 1) * np.float32(scale)
         if softcap > 0:
             scores = softcap * np.tanh(scores / softcap)
+        if bias is not None:
+            scores = scores + np.asarray(bias)[0 if bias.shape[0] == 1 else b, :, :, :length].astype(np.float32)
         end = np.minimum(query_past + np.arange(S) + 1, length) if causal else np.full(S, length)
         start = np.maximum(0, end - window) if window > 0 else np.zeros(S, int)
         cols = np.arange(length)[None]

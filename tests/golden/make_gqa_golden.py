@@ -63,6 +63,25 @@ CASES += [
     ("rot_past_only", "float32", 2, 1, 0, 6, [4, 6], 6, True, -1, False),
 ]
 
+# attention_bias cases (input 10, test_gqa_position_cache.py:48-50, :119-121): name ->
+# (bias batch dim, bias head dim); U(-2, 2) like the reference's feeds, broadcast over a size-1
+# batch or head dimension.
+BIAS = {
+    "bias_prefill": (1, HEADS),
+    "bias_broadcast": (1, 1),
+    "bias_decode_composed_fp16": (2, HEADS),
+    "bias_rot_window": (2, 1),
+    "bias_past_only": (2, HEADS),
+}
+CASES += [
+    ("bias_prefill", "float32", 1, 2, 2, 6, [4], 4, True, -1, False),
+    ("bias_broadcast", "float32", 2, 2, 2, 6, [3, 6], 6, True, -1, False),
+    ("bias_decode_composed_fp16", "float16", 2, 1, 1, 8, [5, 8], 8, True, -1, True),
+    ("bias_rot_window", "float32", 2, 3, 3, 9, [7, 9], 9, True, 3, False),
+    ("bias_past_only", "float32", 2, 1, 0, 6, [4, 6], 6, True, -1, False),
+]
+ROTARY["bias_rot_window"] = (16, False, [[1, 2, 3], [4, 5, 6]])
+
 
 def load_reference(path):
     with open(path) as f:
@@ -102,6 +121,12 @@ def add_rotary(feeds, index, half, ids, dtype):
     return feeds
 
 
+def add_bias(feeds, index, shape, seq, total, dtype):
+    rng = np.random.default_rng(2365 + index)
+    feeds["bias"] = rng.uniform(-2, 2, (shape[0], shape[1], seq, total)).astype(np.dtype(dtype))
+    return feeds
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
@@ -114,6 +139,8 @@ def main():
         if name in ROTARY:
             half, interleaved, ids = ROTARY[name]
             add_rotary(feeds, i, half, ids, dtype)
+        if name in BIAS:
+            add_bias(feeds, i, BIAS[name], seq, total, dtype)
         out, pk, pv = ref(feeds, causal=causal, window=window, composed=composed, interleaved=interleaved)
         for key, val in feeds.items():
             arrays[f"{name}/in/{key}"] = val

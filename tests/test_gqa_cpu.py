@@ -133,9 +133,20 @@ def test_reference_rotary_declines(mutate, reason):
     assert ok == 0 and why.startswith(reason), why
 
 
+def test_attention_bias_is_claimed():
+    n = gnode()
+    n.num_inputs = 11
+    tensor(n.inputs[10], F32, [1, 1, 1, 2049])
+    assert claim(n) == (1, "")
+    tensor(n.inputs[10], F32, [1, 2049])
+    ok, why = claim(n)
+    assert ok == 0 and "attention_bias (input 10) must have rank 4" in why
+    tensor(n.inputs[10], F16, [1, 1, 1, 2049])
+    ok, why = claim(n)
+    assert ok == 0 and "input 10 must have output dtype" in why
+
+
 @pytest.mark.parametrize("mutate,reason", [
-    (lambda n: (setattr(n, "num_inputs", 11), tensor(n.inputs[10], F32, [1, 1, 1, 2049])),
-     "attention_bias is not implemented on B200"),
     (lambda n: (tensor(n.inputs[3], I8, [1, 8, 2048, 128]), tensor(n.inputs[4], I8, [1, 8, 2048, 128]),
                 tensor(n.outputs[1], I8, [1, 8, -1, 128]), tensor(n.outputs[2], I8, [1, 8, -1, 128])),
      "integer GroupQueryAttention caches are not implemented on B200"),

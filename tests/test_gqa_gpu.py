@@ -71,6 +71,8 @@ def test_golden_cases(case, in_place):
     if "cos" in f:  # rotary: cos / sin caches, optional position ids (host copy for validation)
         kw.update(do_rotary=1, rotary_interleaved=int(case.get("interleaved", False)), cos_cache=dev(f["cos"]),
                   sin_cache=dev(f["sin"]), position_ids=f.get("pos"))
+    if "bias" in f:  # attention_bias [1|B, 1|H, S, total]
+        kw["attention_bias"] = dev(f["bias"])
     out, ok, ov = gqa.group_query_attention(q, k, v, pk, pv, lengths, int(f["total"][0]), sink, check_status=True, **kw)
     torch.cuda.synchronize()
     check(host(out), GOLDEN[f"{name}/out/output"], case["dtype"])
@@ -80,7 +82,7 @@ def test_golden_cases(case, in_place):
 
 def run_case(rng, *, dtype="bfloat16", B=1, S=1, H=32, KV=8, D=128, cap=2048, lengths=None, total=None,
              causal=1, window=-1, softcap=0.0, sink=False, smooth=-1, packed=False, new_rows=True, past=True,
-             in_place=False, rotary=None):
+             in_place=False, rotary=None, bias=None):
     npdt = np.float32
     lengths = [cap + S] * B if lengths is None else lengths
     B = len(lengths)
@@ -115,14 +117,21 @@ def run_case(rng, *, dtype="bfloat16", B=1, S=1, H=32, KV=8, D=128, cap=2048, le
             cast = lambda a: None if a is None else a.astype(ndt)
             qn, kn, vn, pkr, pvr, skr = map(cast, (qn, kn, vn, pkr, pvr, skr))
             rot.update(cos=cast(rot["cos"]), sin=cast(rot["sin"]))
+    bias_t = bias_n = None
+    if bias is not None:  # (batch dim, head dim) of an attention_bias [1|B, 1|H, S, total]
+        bias_t = to(rng.uniform(-2, 2, (bias[0], bias[1], S, total)).astype(npdt))
+        bias_n = back(bias_t)
+        if dtype != "float32":
+            import ml_dtypes
+            bias_n = bias_n.astype(np.float16 if dtype == "float16" else ml_dtypes.bfloat16)
     want, wk, wv = gqa_ref.group_query_attention(
         qn, kn if new_rows else None, vn if new_rows else None, pkr, pvr, np.asarray(lengths) - 1, total,
         num_heads=H, kv_num_heads=KV, causal=bool(causal), window=window, softcap=softcap, sink=skr,
-        smooth_softmax=smooth, out_dtype=np.float32, **rot)
+        smooth_softmax=smooth, out_dtype=np.float32, bias=bias_n, **rot)
     want, wk, wv = (np.asarray(x, np.float32) for x in (want, wk, wv))
     lens = torch.tensor(np.asarray(lengths) - 1, dtype=torch.int32, device=DEV)
     kw = dict(num_heads=H, kv_num_heads=KV, causal=causal, local_window_size=window, softcap=softcap,
-              smooth_softmax=smooth, **kw_rot)
+              smooth_softmax=smooth, attention_bias=bias_t, **kw_rot)
     if in_place:
         kw.update(present_key=pkt, present_value=pvt)
     if packed:
@@ -215,3 +224,22 @@ def test_rotary_prefill_rows_and_past_only():
     run_case(np.random.default_rng(24), S=40, cap=64, lengths=[104, 45], H=8, KV=2, rotary=(32, True, None))
     run_case(np.random.default_rng(25), S=1, cap=500, lengths=[500, 321], new_rows=False,
              rotary=(64, False, np.array([[499], [320]], np.int64)))
+
+
+# ---- attention_bias (input 10) ------------------------------------------------------------
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_config1_with_bias(dtype):
+    """Config-1 shapes (the one-wave cluster kernel) with a per-head bias over the 2049 keys."""
+    run_case(np.random.default_rng(31), dtype=dtype, cap=2048, lengths=[2049], bias=(1, 32))
+
+
+@pytest.mark.parametrize("shape", [(2, 8), (1, 1), (2, 1)])
+def test_bias_prefill_rows_and_broadcast(shape):
+    """Prefill rows (the split-K attention kernel) with batch / head broadcast and a window."""
+    run_case(np.random.default_rng(32), dtype="float16", S=24, cap=64, lengths=[88, 50], H=8, KV=2, window=16,
+             bias=shape)
+
+
+def test_bias_with_softcap_sink_and_rotary():
+    run_case(np.random.default_rng(33), dtype="bfloat16", S=3, cap=128, lengths=[131, 90], H=16, KV=4,
+             softcap=30.0, sink=True, rotary=(64, False, None), bias=(2, 16))

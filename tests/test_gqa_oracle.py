@@ -1,5 +1,5 @@
 """oracle/gqa_ref.py against the reference's own GroupQueryAttention oracle
-(tests/ops/test_gqa_position_cache.py:88-134, rotary :71-85), fixtures in
+(tests/ops/test_gqa_position_cache.py:88-134, rotary :71-85, attention_bias :119-121), fixtures in
 tests/golden/gqa_golden.npz."""
 
 import json
@@ -27,7 +27,7 @@ def test_oracle_matches_reference_oracle(case):
         f["q"], f["k"] if case["new_seq"] else None, f["v"] if case["new_seq"] else None, f["pk"], f["pv"],
         f["lengths"], f["total"], num_heads=4, kv_num_heads=2, causal=case["causal"], window=case["window"],
         softcap=0.7 if case["composed"] else 0.0, sink=f.get("sink"), cos=f.get("cos"), sin=f.get("sin"),
-        position_ids=f.get("pos"), interleaved=case.get("interleaved", False))
+        position_ids=f.get("pos"), interleaved=case.get("interleaved", False), bias=f.get("bias"))
     tol = 1e-5 if case["dtype"] == "float32" else 2e-3
     want = DATA[f"{case['name']}/out/output"]
     np.testing.assert_allclose(out.astype(np.float32), want.astype(np.float32), rtol=tol, atol=tol)
