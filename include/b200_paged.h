@@ -301,6 +301,12 @@ typedef struct B200GqaParams {
    * bias_seq (== seq), bias_total (== total_sequence_length)], row-major. */
   const void* attention_bias;
   int32_t bias_batch, bias_heads, bias_seq, bias_total;
+  /* q/k RMS norm (inputs 14 / 15, attention.rs:1070-1078): every query head and every new key
+   * head is x / sqrt(mean(x^2) + qk_norm_epsilon) * weight, rounded to dtype, before the rotary
+   * embedding; weights [head_size] in dtype, both or neither. */
+  const void* q_norm_weight;
+  const void* k_norm_weight;
+  float qk_norm_epsilon;      /* 0 -> 1e-6                                               */
 } B200GqaParams;
 
 B200_API int b200_gqa_params_size(void);
@@ -317,7 +323,7 @@ B200_API int b200_group_query_attention_read_status(const B200GqaParams* p, void
 
 /* Claim predicate, restating group_query_attention_claim (attention.rs:2407-2754) over a
  * plain node description, plus this build's own declines (qk_output, sliding_window_cache,
- * integer caches, q/k norm, head size).  Returns 1 (claim) or 0
+ * integer caches, head size).  Returns 1 (claim) or 0
  * (decline, reason written to `reason`). */
 typedef struct B200GqaNodeInfo {
   int32_t num_inputs;
@@ -330,6 +336,8 @@ typedef struct B200GqaNodeInfo {
   float softcap;
   int32_t has_scale;         /* 0 = attribute absent: 1/sqrt(head_size)                      */
   float scale;
+  int32_t has_qk_norm_epsilon; /* 0 = attribute absent: 1e-6                                 */
+  float qk_norm_epsilon;
 } B200GqaNodeInfo;
 
 B200_API int b200_group_query_attention_claim(const B200GqaNodeInfo* node, char* reason, size_t reason_len);

@@ -378,6 +378,10 @@ void gqa_claim(const GView& v) {
     REQUIRE(s->dtype == out_type && s->rank == 1 && s->shape[0] == nh, "head_sink must be [num_heads] in activation dtype");
   }
   REQUIRE(v.in_present(14) == v.in_present(15), "q_norm_weight and k_norm_weight must be provided together");
+  if (v.in_present(14)) {  // attention.rs:2703-2725
+    for (int idx : {14, 15})
+      REQUIRE(shape_is(v.in(idx), {head}), "Q/K norm weight %d must have shape [head_size=%lld]", idx, (long long)head);
+  }
   REQUIRE(smooth >= -1 && smooth <= 1, "smooth_softmax must be -1 (schema default), 0 or 1");
   REQUIRE(n.qk_output >= 0 && n.qk_output <= 2 && (n.qk_output != 0) == v.out_present(3),
           "qk_output must be 0, 1 or 2 and enabled exactly when output_qk is present");
@@ -386,7 +390,6 @@ void gqa_claim(const GView& v) {
   REQUIRE(!sliding, "sliding_window_cache is not implemented on B200");
   REQUIRE(n.qk_output == 0, "qk_output diagnostics are not implemented on B200");
   REQUIRE(!quantized && n.kv_cache_bit_width == 0, "integer GroupQueryAttention caches are not implemented on B200");
-  REQUIRE(!v.in_present(14), "q/k RMS norm inside GroupQueryAttention is not implemented on B200");
   REQUIRE(head % 8 == 0 && head <= 256, "head_size must be a multiple of 8 up to 256 on B200, got %lld", (long long)head);
 }
 

@@ -306,6 +306,7 @@ void describe_gqa(const GraphReader& g, const OrtNode* node, B200GqaNodeInfo* n)
   n->kv_cache_bit_width = g.int_or(node, "kv_cache_bit_width", 0);
   if (!g.float_attr(node, "softcap", &n->softcap)) n->softcap = 0.f;
   n->has_scale = g.float_attr(node, "scale", &n->scale) ? 1 : 0;
+  n->has_qk_norm_epsilon = g.float_attr(node, "qk_norm_epsilon", &n->qk_norm_epsilon) ? 1 : 0;
 }
 
 }  // namespace
@@ -640,9 +641,9 @@ void ComputeInfo::run_gqa(OrtKernelContext* kctx, void* stream) {
   Bound out1 = output(kctx, 1, {B, KV, pcap, D});
   Bound out2 = output(kctx, 2, {B, KV, pcap, D});
 
-  staging.plan({&in[0], &in[1], &in[2], &in[3], &in[4], &in[5], &in[7], &in[8], &in[9], &in[10], &in[11], &out0, &out1,
-                &out2});
-  for (int i : {0, 1, 2, 3, 4, 5, 7, 8, 9, 10, 11}) staging.place(&in[i], true, false, stream);
+  staging.plan({&in[0], &in[1], &in[2], &in[3], &in[4], &in[5], &in[7], &in[8], &in[9], &in[10], &in[11], &in[14],
+                &in[15], &out0, &out1, &out2});
+  for (int i : {0, 1, 2, 3, 4, 5, 7, 8, 9, 10, 11, 14, 15}) staging.place(&in[i], true, false, stream);
   staging.place(&out0, false, true, stream);
   staging.place(&out1, false, true, stream);
   staging.place(&out2, false, true, stream);
@@ -675,6 +676,8 @@ void ComputeInfo::run_gqa(OrtKernelContext* kctx, void* stream) {
   if (static_cast<int64_t>(seqlens.size()) < B)
     raise(ORT_INVALID_ARGUMENT, "GroupQueryAttention: seqlens_k must hold batch_size values");
   p.head_sink = in[11].dev;
+  p.q_norm_weight = in[14].dev;  // with k_norm_weight; epsilon from the node's attribute
+  p.k_norm_weight = in[15].dev;
   if (in[10].present) {  // attention_bias [1|B, 1|H, S, total]
     if (in[10].shape.size() != 4)
       raise(ORT_EP_FAIL, "GroupQueryAttention: attention_bias must broadcast to [batch,heads,sequence,total]");

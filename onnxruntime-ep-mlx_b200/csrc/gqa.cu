@@ -785,45 +785,82 @@ __global__ void gqa_present_kernel(const GqaArgs a, int tail_only) {
   }
 }
 
-// ------------------------------------------------------------------ rotary embedding
-// RoPE of the node's new query and key rows (do_rotary=1), written to workspace rows that the
-// attention kernels then read (attention.rs:668-681: Q and K rotated at the query rows'
-// positions before K joins present).  One CTA per (batch, query row); fp32 arithmetic, one
-// rounding to the activation type (the reference oracle's _rotate, and gqa_rope_f32).
+// ------------------------------------------------------------------ q/k norm and rotary embedding
+// The node's processed query and new key rows, written to workspace rows that the attention
+// kernels then read.  Per head, in order:
+//  * optional RMS norm (inputs 14 / 15, attention.rs:1070-1078): x / sqrt(mean(x^2) + eps) * w
+//    in fp32, rounded to the activation type (the reference's rms_norm output has that type);
+//  * optional RoPE (do_rotary=1, attention.rs:668-681): Q and K rotated at the query rows'
+//    positions before K joins present, fp32 products and sum each rounded, one rounding to the
+//    activation type (the reference oracle's _rotate, and gqa_rope_f32).
+// One CTA per (batch, query row); the rows are staged in shared memory as fp32.
 struct GqaRope {
-  int H, KV, D, S, new_seq, half, interleaved, rows, first_prompt;
+  int H, KV, D, S, new_seq, half, interleaved, rows, first_prompt, do_rotary;
+  float eps;
   int64_t q_stride, k_stride;
   const void* q;
   const void* k;
   const void* cos;
   const void* sin;
+  const void* qw;          // [D] norm weights (both or neither)
+  const void* kw;
   const int32_t* seqlens;
   const int64_t* pos_ids;  // NULL: positions query_past + s
   void* q_out;             // [B * S, H * D]
   void* k_out;             // [B * new_seq, KV * D]
 };
 
+size_t gqa_rope_smem(int H, int KV, int D) { return sizeof(float) * (size_t)(H + KV) * D; }
+
 template <typename T>
 __global__ void __launch_bounds__(256) gqa_rope_kernel(const GqaRope r) {
+  extern __shared__ float rowbuf[];  // [(H + KV) * D]
   const int row = blockIdx.x;  // b * S + s
   const int b = row / r.S, s = row % r.S;
-  int64_t pos;
-  if (r.pos_ids) pos = r.first_prompt ? r.pos_ids[0] + s : r.pos_ids[(int64_t)b * r.S + s];
-  else pos = max(r.seqlens[b] + 1 - r.S, 0) + s;
-  // the host rejected out-of-range positions before the launch; clamp so no read can stray
-  pos = pos < 0 ? 0 : (pos >= r.rows ? r.rows - 1 : pos);
-  const T* crow = static_cast<const T*>(r.cos) + pos * r.half;
-  const T* srow = static_cast<const T*>(r.sin) + pos * r.half;
-  const int rot = 2 * r.half;
   const int nheads = r.H + (s < r.new_seq ? r.KV : 0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  auto src_row = [&](int h) -> const T* {
+    return h >= r.H ? static_cast<const T*>(r.k) + ((int64_t)b * r.new_seq + s) * r.k_stride + (int64_t)(h - r.H) * r.D
+                    : static_cast<const T*>(r.q) + (int64_t)row * r.q_stride + (int64_t)h * r.D;
+  };
+  for (int h = warp; h < nheads; h += nwarps) {  // stage, and normalise, a head per warp
+    const T* src = src_row(h);
+    float* dst = rowbuf + (int64_t)h * r.D;
+    float acc = 0.f;
+    for (int d = lane; d < r.D; d += 32) {
+      const float x = to_f<T>(src[d]);
+      dst[d] = x;
+      acc = __fadd_rn(acc, __fmul_rn(x, x));
+    }
+    if (r.qw) {
+#pragma unroll
+      for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      const float denom = sqrtf(__fdiv_rn(acc, (float)r.D) + r.eps);
+      const T* w = static_cast<const T*>(h >= r.H ? r.kw : r.qw);
+      for (int d = lane; d < r.D; d += 32)
+        dst[d] = to_f<T>(from_f<T>(__fmul_rn(__fdiv_rn(dst[d], denom), to_f<T>(w[d]))));
+    }
+  }
+  __syncthreads();
+  const T* crow = nullptr;
+  const T* srow = nullptr;
+  if (r.do_rotary) {
+    int64_t pos;
+    if (r.pos_ids) pos = r.first_prompt ? r.pos_ids[0] + s : r.pos_ids[(int64_t)b * r.S + s];
+    else pos = max(r.seqlens[b] + 1 - r.S, 0) + s;
+    // the host rejected out-of-range positions before the launch; clamp so no read can stray
+    pos = pos < 0 ? 0 : (pos >= r.rows ? r.rows - 1 : pos);
+    crow = static_cast<const T*>(r.cos) + pos * r.half;
+    srow = static_cast<const T*>(r.sin) + pos * r.half;
+  }
+  const int rot = r.do_rotary ? 2 * r.half : 0;
   for (int i = threadIdx.x; i < nheads * r.D; i += blockDim.x) {
     const int h = i / r.D, d = i - h * r.D;
     const bool is_k = h >= r.H;
-    const T* src = is_k ? static_cast<const T*>(r.k) + ((int64_t)b * r.new_seq + s) * r.k_stride + (int64_t)(h - r.H) * r.D
-                        : static_cast<const T*>(r.q) + (int64_t)row * r.q_stride + (int64_t)h * r.D;
     T* dst = is_k ? static_cast<T*>(r.k_out) + ((int64_t)b * r.new_seq + s) * ((int64_t)r.KV * r.D) + (int64_t)(h - r.H) * r.D
                   : static_cast<T*>(r.q_out) + (int64_t)row * ((int64_t)r.H * r.D) + (int64_t)h * r.D;
-    const float x = to_f<T>(src[d]);
+    const float* xrow = rowbuf + (int64_t)h * r.D;
+    const float x = xrow[d];
     float y = x;
     if (d < rot) {
       int j, partner;
@@ -837,13 +874,23 @@ __global__ void __launch_bounds__(256) gqa_rope_kernel(const GqaRope r) {
         partner = d < r.half ? d + r.half : d - r.half;
         first = d < r.half;
       }
-      const float c = to_f<T>(crow[j]), sn = to_f<T>(srow[j]), xp = to_f<T>(src[partner]);
+      const float c = to_f<T>(crow[j]), sn = to_f<T>(srow[j]), xp = xrow[partner];
       // two products and one sum, each rounded (no fused multiply-add), as the reference's
       // element-wise ops round them: fp32 caches match bit for bit
       y = __fadd_rn(__fmul_rn(x, c), __fmul_rn(first ? -xp : xp, sn));
     }
     dst[d] = from_f<T>(y);
   }
+}
+
+template <typename T>
+cudaError_t launch_rope(const GqaRope& r, dim3 grid, size_t smem, cudaStream_t stream) {
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(gqa_rope_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  gqa_rope_kernel<T><<<grid, 256, smem, stream>>>(r);
+  return cudaSuccess;
 }
 
 // ------------------------------------------------------------------ host side
@@ -883,7 +930,7 @@ GqaPlan gqa_plan(const B200GqaParams* p) {
     return at;
   };
   P.status = take(sizeof(int));
-  if (p->do_rotary) {  // rotated query and key rows
+  if (p->do_rotary || p->q_norm_weight) {  // normalised / rotated query and key rows
     P.q_rot = take(act_size(p->dtype) * (size_t)p->batch * p->seq * p->num_heads * p->head_size);
     P.k_rot = take(act_size(p->dtype) * (size_t)p->batch * std::max(p->new_seq, 1) * p->kv_num_heads * p->head_size);
   }
@@ -939,6 +986,12 @@ int check_gqa(const B200GqaParams* p) {
     if (p->position_ids && !p->host_position_ids)
       return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: position_ids need their host copy (host_position_ids)");
   }
+  if ((p->q_norm_weight == nullptr) != (p->k_norm_weight == nullptr))
+    return gfail(B200_ERR_INVALID_ARGUMENT, "q_norm_weight and k_norm_weight must be provided together");
+  if ((p->do_rotary || p->q_norm_weight) &&
+      gqa_rope_smem(p->num_heads, p->kv_num_heads, p->head_size) > 227 * 1024)
+    return gfail(B200_ERR_UNSUPPORTED, "GroupQueryAttention: the query and key heads of one row exceed the prologue's "
+                                       "shared memory");
   // attention.rs:637-652
   if (p->attention_bias &&
       ((p->bias_batch != 1 && p->bias_batch != p->batch) || (p->bias_heads != 1 && p->bias_heads != p->num_heads) ||
@@ -1254,13 +1307,18 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     int launches = 0;
     cudaError_t e;
-    if (p->do_rotary) {  // rotate the new rows first; the attention kernels read the rotated copies
+    if (p->do_rotary || p->q_norm_weight) {  // normalise / rotate the new rows first; the attention
+                                             // kernels read the processed copies
       GqaRope r{};
       r.H = a.H;
       r.KV = a.KV;
       r.D = a.D;
       r.S = a.S;
       r.new_seq = a.new_seq;
+      r.do_rotary = p->do_rotary != 0;
+      r.qw = p->q_norm_weight;
+      r.kw = p->k_norm_weight;
+      r.eps = p->qk_norm_epsilon > 0.f ? p->qk_norm_epsilon : 1e-6f;
       r.half = p->rotary_dim / 2;
       r.interleaved = p->rotary_interleaved != 0;
       r.rows = p->rotary_positions;
@@ -1276,10 +1334,11 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
       r.q_out = ws + P.q_rot;
       r.k_out = ws + P.k_rot;
       const dim3 grid((unsigned)(a.B * a.S));
-      if (a.dtype == B200_DTYPE_FLOAT) gqa_rope_kernel<float><<<grid, 256, 0, stream>>>(r);
-      else if (a.dtype == B200_DTYPE_FLOAT16) gqa_rope_kernel<__half><<<grid, 256, 0, stream>>>(r);
-      else gqa_rope_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(r);
-      e = cudaGetLastError();
+      const size_t smem = gqa_rope_smem(a.H, a.KV, a.D);
+      if (a.dtype == B200_DTYPE_FLOAT) e = launch_rope<float>(r, grid, smem, stream);
+      else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_rope<__half>(r, grid, smem, stream);
+      else e = launch_rope<__nv_bfloat16>(r, grid, smem, stream);
+      if (e == cudaSuccess) e = cudaGetLastError();
       if (e != cudaSuccess) return gfail(B200_ERR_CUDA, std::string("GroupQueryAttention: CUDA error: ") + cudaGetErrorString(e));
       add_launches(1);
       a.q = r.q_out;

@@ -99,7 +99,7 @@ class GqaParams(ctypes.Structure):
         ("cos_cache", _vp), ("sin_cache", _vp), ("position_ids", _vp), ("host_position_ids", _vp),
         ("position_ids_width", _i32),
         ("attention_bias", _vp), ("bias_batch", _i32), ("bias_heads", _i32), ("bias_seq", _i32),
-        ("bias_total", _i32),
+        ("bias_total", _i32), ("q_norm_weight", _vp), ("k_norm_weight", _vp), ("qk_norm_epsilon", _f32),
     ]
 
 
@@ -113,7 +113,8 @@ class GqaNodeInfo(ctypes.Structure):
         ("do_rotary", _i64), ("rotary_interleaved", _i64), ("sliding_window_cache", _i64),
         ("smooth_softmax", _i64), ("qk_output", _i64), ("kv_cache_bit_width", _i64),
         ("has_causal", _i32), ("has_local_window_size", _i32), ("has_smooth_softmax", _i32),
-        ("softcap", _f32), ("has_scale", _i32), ("scale", _f32),
+        ("softcap", _f32), ("has_scale", _i32), ("scale", _f32), ("has_qk_norm_epsilon", _i32),
+        ("qk_norm_epsilon", _f32),
     ]
 
 

@@ -43,13 +43,15 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
                  local_window_size=-1, softcap=0.0, smooth_softmax=-1, present_key=None,
                  present_value=None, with_present=True, host_seqlens_k=None, output=None,
                  do_rotary=0, rotary_interleaved=0, cos_cache=None, sin_cache=None, position_ids=None,
-                 attention_bias=None):
+                 attention_bias=None, q_norm_weight=None, k_norm_weight=None, qk_norm_epsilon=1e-6):
     """Fill a ``B200GqaParams``.  Returns ``(params, keepalive, output, present_key, present_value)``.
 
     ``do_rotary=1`` takes ``cos_cache``/``sin_cache`` ``[positions, rotary_dim/2]`` (inputs 7 and
     8) and optionally ``position_ids`` int64 ``[batch, >=seq]`` (input 9; a host copy is made for
     the reference's bounds checks).  ``attention_bias`` ``[1|batch, 1|heads, seq, total]`` (input
-    10, the activation dtype) is added to the scores of the visible keys."""
+    10, the activation dtype) is added to the scores of the visible keys.  ``q_norm_weight`` /
+    ``k_norm_weight`` ``[head_size]`` (inputs 14 / 15) RMS-normalise every query head and new key
+    head before the rotary embedding."""
     H, KV = int(num_heads), int(kv_num_heads)
     packed = key is None and value is None  # packed QKV in query (inputs 1 and 2 absent)
     B, S = int(query.shape[0]), int(query.shape[1])
@@ -127,13 +129,16 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
                                   "GroupQueryAttention: attention_bias must broadcast to [batch,heads,sequence,total]")
         p.attention_bias = _ptr(attention_bias)
         p.bias_batch, p.bias_heads, p.bias_seq, p.bias_total = (int(x) for x in attention_bias.shape)
+    if q_norm_weight is not None:
+        p.q_norm_weight, p.k_norm_weight = _ptr(q_norm_weight), _ptr(k_norm_weight)
+        p.qk_norm_epsilon = float(qk_norm_epsilon)
     nbytes = ctypes.c_size_t(0)
     check(LIB.b200_group_query_attention_workspace_size(ctypes.byref(p), ctypes.byref(nbytes)))
     ws = _workspace(dev, nbytes.value)
     p.workspace = _ptr(ws)
     p.workspace_bytes = ws.numel()
     keep = (query, key, value, past_key, past_value, seqlens_k, head_sink, host_seqlens_k, ws, cos_cache, sin_cache,
-            position_ids, host_ids, attention_bias)
+            position_ids, host_ids, attention_bias, q_norm_weight, k_norm_weight)
     return p, keep, output, present_key, present_value
 
 

@@ -48,6 +48,14 @@ def rotate(x, cos, sin, positions, interleaved):
     return out
 
 
+def rms_norm(x, weight, eps):
+    """Per-head RMS norm of ``x [heads, seq, D]`` over D in fp32, ``x / sqrt(mean(x^2) + eps) * w``,
+    rounded back to ``x.dtype`` (attention.rs:1070-1078; tests/ops/test_gqa11.py:52-130)."""
+    xf = x.astype(np.float32)
+    denom = np.sqrt(np.mean(xf * xf, axis=-1, keepdims=True) + np.float32(eps))
+    return (xf / denom * np.asarray(weight, np.float32)).astype(x.dtype)
+
+
 def rotary_positions(b, seq, query_past, total, position_ids):
     """Positions of batch row ``b``'s query rows (attention.rs:538-585): ``query_past + s``
     without ids; with ids, the first id as an offset on a first prompt (``total == seq``),
@@ -63,14 +71,15 @@ def rotary_positions(b, seq, query_past, total, position_ids):
 def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_heads, kv_num_heads,
                           scale=None, causal=True, window=-1, softcap=0.0, sink=None,
                           smooth_softmax=-1, cos=None, sin=None, position_ids=None, interleaved=False,
-                          out_dtype=None, bias=None):
+                          out_dtype=None, bias=None, q_norm=None, k_norm=None, norm_eps=1e-6):
     """Returns ``(output [B,S,H*D], present_k, present_v [B,KV,max(cap,total),D])``.
 
     ``q`` [B,S,H*D]; ``k``/``v`` [B,new_seq,KV*D] (new_seq may be 0); ``past_k``/``past_v``
     [B,KV,cap,D] or None; ``cos``/``sin`` [positions, rotary_dim/2] turn on the rotary
     embedding of the new query and key rows (``position_ids`` [B, >=S] optional).  ``bias``
     [1|B, 1|H, S, total] is added to the (soft-capped) scores of the visible keys
-    (test_gqa_position_cache.py:119-121, attention.rs:746-755).  Arrays keep
+    (test_gqa_position_cache.py:119-121, attention.rs:746-755).  ``q_norm`` / ``k_norm``
+    ``[D]`` RMS-normalise the query heads and new key heads before the rotary embedding.  Arrays keep
     their dtype; math is fp32, the output is rounded to the activation dtype (or kept in
     ``out_dtype``, e.g. fp32 for tolerance checks)."""
     B, S, hidden = q.shape
@@ -101,6 +110,10 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
                 pv[b, :, length:cap] = past_v[b, :, length:cap]
         kb = None if not new_seq else k[b].reshape(new_seq, KV, D).transpose(1, 0, 2)  # [KV, new_seq, D]
         qb = q[b].reshape(S, H, D).transpose(1, 0, 2)                                      # [H, S, D]
+        if q_norm is not None:
+            qb = rms_norm(qb, q_norm, norm_eps)
+            if new_seq:
+                kb = rms_norm(kb, k_norm, norm_eps)
         if cos is not None:
             ids = rotary_positions(b, S, query_past, total, position_ids)
             qb = rotate(qb, cos, sin, ids, interleaved)

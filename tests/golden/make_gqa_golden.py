@@ -6,7 +6,8 @@ Usage (build container only; the reference checkout does not travel to GPU boxes
 
 ``_reference`` (tests/ops/test_gqa_position_cache.py:88-134, pinned there to ORT v1.31.0) and
 its ``_rotate`` (:71-85) are taken from the test file with ``ast`` and executed in a private
-namespace holding ``numpy``;
+namespace holding ``numpy`` (the ``qknorm`` entry restates the inline expectation of
+tests/ops/test_gqa11.py:52-130, whose test has no separate oracle function);
 the test module itself imports onnx helpers that are absent here.  Its geometry is fixed at
 4 q heads, 2 kv heads, head size 32, scale 1/sqrt(32); composed cases use softcap 0.7 and the
 feed ``sink``.  Inputs are seeded numpy (``default_rng(365 + case index)``) and stored with
@@ -150,9 +151,44 @@ def main():
         meta.append(dict(name=name, dtype=dtype, batch=batch, seq=seq, new_seq=new_seq, cap=cap,
                          total=total, causal=causal, window=window, composed=composed,
                          interleaved=bool(interleaved)))
+    # q/k RMS norm inputs 14 / 15 (tests/ops/test_gqa11.py:52-130): the test's seeded inputs and
+    # its own expectation, restated (fp32, head 8, past 2, three new rows, eps 1e-5).
+    b, sq, past, nh, kvh, head = 1, 3, 2, 4, 2, 8
+    total = past + sq
+    rng = np.random.default_rng(129)
+    q = rng.standard_normal((b, sq, nh * head)).astype(np.float32)
+    k = rng.standard_normal((b, sq, kvh * head)).astype(np.float32)
+    v = rng.standard_normal((b, sq, kvh * head)).astype(np.float32)
+    pk = rng.standard_normal((b, kvh, past, head)).astype(np.float32)
+    pv = rng.standard_normal((b, kvh, past, head)).astype(np.float32)
+    qw = np.linspace(0.75, 1.25, head).astype(np.float32)
+    kw = np.linspace(1.25, 0.75, head).astype(np.float32)
+    eps = 1e-5
+    qh = q.reshape(b, sq, nh, head).transpose(0, 2, 1, 3)
+    kh = k.reshape(b, sq, kvh, head).transpose(0, 2, 1, 3)
+    vh = v.reshape(b, sq, kvh, head).transpose(0, 2, 1, 3)
+    qh = qh / np.sqrt(np.mean(qh * qh, axis=-1, keepdims=True) + eps) * qw
+    kh = kh / np.sqrt(np.mean(kh * kh, axis=-1, keepdims=True) + eps) * kw
+    present_k = np.concatenate([pk, kh], axis=2)
+    present_v = np.concatenate([pv, vh], axis=2)
+    keys = np.repeat(present_k, nh // kvh, axis=1)
+    vals = np.repeat(present_v, nh // kvh, axis=1)
+    scores = np.matmul(qh, keys.transpose(0, 1, 3, 2)) / np.sqrt(head)
+    causal = np.arange(total)[None, :] <= (past + np.arange(sq))[:, None]
+    scores = np.where(causal[None, None], scores, -np.inf)
+    probs = np.exp(scores - scores.max(axis=-1, keepdims=True))
+    probs /= probs.sum(axis=-1, keepdims=True)
+    expected = np.matmul(probs, vals).transpose(0, 2, 1, 3).reshape(b, sq, nh * head)
+    for key, val in dict(q=q, k=k, v=v, pk=pk, pv=pv, qw=qw, kw=kw, eps=np.array([eps], np.float32),
+                         lengths=np.array([total - 1], np.int32), total=np.array([total], np.int32)).items():
+        arrays[f"qknorm/in/{key}"] = val
+    arrays["qknorm/out/output"] = expected.astype(np.float32)
+    arrays["qknorm/out/present_k"] = present_k.astype(np.float32)
+    arrays["qknorm/out/present_v"] = present_v.astype(np.float32)
+
     arrays["meta"] = np.frombuffer(json.dumps(meta).encode(), np.uint8)
     np.savez_compressed(os.path.join(HERE, "gqa_golden.npz"), **arrays)
-    print(f"wrote {len(meta)} cases to gqa_golden.npz")
+    print(f"wrote {len(meta)} cases (+ qknorm) to gqa_golden.npz")
 
 
 if __name__ == "__main__":

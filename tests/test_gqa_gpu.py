@@ -82,7 +82,7 @@ def test_golden_cases(case, in_place):
 
 def run_case(rng, *, dtype="bfloat16", B=1, S=1, H=32, KV=8, D=128, cap=2048, lengths=None, total=None,
              causal=1, window=-1, softcap=0.0, sink=False, smooth=-1, packed=False, new_rows=True, past=True,
-             in_place=False, rotary=None, bias=None):
+             in_place=False, rotary=None, bias=None, qk_norm=False):
     npdt = np.float32
     lengths = [cap + S] * B if lengths is None else lengths
     B = len(lengths)
@@ -124,14 +124,25 @@ def run_case(rng, *, dtype="bfloat16", B=1, S=1, H=32, KV=8, D=128, cap=2048, le
         if dtype != "float32":
             import ml_dtypes
             bias_n = bias_n.astype(np.float16 if dtype == "float16" else ml_dtypes.bfloat16)
+    norm_t, norm_n = {}, {}
+    if qk_norm:  # q / k RMS norm weights [D] in the activation type, epsilon 1e-5
+        qw_t, kw_t = to(rng.uniform(0.5, 1.5, D).astype(npdt)), to(rng.uniform(0.5, 1.5, D).astype(npdt))
+        qw_n, kw_n = back(qw_t), back(kw_t)
+        if dtype != "float32":
+            import ml_dtypes
+            ndt = np.float16 if dtype == "float16" else ml_dtypes.bfloat16
+            qn, kn, vn, pkr, pvr, skr = (None if a is None else a.astype(ndt) for a in (qn, kn, vn, pkr, pvr, skr))
+            qw_n, kw_n = qw_n.astype(ndt), kw_n.astype(ndt)
+        norm_t = dict(q_norm_weight=qw_t, k_norm_weight=kw_t, qk_norm_epsilon=1e-5)
+        norm_n = dict(q_norm=qw_n, k_norm=kw_n, norm_eps=1e-5)
     want, wk, wv = gqa_ref.group_query_attention(
         qn, kn if new_rows else None, vn if new_rows else None, pkr, pvr, np.asarray(lengths) - 1, total,
         num_heads=H, kv_num_heads=KV, causal=bool(causal), window=window, softcap=softcap, sink=skr,
-        smooth_softmax=smooth, out_dtype=np.float32, bias=bias_n, **rot)
+        smooth_softmax=smooth, out_dtype=np.float32, bias=bias_n, **rot, **norm_n)
     want, wk, wv = (np.asarray(x, np.float32) for x in (want, wk, wv))
     lens = torch.tensor(np.asarray(lengths) - 1, dtype=torch.int32, device=DEV)
     kw = dict(num_heads=H, kv_num_heads=KV, causal=causal, local_window_size=window, softcap=softcap,
-              smooth_softmax=smooth, attention_bias=bias_t, **kw_rot)
+              smooth_softmax=smooth, attention_bias=bias_t, **kw_rot, **norm_t)
     if in_place:
         kw.update(present_key=pkt, present_value=pvt)
     if packed:
@@ -143,7 +154,11 @@ def run_case(rng, *, dtype="bfloat16", B=1, S=1, H=32, KV=8, D=128, cap=2048, le
     check(back(out), want, dtype)
     if ok is not None:
         n = min(ok.shape[2], wk.shape[2])
-        np.testing.assert_array_equal(back(ok)[:, :, :n], wk[:, :, :n])
+        if qk_norm:  # normalised key rows: the row sum's order may move the rounding by one ulp
+            ulp = {"float32": 2.0 ** -23, "float16": 2.0 ** -10, "bfloat16": 2.0 ** -7}[dtype]
+            np.testing.assert_allclose(back(ok)[:, :, :n], wk[:, :, :n], rtol=ulp, atol=1e-6)
+        else:
+            np.testing.assert_array_equal(back(ok)[:, :, :n], wk[:, :, :n])
         np.testing.assert_array_equal(back(ov)[:, :, :n], wv[:, :, :n])
 
 
@@ -243,3 +258,27 @@ def test_bias_prefill_rows_and_broadcast(shape):
 def test_bias_with_softcap_sink_and_rotary():
     run_case(np.random.default_rng(33), dtype="bfloat16", S=3, cap=128, lengths=[131, 90], H=16, KV=4,
              softcap=30.0, sink=True, rotary=(64, False, None), bias=(2, 16))
+
+
+# ---- q / k RMS norm (inputs 14 / 15) --------------------------------------------------------
+def test_qk_norm_reference_case():
+    """tests/ops/test_gqa11.py:52-130: fp32, 4q/2kv, head 8, past 2, three new rows, eps 1e-5."""
+    f = {k.split("/")[-1]: GOLDEN[k] for k in GOLDEN.files if k.startswith("qknorm/in/")}
+    out, ok, ov = gqa.group_query_attention(
+        dev(f["q"]), dev(f["k"]), dev(f["v"]), dev(f["pk"]), dev(f["pv"]), dev(f["lengths"]), int(f["total"][0]),
+        num_heads=4, kv_num_heads=2, q_norm_weight=dev(f["qw"]), k_norm_weight=dev(f["kw"]),
+        qk_norm_epsilon=float(f["eps"][0]), check_status=True)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(host(out), GOLDEN["qknorm/out/output"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(host(ok), GOLDEN["qknorm/out/present_k"], rtol=1e-6, atol=1e-6)
+    np.testing.assert_array_equal(host(ov), GOLDEN["qknorm/out/present_v"])
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_config1_with_qk_norm_and_rotary(dtype):
+    run_case(np.random.default_rng(41), dtype=dtype, cap=2048, lengths=[2049], qk_norm=True,
+             rotary=(64, False, None))
+
+
+def test_qk_norm_prefill_rows():
+    run_case(np.random.default_rng(42), dtype="float16", S=17, cap=64, lengths=[81, 30], H=8, KV=2, qk_norm=True)

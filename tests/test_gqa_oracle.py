@@ -56,3 +56,14 @@ def test_growing_cache_appends_after_capacity():
     p = np.exp(s - s.max(1, keepdims=True))
     p /= p.sum(1, keepdims=True)
     np.testing.assert_allclose(out[0, 0].reshape(4, 32), np.einsum("hk,hkd->hd", p, vals), rtol=1e-5, atol=1e-6)
+
+
+def test_oracle_qk_norm_matches_reference_case():
+    """q/k RMS norm inputs 14 / 15 (tests/ops/test_gqa11.py:52-130, fp32, eps 1e-5)."""
+    f = {k.split("/")[-1]: DATA[k] for k in DATA.files if k.startswith("qknorm/in/")}
+    out, pk, pv = gqa_ref.group_query_attention(
+        f["q"], f["k"], f["v"], f["pk"], f["pv"], f["lengths"], f["total"], num_heads=4, kv_num_heads=2,
+        q_norm=f["qw"], k_norm=f["kw"], norm_eps=float(f["eps"][0]))
+    np.testing.assert_allclose(out, DATA["qknorm/out/output"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(pk, DATA["qknorm/out/present_k"], rtol=1e-6, atol=1e-6)
+    np.testing.assert_array_equal(pv, DATA["qknorm/out/present_v"])
