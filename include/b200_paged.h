@@ -307,6 +307,12 @@ typedef struct B200GqaParams {
   const void* q_norm_weight;
   const void* k_norm_weight;
   float qk_norm_epsilon;      /* 0 -> 1e-6                                               */
+  /* qk_output diagnostics (attribute qk_output, output 3, attention.rs:771-787): 1 = the
+   * logits (scale * q.k, soft-capped, plus attention_bias) of the visible keys and 0
+   * elsewhere, 2 = the softmax probabilities (sink included); [batch, num_heads, seq,
+   * total_sequence_length] in dtype, columns from each row's length on are 0. */
+  int32_t qk_output;
+  void* output_qk;
 } B200GqaParams;
 
 B200_API int b200_gqa_params_size(void);
@@ -322,8 +328,8 @@ B200_API int b200_group_query_attention(const B200GqaParams* p, void* stream);
 B200_API int b200_group_query_attention_read_status(const B200GqaParams* p, void* stream);
 
 /* Claim predicate, restating group_query_attention_claim (attention.rs:2407-2754) over a
- * plain node description, plus this build's own declines (qk_output, sliding_window_cache,
- * integer caches, head size).  Returns 1 (claim) or 0
+ * plain node description, plus this build's own declines (sliding_window_cache, integer
+ * caches, head size).  Returns 1 (claim) or 0
  * (decline, reason written to `reason`). */
 typedef struct B200GqaNodeInfo {
   int32_t num_inputs;

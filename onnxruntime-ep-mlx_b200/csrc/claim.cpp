@@ -388,7 +388,6 @@ void gqa_claim(const GView& v) {
   REQUIRE(std::isfinite(n.softcap) && n.softcap >= 0.f, "softcap must be finite and non-negative");
   // Forms the reference accepts that this build does not implement (the node stays on ORT).
   REQUIRE(!sliding, "sliding_window_cache is not implemented on B200");
-  REQUIRE(n.qk_output == 0, "qk_output diagnostics are not implemented on B200");
   REQUIRE(!quantized && n.kv_cache_bit_width == 0, "integer GroupQueryAttention caches are not implemented on B200");
   REQUIRE(head % 8 == 0 && head <= 256, "head_size must be a multiple of 8 up to 256 on B200, got %lld", (long long)head);
 }

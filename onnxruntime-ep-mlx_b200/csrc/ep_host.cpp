@@ -593,6 +593,7 @@ int b200_ep_node_compute_gqa(B200EpNode* n, const B200GqaParams* t, void* stream
     p.do_rotary = a.do_rotary != 0;  // the tensors carry cos / sin / position_ids and their sizes
     p.rotary_interleaved = a.rotary_interleaved != 0;
     p.qk_norm_epsilon = a.has_qk_norm_epsilon ? a.qk_norm_epsilon : 1e-6f;  // the tensors carry the weights
+    p.qk_output = (int32_t)a.qk_output;  // the tensors carry output_qk
     size_t need = 0;
     int rc = b200_group_query_attention_workspace_size(&p, &need);
     if (rc) return rc;

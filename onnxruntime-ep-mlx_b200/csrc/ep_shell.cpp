@@ -640,13 +640,15 @@ void ComputeInfo::run_gqa(OrtKernelContext* kctx, void* stream) {
   Bound out0 = output(kctx, 0, {B, S, H * D});
   Bound out1 = output(kctx, 1, {B, KV, pcap, D});
   Bound out2 = output(kctx, 2, {B, KV, pcap, D});
+  Bound out3 = output(kctx, 3, {B, H, S, total[0]});  // qk_output diagnostics
 
   staging.plan({&in[0], &in[1], &in[2], &in[3], &in[4], &in[5], &in[7], &in[8], &in[9], &in[10], &in[11], &in[14],
-                &in[15], &out0, &out1, &out2});
+                &in[15], &out0, &out1, &out2, &out3});
   for (int i : {0, 1, 2, 3, 4, 5, 7, 8, 9, 10, 11, 14, 15}) staging.place(&in[i], true, false, stream);
   staging.place(&out0, false, true, stream);
   staging.place(&out1, false, true, stream);
   staging.place(&out2, false, true, stream);
+  staging.place(&out3, false, true, stream);
 
   B200GqaParams p{};
   p.head_size = static_cast<int32_t>(D);
@@ -676,6 +678,7 @@ void ComputeInfo::run_gqa(OrtKernelContext* kctx, void* stream) {
   if (static_cast<int64_t>(seqlens.size()) < B)
     raise(ORT_INVALID_ARGUMENT, "GroupQueryAttention: seqlens_k must hold batch_size values");
   p.head_sink = in[11].dev;
+  p.output_qk = out3.dev;        // with the node's qk_output mode
   p.q_norm_weight = in[14].dev;  // with k_norm_weight; epsilon from the node's attribute
   p.k_norm_weight = in[15].dev;
   if (in[10].present) {  // attention_bias [1|B, 1|H, S, total]

@@ -58,6 +58,8 @@ struct GqaArgs {
   const void* sink;
   const void* bias;                       // attention_bias [Bb, Hb, S, total] or null
   int64_t bias_bstride, bias_hstride;     // 0 for a broadcast (size-1) dimension
+  void* qk_out;                           // qk_output diagnostics [B, H, S, total] or null
+  int qk_mode;                            // 1 logits, 2 probabilities
   void* out;
   int row_tiles, splits, fused_copy, present_separate;
   float* part_o;   // [groups][splits][R][D]
@@ -883,6 +885,74 @@ __global__ void __launch_bounds__(256) gqa_rope_kernel(const GqaRope r) {
   }
 }
 
+// ------------------------------------------------------------------ qk_output diagnostics
+// attention.rs:756-787: for every (batch, head, query row) the logits of keys [0, length)
+// (scale * q.k, soft-capped, plus attention_bias) where visible and 0 elsewhere (mode 1), or
+// the softmax probabilities with the sink in the denominator (mode 2); columns [length, total)
+// are 0.  A diagnostic path: one CTA per row recomputes the scores (twice for mode 2) from the
+// query / key rows the attention kernels read.
+template <typename T>
+__global__ void __launch_bounds__(128) gqa_qk_kernel(const GqaArgs a) {
+  extern __shared__ float qrow[];  // [D]
+  __shared__ float red[2][4];
+  const int row = blockIdx.x;  // (b * H + h) * S + s
+  const int s = row % a.S, h = (row / a.S) % a.H, b = row / (a.S * a.H);
+  const int kh = h / a.g, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const BatchGeom bg = batch_geom(a, b);
+  const int pos = bg.query_past + s;
+  const int end = a.causal ? min(pos + 1, bg.length) : bg.length;
+  const int start = a.window > 0 ? max(0, end - a.window) : 0;
+  for (int d = tid; d < a.D; d += blockDim.x)
+    qrow[d] = to_f(static_cast<const T*>(a.q)[((int64_t)b * a.S + s) * a.q_stride + (int64_t)h * a.D + d]);
+  __syncthreads();
+  const T* bias = a.bias ? static_cast<const T*>(a.bias) + b * a.bias_bstride + (int64_t)h * a.bias_hstride +
+                               (int64_t)s * a.total
+                         : nullptr;
+  auto logit = [&](int j) {
+    const T* krow = key_row<T>(a, bg, b, kh, j, false);
+    float acc = 0.f;
+    for (int d = 0; d < a.D; ++d) acc = fmaf(qrow[d], to_f(krow[d]), acc);
+    float x = acc * a.scale;
+    if (a.softcap > 0.f) x = a.softcap * tanhf(x / a.softcap);
+    if (bias) x += to_f(bias[j]);
+    return x;
+  };
+  T* out = static_cast<T*>(a.qk_out) + (int64_t)row * a.total;
+  float M = -INFINITY, L = 0.f;
+  if (a.qk_mode == 2) {  // max and sum over the visible keys (and the sink)
+    float m = -INFINITY;
+    for (int j = start + tid; j < end; j += blockDim.x) m = fmaxf(m, logit(j));
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[0][warp] = m;
+    __syncthreads();
+    M = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
+    float sink = -INFINITY;
+    if (a.sink) sink = to_f(static_cast<const T*>(a.sink)[h]);
+    else if (a.smooth) sink = 0.f;
+    M = fmaxf(M, sink);
+    float l = 0.f;
+    for (int j = start + tid; j < end; j += blockDim.x) l += expf(logit(j) - M);
+    for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) red[1][warp] = l;
+    __syncthreads();
+    L = red[1][0] + red[1][1] + red[1][2] + red[1][3] + (sink == -INFINITY ? 0.f : expf(sink - M));
+  }
+  for (int j = tid; j < a.total; j += blockDim.x) {
+    float y = 0.f;
+    if (j >= start && j < end) {
+      const float x = logit(j);
+      y = a.qk_mode == 1 ? x : (L > 0.f ? expf(x - M) / L : 0.f);
+    }
+    out[j] = from_f<T>(y);
+  }
+}
+
+template <typename T>
+cudaError_t launch_qk(const GqaArgs& a, cudaStream_t stream) {
+  gqa_qk_kernel<T><<<(unsigned)(a.B * a.H * a.S), 128, sizeof(float) * a.D, stream>>>(a);
+  return cudaGetLastError();
+}
+
 template <typename T>
 cudaError_t launch_rope(const GqaRope& r, dim3 grid, size_t smem, cudaStream_t stream) {
   if (smem > 48 * 1024) {
@@ -986,6 +1056,9 @@ int check_gqa(const B200GqaParams* p) {
     if (p->position_ids && !p->host_position_ids)
       return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: position_ids need their host copy (host_position_ids)");
   }
+  if (p->qk_output < 0 || p->qk_output > 2 || (p->qk_output != 0) != (p->output_qk != nullptr))
+    return gfail(B200_ERR_INVALID_ARGUMENT,
+                 "qk_output must be 0, 1 or 2 and enabled exactly when output_qk is present");
   if ((p->q_norm_weight == nullptr) != (p->k_norm_weight == nullptr))
     return gfail(B200_ERR_INVALID_ARGUMENT, "q_norm_weight and k_norm_weight must be provided together");
   if ((p->do_rotary || p->q_norm_weight) &&
@@ -1356,6 +1429,14 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
     else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_gqa<__half>(a, P, cluster, tail_rows, stream, &launches);
     else e = launch_gqa<__nv_bfloat16>(a, P, cluster, tail_rows, stream, &launches);
     add_launches(launches);
+    if (e == cudaSuccess && p->qk_output) {  // diagnostics after the attention of the call
+      a.qk_out = p->output_qk;
+      a.qk_mode = p->qk_output;
+      if (a.dtype == B200_DTYPE_FLOAT) e = launch_qk<float>(a, stream);
+      else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_qk<__half>(a, stream);
+      else e = launch_qk<__nv_bfloat16>(a, stream);
+      add_launches(1);
+    }
     if (e != cudaSuccess)
       return gfail(B200_ERR_CUDA, std::string("GroupQueryAttention: CUDA error: ") + cudaGetErrorString(e));
     return B200_OK;

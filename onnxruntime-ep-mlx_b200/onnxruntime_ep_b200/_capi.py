@@ -100,6 +100,7 @@ class GqaParams(ctypes.Structure):
         ("position_ids_width", _i32),
         ("attention_bias", _vp), ("bias_batch", _i32), ("bias_heads", _i32), ("bias_seq", _i32),
         ("bias_total", _i32), ("q_norm_weight", _vp), ("k_norm_weight", _vp), ("qk_norm_epsilon", _f32),
+        ("qk_output", _i32), ("output_qk", _vp),
     ]
 
 

@@ -43,7 +43,8 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
                  local_window_size=-1, softcap=0.0, smooth_softmax=-1, present_key=None,
                  present_value=None, with_present=True, host_seqlens_k=None, output=None,
                  do_rotary=0, rotary_interleaved=0, cos_cache=None, sin_cache=None, position_ids=None,
-                 attention_bias=None, q_norm_weight=None, k_norm_weight=None, qk_norm_epsilon=1e-6):
+                 attention_bias=None, q_norm_weight=None, k_norm_weight=None, qk_norm_epsilon=1e-6,
+                 qk_output=0, output_qk=None):
     """Fill a ``B200GqaParams``.  Returns ``(params, keepalive, output, present_key, present_value)``.
 
     ``do_rotary=1`` takes ``cos_cache``/``sin_cache`` ``[positions, rotary_dim/2]`` (inputs 7 and
@@ -51,7 +52,8 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
     the reference's bounds checks).  ``attention_bias`` ``[1|batch, 1|heads, seq, total]`` (input
     10, the activation dtype) is added to the scores of the visible keys.  ``q_norm_weight`` /
     ``k_norm_weight`` ``[head_size]`` (inputs 14 / 15) RMS-normalise every query head and new key
-    head before the rotary embedding."""
+    head before the rotary embedding.  ``qk_output`` 1 / 2 fills ``output_qk`` ``[batch, heads,
+    seq, total]`` (allocated when not given) with the visible logits / the probabilities."""
     H, KV = int(num_heads), int(kv_num_heads)
     packed = key is None and value is None  # packed QKV in query (inputs 1 and 2 absent)
     B, S = int(query.shape[0]), int(query.shape[1])
@@ -132,27 +134,33 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
     if q_norm_weight is not None:
         p.q_norm_weight, p.k_norm_weight = _ptr(q_norm_weight), _ptr(k_norm_weight)
         p.qk_norm_epsilon = float(qk_norm_epsilon)
+    if qk_output:
+        if output_qk is None:
+            output_qk = torch.empty((B, H, S, total), dtype=query.dtype, device=dev)
+        p.qk_output, p.output_qk = int(qk_output), _ptr(output_qk)
     nbytes = ctypes.c_size_t(0)
     check(LIB.b200_group_query_attention_workspace_size(ctypes.byref(p), ctypes.byref(nbytes)))
     ws = _workspace(dev, nbytes.value)
     p.workspace = _ptr(ws)
     p.workspace_bytes = ws.numel()
     keep = (query, key, value, past_key, past_value, seqlens_k, head_sink, host_seqlens_k, ws, cos_cache, sin_cache,
-            position_ids, host_ids, attention_bias, q_norm_weight, k_norm_weight)
+            position_ids, host_ids, attention_bias, q_norm_weight, k_norm_weight, output_qk)
     return p, keep, output, present_key, present_value
 
 
 def group_query_attention(query, key, value, past_key, past_value, seqlens_k, total_sequence_length,
                           head_sink=None, *, stream=None, check_status=False, **kwargs):
-    """One GroupQueryAttention node.  Returns ``(output, present_key, present_value)``.
+    """One GroupQueryAttention node.  Returns ``(output, present_key, present_value)``, plus
+    ``output_qk`` when ``qk_output`` is 1 or 2.
 
     ``check_status=True`` synchronises and raises ``B200Error`` when a bounded device wait of
     the call ran out."""
     p, keep, out, pk, pv = build_params(query, key, value, past_key, past_value, seqlens_k,
                                         total_sequence_length, head_sink, **kwargs)
+    qk = keep[-1]
     s = stream if stream is not None else torch.cuda.current_stream(query.device)
     check(LIB.b200_group_query_attention(ctypes.byref(p), ctypes.c_void_p(s.cuda_stream)))
     if check_status:
         check(LIB.b200_group_query_attention_read_status(ctypes.byref(p), ctypes.c_void_p(s.cuda_stream)))
     del keep
-    return out, pk, pv
+    return (out, pk, pv) if qk is None else (out, pk, pv, qk)

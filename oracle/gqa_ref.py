@@ -71,7 +71,7 @@ def rotary_positions(b, seq, query_past, total, position_ids):
 def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_heads, kv_num_heads,
                           scale=None, causal=True, window=-1, softcap=0.0, sink=None,
                           smooth_softmax=-1, cos=None, sin=None, position_ids=None, interleaved=False,
-                          out_dtype=None, bias=None, q_norm=None, k_norm=None, norm_eps=1e-6):
+                          out_dtype=None, bias=None, q_norm=None, k_norm=None, norm_eps=1e-6, qk_output=0):
     """Returns ``(output [B,S,H*D], present_k, present_v [B,KV,max(cap,total),D])``.
 
     ``q`` [B,S,H*D]; ``k``/``v`` [B,new_seq,KV*D] (new_seq may be 0); ``past_k``/``past_v``
@@ -79,7 +79,10 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
     embedding of the new query and key rows (``position_ids`` [B, >=S] optional).  ``bias``
     [1|B, 1|H, S, total] is added to the (soft-capped) scores of the visible keys
     (test_gqa_position_cache.py:119-121, attention.rs:746-755).  ``q_norm`` / ``k_norm``
-    ``[D]`` RMS-normalise the query heads and new key heads before the rotary embedding.  Arrays keep
+    ``[D]`` RMS-normalise the query heads and new key heads before the rotary embedding.
+    ``qk_output`` 1 / 2 also returns the diagnostics ``[B, H, S, total]``: the visible logits
+    (0 elsewhere) / the probabilities, zero from each row's length on (test_gqa_position_cache.py:
+    130-131, attention.rs:771-787).  Arrays keep
     their dtype; math is fp32, the output is rounded to the activation dtype (or kept in
     ``out_dtype``, e.g. fp32 for tolerance checks)."""
     B, S, hidden = q.shape
@@ -95,6 +98,7 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
     pk = np.zeros((B, KV, pcap, D), dt)
     pv = np.zeros((B, KV, pcap, D), dt)
     out = np.empty((B, S, H * D), out_dtype or dt)
+    diag = np.zeros((B, H, S, total), out_dtype or dt)
     if sink is None and smooth_softmax == 1:
         sink = np.zeros(H, np.float32)
     for b in range(B):
@@ -140,5 +144,7 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
             logits = np.concatenate([logits, np.broadcast_to(s, (H, S, 1))], -1)
         e = np.exp(logits - logits.max(-1, keepdims=True))
         probs = (e / e.sum(-1, keepdims=True))[..., :length]
+        if qk_output:
+            diag[b, :, :, :length] = np.where(visible[None], scores, 0) if qk_output == 1 else probs
         out[b] = (probs @ vals).transpose(1, 0, 2).reshape(S, H * D).astype(out.dtype)
-    return out, pk, pv
+    return (out, pk, pv, diag) if qk_output else (out, pk, pv)

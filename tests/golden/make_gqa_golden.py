@@ -83,6 +83,22 @@ CASES += [
 ]
 ROTARY["bias_rot_window"] = (16, False, [[1, 2, 3], [4, 5, 6]])
 
+# qk_output diagnostics (output 3, test_gqa_position_cache.py:130-131): name -> mode (1 = the
+# visible logits, 2 = the probabilities).
+QK = {
+    "qk_scores_bias": 1,
+    "qk_scores_window": 1,
+    "qk_probs_composed_fp16": 2,
+    "qk_probs_past_only": 2,
+}
+CASES += [
+    ("qk_scores_bias", "float32", 2, 2, 2, 6, [3, 6], 6, True, -1, False),
+    ("qk_scores_window", "float32", 1, 4, 4, 9, [9], 9, True, 3, False),
+    ("qk_probs_composed_fp16", "float16", 1, 3, 3, 8, [8], 8, True, 4, True),
+    ("qk_probs_past_only", "float32", 2, 1, 0, 6, [4, 6], 6, True, -1, True),
+]
+BIAS["qk_scores_bias"] = (2, HEADS)
+
 
 def load_reference(path):
     with open(path) as f:
@@ -142,15 +158,19 @@ def main():
             add_rotary(feeds, i, half, ids, dtype)
         if name in BIAS:
             add_bias(feeds, i, BIAS[name], seq, total, dtype)
-        out, pk, pv = ref(feeds, causal=causal, window=window, composed=composed, interleaved=interleaved)
+        mode = QK.get(name, 0)
+        res = ref(feeds, causal=causal, window=window, composed=composed, interleaved=interleaved, mode=mode)
+        out, pk, pv = res[:3]
         for key, val in feeds.items():
             arrays[f"{name}/in/{key}"] = val
         arrays[f"{name}/out/output"] = out
         arrays[f"{name}/out/present_k"] = pk
         arrays[f"{name}/out/present_v"] = pv
+        if mode:
+            arrays[f"{name}/out/qk"] = res[3]
         meta.append(dict(name=name, dtype=dtype, batch=batch, seq=seq, new_seq=new_seq, cap=cap,
                          total=total, causal=causal, window=window, composed=composed,
-                         interleaved=bool(interleaved)))
+                         interleaved=bool(interleaved), mode=mode))
     # q/k RMS norm inputs 14 / 15 (tests/ops/test_gqa11.py:52-130): the test's seeded inputs and
     # its own expectation, restated (fp32, head 8, past 2, three new rows, eps 1e-5).
     b, sq, past, nh, kvh, head = 1, 3, 2, 4, 2, 8

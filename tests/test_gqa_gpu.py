@@ -73,9 +73,14 @@ def test_golden_cases(case, in_place):
                   sin_cache=dev(f["sin"]), position_ids=f.get("pos"))
     if "bias" in f:  # attention_bias [1|B, 1|H, S, total]
         kw["attention_bias"] = dev(f["bias"])
-    out, ok, ov = gqa.group_query_attention(q, k, v, pk, pv, lengths, int(f["total"][0]), sink, check_status=True, **kw)
+    mode = case.get("mode", 0)
+    res = gqa.group_query_attention(q, k, v, pk, pv, lengths, int(f["total"][0]), sink, check_status=True,
+                                    qk_output=mode, **kw)
+    out, ok, ov = res[:3]
     torch.cuda.synchronize()
     check(host(out), GOLDEN[f"{name}/out/output"], case["dtype"])
+    if mode:  # qk_output diagnostics [B, H, S, total]
+        check(host(res[3]), GOLDEN[f"{name}/out/qk"], case["dtype"])
     np.testing.assert_array_equal(host(ok), GOLDEN[f"{name}/out/present_k"])
     np.testing.assert_array_equal(host(ov), GOLDEN[f"{name}/out/present_v"])
 

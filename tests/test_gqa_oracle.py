@@ -23,12 +23,17 @@ def feeds_of(name):
 @pytest.mark.parametrize("case", META, ids=[c["name"] for c in META])
 def test_oracle_matches_reference_oracle(case):
     f = feeds_of(case["name"])
-    out, pk, pv = gqa_ref.group_query_attention(
+    mode = case.get("mode", 0)
+    res = gqa_ref.group_query_attention(
         f["q"], f["k"] if case["new_seq"] else None, f["v"] if case["new_seq"] else None, f["pk"], f["pv"],
         f["lengths"], f["total"], num_heads=4, kv_num_heads=2, causal=case["causal"], window=case["window"],
         softcap=0.7 if case["composed"] else 0.0, sink=f.get("sink"), cos=f.get("cos"), sin=f.get("sin"),
-        position_ids=f.get("pos"), interleaved=case.get("interleaved", False), bias=f.get("bias"))
+        position_ids=f.get("pos"), interleaved=case.get("interleaved", False), bias=f.get("bias"), qk_output=mode)
+    out, pk, pv = res[:3]
     tol = 1e-5 if case["dtype"] == "float32" else 2e-3
+    if mode:  # qk_output diagnostics
+        np.testing.assert_allclose(res[3].astype(np.float32), DATA[f"{case['name']}/out/qk"].astype(np.float32),
+                                   rtol=tol, atol=tol)
     want = DATA[f"{case['name']}/out/output"]
     np.testing.assert_allclose(out.astype(np.float32), want.astype(np.float32), rtol=tol, atol=tol)
     # present: the reference keeps the cap-row buffer; this restatement has max(cap, total) rows
