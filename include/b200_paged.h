@@ -313,6 +313,16 @@ typedef struct B200GqaParams {
    * total_sequence_length] in dtype, columns from each row's length on are 0. */
   int32_t qk_output;
   void* output_qk;
+  /* integer caches (kv_cache_bit_width 8 / 4, inputs 12 / 13, kv_cache.rs:16-108,
+   * test_quantized_kv.py:22-195): past and present hold int8 codes, or +8-biased int4 nibbles
+   * (two channels per byte, the even channel in the low nibble; rows of head_size / 2 bytes).
+   * New rows are encoded as rint(x * (1 / scale)) clipped to the code range (scale 0 -> 1) and
+   * the attention reads every key and value decoded (code * scale), new rows included; scales
+   * are PER_TENSOR [1] or PER_CHANNEL [kv_num_heads, head_size] fp32. */
+  int32_t cache_dtype;        /* 0 or dtype: float caches; B200_DTYPE_INT8 or _UINT8 (int4) */
+  const float* k_scale;
+  const float* v_scale;
+  int32_t k_quant_per_channel, v_quant_per_channel;
 } B200GqaParams;
 
 B200_API int b200_gqa_params_size(void);
@@ -328,8 +338,7 @@ B200_API int b200_group_query_attention(const B200GqaParams* p, void* stream);
 B200_API int b200_group_query_attention_read_status(const B200GqaParams* p, void* stream);
 
 /* Claim predicate, restating group_query_attention_claim (attention.rs:2407-2754) over a
- * plain node description, plus this build's own declines (sliding_window_cache, integer
- * caches, head size).  Returns 1 (claim) or 0
+ * plain node description, plus this build's own declines (sliding_window_cache, head size).  Returns 1 (claim) or 0
  * (decline, reason written to `reason`). */
 typedef struct B200GqaNodeInfo {
   int32_t num_inputs;
@@ -344,6 +353,8 @@ typedef struct B200GqaNodeInfo {
   float scale;
   int32_t has_qk_norm_epsilon; /* 0 = attribute absent: 1e-6                                 */
   float qk_norm_epsilon;
+  char k_quant_type[16];     /* "NONE" (default), "PER_TENSOR", "PER_CHANNEL"                */
+  char v_quant_type[16];
 } B200GqaNodeInfo;
 
 B200_API int b200_group_query_attention_claim(const B200GqaNodeInfo* node, char* reason, size_t reason_len);

@@ -268,6 +268,42 @@ struct GView {
   const B200TensorInfo* out(int i) const { return out_present(i) ? &n->outputs[i] : nullptr; }
 };
 
+// kv_cache.rs:16-108 with paged = false: inputs 12 / 13 are the scales, kv_cache_bit_width
+// states the storage.
+void gqa_kv_cache_claim(const GView& v, int activation, int64_t heads, int64_t head) {
+  const B200GqaNodeInfo& n = *v.n;
+  const int cache_type = v.in(3) ? v.in(3)->dtype : activation;
+  const bool quantized = integer_cache(cache_type);
+  struct Side { int cache, scale; const char* name; const char* quant; };
+  const Side sides[2] = {{3, 12, "k", n.k_quant_type}, {4, 13, "v", n.v_quant_type}};
+  for (const Side& s : sides) {
+    const int dtype = v.in(s.cache) ? v.in(s.cache)->dtype : activation;
+    REQUIRE(dtype == cache_type, "key/value caches must share one storage dtype");
+    const std::string mode = s.quant[0] ? std::string(s.quant, strnlen(s.quant, 16)) : "NONE";
+    if (quantized) {
+      REQUIRE(mode == "PER_TENSOR" || mode == "PER_CHANNEL",
+              "integer %s cache requires PER_TENSOR or PER_CHANNEL quantization", s.name);
+      const B200TensorInfo* info = v.in(s.scale);
+      if (!info) deny("quantized %s cache requires a scale tensor", s.name);
+      REQUIRE(info->dtype == B200_DTYPE_FLOAT, "%s_scale must be float32", s.name);
+      bool known = info->rank >= 0;
+      int64_t count = 1;
+      for (int i = 0; i < info->rank && known; ++i) {
+        if (info->shape[i] < 0) known = false; else count *= info->shape[i];
+      }
+      const int64_t expected = mode == "PER_TENSOR" ? 1 : heads * head;
+      REQUIRE(!known || count == expected, "%s_scale must contain %lld elements", s.name, (long long)expected);
+    } else {
+      REQUIRE(dtype == activation && mode == "NONE" && !v.in_present(s.scale),
+              "floating %s cache requires activation dtype, NONE quantization and no scale", s.name);
+    }
+    if (v.out_present(s.cache - 2))
+      REQUIRE(v.out(s.cache - 2)->dtype == dtype, "present %s cache must retain its input storage dtype", s.name);
+  }
+  const int64_t expected_bits = cache_type == B200_DTYPE_INT8 ? 8 : cache_type == B200_DTYPE_UINT8 ? 4 : 0;
+  REQUIRE(n.kv_cache_bit_width == expected_bits, "kv_cache_bit_width must agree with cache storage");
+}
+
 bool same_shape(const B200TensorInfo* a, const B200TensorInfo* b) {
   if (!a || !b || a->rank != b->rank) return false;
   for (int i = 0; i < a->rank && i < B200_MAX_RANK; ++i)
@@ -336,6 +372,20 @@ void gqa_claim(const GView& v) {
   const int64_t total_heads = packed ? nh + 2 * kvh : nh;
   REQUIRE(q->shape[2] % total_heads == 0, "query hidden size must match head count");
   const int64_t head = q->shape[2] / total_heads;
+  gqa_kv_cache_claim(v, out_type, kvh, head);
+  const int64_t bits = n.kv_cache_bit_width;
+  REQUIRE(bits != 4 || head % 2 == 0,
+          "GQA packed INT4 requires an even logical head size (pinned CheckPast byte geometry)");
+  REQUIRE(!sliding || bits == 0 || head % (bits == 4 ? 32 : 16) == 0,
+          "sliding integer cache rows must satisfy pinned 16-byte alignment");
+  const int64_t cache_head = bits == 4 ? (head + 1) / 2 : head;
+  if (has_bias) {
+    const B200TensorInfo* bias = v.in(10);
+    REQUIRE((bias->shape[0] < 0 || bias->shape[0] == 1 || q->shape[0] < 0 || bias->shape[0] == q->shape[0]) &&
+                (bias->shape[1] < 0 || bias->shape[1] == 1 || bias->shape[1] == nh) &&
+                (bias->shape[2] < 0 || q->shape[1] < 0 || bias->shape[2] == q->shape[1]),
+            "attention_bias must broadcast to [batch,num_heads,sequence_length,total_sequence_length]");
+  }
   if (!packed) {
     for (int idx : {1, 2}) {
       const B200TensorInfo* kv = v.in(idx);
@@ -350,7 +400,7 @@ void gqa_claim(const GView& v) {
   for (int idx : {3, 4}) {
     const B200TensorInfo* c = v.in(idx);
     if (!c) continue;
-    REQUIRE(c->rank == 4 && c->shape[1] == kvh && c->shape[3] == head &&
+    REQUIRE(c->rank == 4 && c->shape[1] == kvh && c->shape[3] == cache_head &&
                 (c->shape[0] < 0 || q->shape[0] < 0 || c->shape[0] == q->shape[0]),
             "past cache must be [batch,kv_num_heads,capacity,stored_head_size]");
   }
@@ -388,7 +438,6 @@ void gqa_claim(const GView& v) {
   REQUIRE(std::isfinite(n.softcap) && n.softcap >= 0.f, "softcap must be finite and non-negative");
   // Forms the reference accepts that this build does not implement (the node stays on ORT).
   REQUIRE(!sliding, "sliding_window_cache is not implemented on B200");
-  REQUIRE(!quantized && n.kv_cache_bit_width == 0, "integer GroupQueryAttention caches are not implemented on B200");
   REQUIRE(head % 8 == 0 && head <= 256, "head_size must be a multiple of 8 up to 256 on B200, got %lld", (long long)head);
 }
 

@@ -307,6 +307,8 @@ void describe_gqa(const GraphReader& g, const OrtNode* node, B200GqaNodeInfo* n)
   if (!g.float_attr(node, "softcap", &n->softcap)) n->softcap = 0.f;
   n->has_scale = g.float_attr(node, "scale", &n->scale) ? 1 : 0;
   n->has_qk_norm_epsilon = g.float_attr(node, "qk_norm_epsilon", &n->qk_norm_epsilon) ? 1 : 0;
+  g.string_attr(node, "k_quant_type", n->k_quant_type, sizeof n->k_quant_type);
+  g.string_attr(node, "v_quant_type", n->v_quant_type, sizeof n->v_quant_type);
 }
 
 }  // namespace
@@ -636,15 +638,18 @@ void ComputeInfo::run_gqa(OrtKernelContext* kctx, void* stream) {
   if (in[9].present) ids = host_values<int64_t>(in[9], device);
   const int64_t cap = in[3].present ? in[3].dim(2) : 0;
   const int64_t pcap = std::max<int64_t>(cap, total[0]);
+  // integer caches (kv_cache_bit_width): present rows keep the past's stored width
+  const bool int_cache = in[3].present && (in[3].dtype == B200_DTYPE_INT8 || in[3].dtype == B200_DTYPE_UINT8);
+  const int64_t width = int_cache ? in[3].dim(3) : D;
 
   Bound out0 = output(kctx, 0, {B, S, H * D});
-  Bound out1 = output(kctx, 1, {B, KV, pcap, D});
-  Bound out2 = output(kctx, 2, {B, KV, pcap, D});
+  Bound out1 = output(kctx, 1, {B, KV, pcap, width});
+  Bound out2 = output(kctx, 2, {B, KV, pcap, width});
   Bound out3 = output(kctx, 3, {B, H, S, total[0]});  // qk_output diagnostics
 
-  staging.plan({&in[0], &in[1], &in[2], &in[3], &in[4], &in[5], &in[7], &in[8], &in[9], &in[10], &in[11], &in[14],
-                &in[15], &out0, &out1, &out2, &out3});
-  for (int i : {0, 1, 2, 3, 4, 5, 7, 8, 9, 10, 11, 14, 15}) staging.place(&in[i], true, false, stream);
+  staging.plan({&in[0], &in[1], &in[2], &in[3], &in[4], &in[5], &in[7], &in[8], &in[9], &in[10], &in[11], &in[12],
+                &in[13], &in[14], &in[15], &out0, &out1, &out2, &out3});
+  for (int i : {0, 1, 2, 3, 4, 5, 7, 8, 9, 10, 11, 12, 13, 14, 15}) staging.place(&in[i], true, false, stream);
   staging.place(&out0, false, true, stream);
   staging.place(&out1, false, true, stream);
   staging.place(&out2, false, true, stream);
@@ -679,6 +684,11 @@ void ComputeInfo::run_gqa(OrtKernelContext* kctx, void* stream) {
     raise(ORT_INVALID_ARGUMENT, "GroupQueryAttention: seqlens_k must hold batch_size values");
   p.head_sink = in[11].dev;
   p.output_qk = out3.dev;        // with the node's qk_output mode
+  if (int_cache) {               // with the node's k / v quant types
+    p.cache_dtype = in[3].dtype;
+    p.k_scale = static_cast<const float*>(in[12].dev);
+    p.v_scale = static_cast<const float*>(in[13].dev);
+  }
   p.q_norm_weight = in[14].dev;  // with k_norm_weight; epsilon from the node's attribute
   p.k_norm_weight = in[15].dev;
   if (in[10].present) {  // attention_bias [1|B, 1|H, S, total]

@@ -60,6 +60,11 @@ struct GqaArgs {
   int64_t bias_bstride, bias_hstride;     // 0 for a broadcast (size-1) dimension
   void* qk_out;                           // qk_output diagnostics [B, H, S, total] or null
   int qk_mode;                            // 1 logits, 2 probabilities
+  int cache_bits;                         // 0 float caches, 8 int8, 4 int4 (codes in pk / pv, ok / ov)
+  int cache_w;                            // bytes per stored cache row (int caches)
+  const float* kscale;                    // int caches: PER_TENSOR [1] or PER_CHANNEL [KV, D]
+  const float* vscale;
+  int kpc, vpc;                           // per-channel scales
   void* out;
   int row_tiles, splits, fused_copy, present_separate;
   float* part_o;   // [groups][splits][R][D]
@@ -885,6 +890,179 @@ __global__ void __launch_bounds__(256) gqa_rope_kernel(const GqaRope r) {
   }
 }
 
+// ------------------------------------------------------------------ integer caches
+// kv_cache_bit_width 8 / 4 (kv_cache.rs:16-108; test_quantized_kv.py:22-47 with paged = false):
+// a code is rint(x * (1 / scale)) clipped to [-2^(bits-1), 2^(bits-1) - 1], a zero scale
+// multiplying by 1; int4 codes are stored +8-biased, two per byte, the even channel in the low
+// nibble.  A cached value is code * scale.  New rows go through the same encoding before the
+// attention reads them, as the reference reads every key and value from the encoded cache.
+__device__ __forceinline__ int gqa_code(float x, float scale, int bits) {
+  const float inv = scale != 0.f ? __fdiv_rn(1.f, scale) : 1.f;
+  const float lim = bits == 8 ? 128.f : 8.f;
+  return (int)fminf(fmaxf(rintf(__fmul_rn(x, inv)), -lim), lim - 1.f);
+}
+
+__device__ __forceinline__ float gqa_scale(const GqaArgs& a, bool value, int kh, int d) {
+  const float* sc = value ? a.vscale : a.kscale;
+  return (value ? a.vpc : a.kpc) ? sc[(int64_t)kh * a.D + d] : sc[0];
+}
+
+// Channel d of key / value row `pos` of kv head kh of batch b, decoded: past rows from the
+// integer past cache, new rows encoded and decoded on the fly.
+template <typename T>
+__device__ __forceinline__ float gqa_int_value(const GqaArgs& a, const BatchGeom& bg, int b, int kh, int pos, int d,
+                                               bool value) {
+  const float scale = gqa_scale(a, value, kh, d);
+  int code;
+  if (pos < bg.past) {
+    const uint8_t* row = static_cast<const uint8_t*>(value ? a.pv : a.pk) + (((int64_t)b * a.KV + kh) * a.cap + pos) * a.cache_w;
+    if (a.cache_bits == 8) {
+      code = (int)reinterpret_cast<const int8_t*>(row)[d];
+    } else {
+      const uint8_t byte = row[d >> 1];
+      code = (int)((d & 1) ? byte >> 4 : byte & 15) - 8;
+    }
+  } else {
+    const T* src = static_cast<const T*>(value ? a.v : a.k);
+    const int64_t stride = value ? a.v_stride : a.k_stride;
+    code = gqa_code(to_f(src[((int64_t)b * a.new_seq + (pos - bg.past)) * stride + (int64_t)kh * a.D + d]), scale,
+                    a.cache_bits);
+  }
+  return __fmul_rn((float)code, scale);
+}
+
+// present rows of an integer cache: past rows copied (a separate present buffer), new rows
+// encoded, the old buffer's rows past the length copied, then zero codes up to present_cap.
+// One thread per stored byte of one row; grid (rows of B * KV heads).
+template <typename T>
+__global__ void __launch_bounds__(256) gqa_int_present_kernel(const GqaArgs a) {
+  const int64_t row = blockIdx.x;  // (b * KV + kh) * pcap + r
+  const int r = (int)(row % a.pcap), kh = (int)((row / a.pcap) % a.KV), b = (int)(row / ((int64_t)a.pcap * a.KV));
+  const BatchGeom bg = batch_geom(a, b);
+  const bool separate = a.present_separate != 0;
+  const bool is_new = a.new_seq > 0 && r >= bg.past && r < bg.length;
+  if (!separate && !is_new) return;  // shared buffer: only the new rows change
+  const uint8_t zero = a.cache_bits == 8 ? 0 : 0x88;
+  for (int side = 0; side < 2; ++side) {
+    uint8_t* dst = static_cast<uint8_t*>(side ? a.ov : a.ok) + row * a.cache_w;
+    const uint8_t* src = a.cap > 0 ? static_cast<const uint8_t*>(side ? a.pv : a.pk) +
+                                         (((int64_t)b * a.KV + kh) * a.cap + r) * a.cache_w
+                                   : nullptr;
+    for (int j = threadIdx.x; j < a.cache_w; j += blockDim.x) {
+      uint8_t byte = zero;
+      if (is_new) {
+        const T* x = static_cast<const T*>(side ? a.v : a.k) +
+                     ((int64_t)b * a.new_seq + (r - bg.past)) * (side ? a.v_stride : a.k_stride) + (int64_t)kh * a.D;
+        if (a.cache_bits == 8) {
+          byte = (uint8_t)(int8_t)gqa_code(to_f(x[j]), gqa_scale(a, side, kh, j), 8);
+        } else {
+          const int d0 = 2 * j, d1 = 2 * j + 1;
+          const int lo = gqa_code(to_f(x[d0]), gqa_scale(a, side, kh, d0), 4) + 8;
+          const int hi = d1 < a.D ? gqa_code(to_f(x[d1]), gqa_scale(a, side, kh, d1), 4) + 8 : 8;
+          byte = (uint8_t)(lo | (hi << 4));
+        }
+      } else if (r < a.cap) {
+        byte = src[j];
+      }
+      dst[j] = byte;
+    }
+  }
+}
+
+// Attention over integer caches: one CTA (4 warps) per (batch, head, query row); the warps split
+// the visible keys, the lanes the channels; online softmax per warp, merged in shared memory.
+template <typename T, int EPL>
+__global__ void __launch_bounds__(128) gqa_int_attention_kernel(const GqaArgs a) {
+  constexpr int kWarps = 4;
+  __shared__ float qs[32 * EPL];
+  __shared__ float red_m[kWarps], red_l[kWarps];
+  __shared__ float red_o[kWarps][32 * EPL];
+  const int row = blockIdx.x;  // (b * H + h) * S + s
+  const int s = row % a.S, h = (row / a.S) % a.H, b = row / (a.S * a.H);
+  const int kh = h / a.g, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *a.status = 0;
+  const BatchGeom bg = batch_geom(a, b);
+  const int pos = bg.query_past + s;
+  const int end = a.causal ? min(pos + 1, bg.length) : bg.length;
+  const int start = a.window > 0 ? max(0, end - a.window) : 0;
+  for (int d = threadIdx.x; d < 32 * EPL; d += blockDim.x)
+    qs[d] = d < a.D ? to_f(static_cast<const T*>(a.q)[((int64_t)b * a.S + s) * a.q_stride + (int64_t)h * a.D + d]) : 0.f;
+  __syncthreads();
+  const T* bias = a.bias ? static_cast<const T*>(a.bias) + b * a.bias_bstride + (int64_t)h * a.bias_hstride +
+                               (int64_t)s * a.total
+                         : nullptr;
+  float m = -INFINITY, l = 0.f, o[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) o[e] = 0.f;
+  for (int j = start + warp; j < end; j += kWarps) {
+    float dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int d = lane + 32 * e;
+      if (d < a.D) dot = fmaf(qs[d], gqa_int_value<T>(a, bg, b, kh, j, d, false), dot);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    float x = dot * a.scale;
+    if (a.softcap > 0.f) x = a.softcap * tanhf(x / a.softcap);
+    if (bias) x += to_f(bias[j]);
+    const float mn = fmaxf(m, x);
+    const float alpha = expf(m - mn);  // m = -inf on the first key gives 0
+    const float p = expf(x - mn);
+    l = l * alpha + p;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int d = lane + 32 * e;
+      const float vv = d < a.D ? gqa_int_value<T>(a, bg, b, kh, j, d, true) : 0.f;
+      o[e] = o[e] * alpha + p * vv;
+    }
+    m = mn;
+  }
+  if (lane == 0) {
+    red_m[warp] = m;
+    red_l[warp] = l;
+  }
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) red_o[warp][lane + 32 * e] = o[e];
+  __syncthreads();
+  if (warp != 0) return;
+  float M = -INFINITY;
+  for (int w = 0; w < kWarps; ++w) M = fmaxf(M, red_m[w]);
+  float sink = -INFINITY;
+  if (a.sink) sink = to_f(static_cast<const T*>(a.sink)[h]);
+  else if (a.smooth) sink = 0.f;
+  M = fmaxf(M, sink);
+  float L = sink == -INFINITY ? 0.f : expf(sink - M), f[kWarps];
+  for (int w = 0; w < kWarps; ++w) {
+    f[w] = red_m[w] == -INFINITY ? 0.f : expf(red_m[w] - M);
+    L += red_l[w] * f[w];
+  }
+  T* out = static_cast<T*>(a.out) + ((int64_t)b * a.S + s) * ((int64_t)a.H * a.D) + (int64_t)h * a.D;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int d = lane + 32 * e;
+    if (d >= a.D) continue;
+    float acc = 0.f;
+    for (int w = 0; w < kWarps; ++w) acc += red_o[w][d] * f[w];
+    out[d] = from_f<T>(L > 0.f ? acc / L : 0.f);
+  }
+}
+
+template <typename T>
+cudaError_t launch_int(const GqaArgs& a, cudaStream_t stream, int* launches) {
+  if (a.ok && a.pcap > 0) {
+    gqa_int_present_kernel<T><<<(unsigned)((int64_t)a.B * a.KV * a.pcap), 256, 0, stream>>>(a);
+    ++*launches;
+  }
+  const unsigned grid = (unsigned)(a.B * a.H * a.S);
+  const int epl = (a.D + 31) / 32;
+  if (epl <= 2) gqa_int_attention_kernel<T, 2><<<grid, 128, 0, stream>>>(a);
+  else if (epl <= 4) gqa_int_attention_kernel<T, 4><<<grid, 128, 0, stream>>>(a);
+  else gqa_int_attention_kernel<T, 8><<<grid, 128, 0, stream>>>(a);
+  ++*launches;
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ qk_output diagnostics
 // attention.rs:756-787: for every (batch, head, query row) the logits of keys [0, length)
 // (scale * q.k, soft-capped, plus attention_bias) where visible and 0 elsewhere (mode 1), or
@@ -909,9 +1087,13 @@ __global__ void __launch_bounds__(128) gqa_qk_kernel(const GqaArgs a) {
                                (int64_t)s * a.total
                          : nullptr;
   auto logit = [&](int j) {
-    const T* krow = key_row<T>(a, bg, b, kh, j, false);
     float acc = 0.f;
-    for (int d = 0; d < a.D; ++d) acc = fmaf(qrow[d], to_f(krow[d]), acc);
+    if (a.cache_bits) {
+      for (int d = 0; d < a.D; ++d) acc = fmaf(qrow[d], gqa_int_value<T>(a, bg, b, kh, j, d, false), acc);
+    } else {
+      const T* krow = key_row<T>(a, bg, b, kh, j, false);
+      for (int d = 0; d < a.D; ++d) acc = fmaf(qrow[d], to_f(krow[d]), acc);
+    }
     float x = acc * a.scale;
     if (a.softcap > 0.f) x = a.softcap * tanhf(x / a.softcap);
     if (bias) x += to_f(bias[j]);
@@ -1055,6 +1237,16 @@ int check_gqa(const B200GqaParams* p) {
                    "rotary caches must have matching [positions,rotary_dim/2] shapes within the head");
     if (p->position_ids && !p->host_position_ids)
       return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: position_ids need their host copy (host_position_ids)");
+  }
+  if (p->cache_dtype != 0 && p->cache_dtype != p->dtype && p->cache_dtype != B200_DTYPE_INT8 &&
+      p->cache_dtype != B200_DTYPE_UINT8)
+    return gfail(B200_ERR_UNSUPPORTED, "GroupQueryAttention: caches must be in the activation type, int8 or int4");
+  if ((p->cache_dtype == B200_DTYPE_INT8 || p->cache_dtype == B200_DTYPE_UINT8)) {
+    if (!p->k_scale || !p->v_scale)
+      return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: integer caches require k_scale and v_scale");
+    if (p->cache_dtype == B200_DTYPE_UINT8 && p->head_size % 2)
+      return gfail(B200_ERR_INVALID_ARGUMENT,
+                   "GQA packed INT4 requires an even logical head size (pinned CheckPast byte geometry)");
   }
   if (p->qk_output < 0 || p->qk_output > 2 || (p->qk_output != 0) != (p->output_qk != nullptr))
     return gfail(B200_ERR_INVALID_ARGUMENT,
@@ -1370,6 +1562,14 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
     a.splits = P.splits;
     a.fused_copy = P.fused && p->present_key != nullptr;
     a.present_separate = p->present_key != nullptr && p->present_key != p->past_key;
+    if (p->cache_dtype == B200_DTYPE_INT8 || p->cache_dtype == B200_DTYPE_UINT8) {
+      a.cache_bits = p->cache_dtype == B200_DTYPE_INT8 ? 8 : 4;
+      a.cache_w = a.cache_bits == 8 ? a.D : (a.D + 1) / 2;
+      a.kscale = p->k_scale;
+      a.vscale = p->v_scale;
+      a.kpc = p->k_quant_per_channel != 0;
+      a.vpc = p->v_quant_per_channel != 0;
+    }
     char* ws = static_cast<char*>(p->workspace);
     a.status = reinterpret_cast<int*>(ws + P.status);
     if (P.splits > 1) {
@@ -1421,13 +1621,19 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
         a.k_stride = (int64_t)a.KV * a.D;
       }
     }
-    // Rows past some batch's length exist in present only when a length is below its capacity.
-    bool tail_rows = false;
-    for (int b = 0; b < p->batch; ++b) tail_rows |= p->host_seqlens_k[b] + 1 < a.pcap;
-    const bool cluster = cluster_path(p, P);
-    if (a.dtype == B200_DTYPE_FLOAT) e = launch_gqa<float>(a, P, cluster, tail_rows, stream, &launches);
-    else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_gqa<__half>(a, P, cluster, tail_rows, stream, &launches);
-    else e = launch_gqa<__nv_bfloat16>(a, P, cluster, tail_rows, stream, &launches);
+    if (a.cache_bits) {  // integer caches: the codec kernels (a correctness path)
+      if (a.dtype == B200_DTYPE_FLOAT) e = launch_int<float>(a, stream, &launches);
+      else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_int<__half>(a, stream, &launches);
+      else e = launch_int<__nv_bfloat16>(a, stream, &launches);
+    } else {
+      // Rows past some batch's length exist in present only when a length is below its capacity.
+      bool tail_rows = false;
+      for (int b = 0; b < p->batch; ++b) tail_rows |= p->host_seqlens_k[b] + 1 < a.pcap;
+      const bool cluster = cluster_path(p, P);
+      if (a.dtype == B200_DTYPE_FLOAT) e = launch_gqa<float>(a, P, cluster, tail_rows, stream, &launches);
+      else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_gqa<__half>(a, P, cluster, tail_rows, stream, &launches);
+      else e = launch_gqa<__nv_bfloat16>(a, P, cluster, tail_rows, stream, &launches);
+    }
     add_launches(launches);
     if (e == cudaSuccess && p->qk_output) {  // diagnostics after the attention of the call
       a.qk_out = p->output_qk;

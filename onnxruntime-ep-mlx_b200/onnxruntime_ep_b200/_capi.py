@@ -101,6 +101,8 @@ class GqaParams(ctypes.Structure):
         ("attention_bias", _vp), ("bias_batch", _i32), ("bias_heads", _i32), ("bias_seq", _i32),
         ("bias_total", _i32), ("q_norm_weight", _vp), ("k_norm_weight", _vp), ("qk_norm_epsilon", _f32),
         ("qk_output", _i32), ("output_qk", _vp),
+        ("cache_dtype", _i32), ("k_scale", _vp), ("v_scale", _vp), ("k_quant_per_channel", _i32),
+        ("v_quant_per_channel", _i32),
     ]
 
 
@@ -115,7 +117,7 @@ class GqaNodeInfo(ctypes.Structure):
         ("smooth_softmax", _i64), ("qk_output", _i64), ("kv_cache_bit_width", _i64),
         ("has_causal", _i32), ("has_local_window_size", _i32), ("has_smooth_softmax", _i32),
         ("softcap", _f32), ("has_scale", _i32), ("scale", _f32), ("has_qk_norm_epsilon", _i32),
-        ("qk_norm_epsilon", _f32),
+        ("qk_norm_epsilon", _f32), ("k_quant_type", ctypes.c_char * 16), ("v_quant_type", ctypes.c_char * 16),
     ]
 
 

@@ -20,6 +20,7 @@ import ctypes
 import numpy as np
 import torch
 
+from . import _capi
 from ._capi import (DTYPE_BFLOAT16, DTYPE_FLOAT, DTYPE_FLOAT16, LIB, GqaParams, check)
 
 _DTYPES = {torch.float32: DTYPE_FLOAT, torch.float16: DTYPE_FLOAT16, torch.bfloat16: DTYPE_BFLOAT16}
@@ -44,7 +45,8 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
                  present_value=None, with_present=True, host_seqlens_k=None, output=None,
                  do_rotary=0, rotary_interleaved=0, cos_cache=None, sin_cache=None, position_ids=None,
                  attention_bias=None, q_norm_weight=None, k_norm_weight=None, qk_norm_epsilon=1e-6,
-                 qk_output=0, output_qk=None):
+                 qk_output=0, output_qk=None, k_scale=None, v_scale=None, k_quant_type="NONE",
+                 v_quant_type="NONE"):
     """Fill a ``B200GqaParams``.  Returns ``(params, keepalive, output, present_key, present_value)``.
 
     ``do_rotary=1`` takes ``cos_cache``/``sin_cache`` ``[positions, rotary_dim/2]`` (inputs 7 and
@@ -53,7 +55,10 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
     10, the activation dtype) is added to the scores of the visible keys.  ``q_norm_weight`` /
     ``k_norm_weight`` ``[head_size]`` (inputs 14 / 15) RMS-normalise every query head and new key
     head before the rotary embedding.  ``qk_output`` 1 / 2 fills ``output_qk`` ``[batch, heads,
-    seq, total]`` (allocated when not given) with the visible logits / the probabilities."""
+    seq, total]`` (allocated when not given) with the visible logits / the probabilities.  int8 /
+    uint8 (int4) ``past_key``/``past_value`` select the integer caches, with ``k_scale`` /
+    ``v_scale`` fp32 (inputs 12 / 13) and ``k_quant_type`` / ``v_quant_type`` PER_TENSOR or
+    PER_CHANNEL; present is allocated in the same storage."""
     H, KV = int(num_heads), int(kv_num_heads)
     packed = key is None and value is None  # packed QKV in query (inputs 1 and 2 absent)
     B, S = int(query.shape[0]), int(query.shape[1])
@@ -73,8 +78,13 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
     host_seqlens_k = np.ascontiguousarray(np.asarray(host_seqlens_k, dtype=np.int32))
     dev = query.device
     pcap = max(cap, total)
+    int_cache = past_key is not None and past_key.dtype in (torch.int8, torch.uint8)
     if with_present and present_key is None:
-        present_key = torch.empty((B, KV, pcap, D), dtype=query.dtype, device=dev)
+        if int_cache:
+            width = D if past_key.dtype == torch.int8 else (D + 1) // 2
+            present_key = torch.empty((B, KV, pcap, width), dtype=past_key.dtype, device=dev)
+        else:
+            present_key = torch.empty((B, KV, pcap, D), dtype=query.dtype, device=dev)
         present_value = torch.empty_like(present_key)
     if present_key is not None:
         pcap = int(present_key.shape[2])
@@ -134,6 +144,13 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
     if q_norm_weight is not None:
         p.q_norm_weight, p.k_norm_weight = _ptr(q_norm_weight), _ptr(k_norm_weight)
         p.qk_norm_epsilon = float(qk_norm_epsilon)
+    if int_cache:
+        p.cache_dtype = _capi.DTYPE_INT8 if past_key.dtype == torch.int8 else _capi.DTYPE_UINT8
+        k_scale = torch.as_tensor(k_scale, dtype=torch.float32).to(dev).contiguous()
+        v_scale = torch.as_tensor(v_scale, dtype=torch.float32).to(dev).contiguous()
+        p.k_scale, p.v_scale = _ptr(k_scale), _ptr(v_scale)
+        p.k_quant_per_channel = int(k_quant_type == "PER_CHANNEL")
+        p.v_quant_per_channel = int(v_quant_type == "PER_CHANNEL")
     if qk_output:
         if output_qk is None:
             output_qk = torch.empty((B, H, S, total), dtype=query.dtype, device=dev)
@@ -144,7 +161,7 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
     p.workspace = _ptr(ws)
     p.workspace_bytes = ws.numel()
     keep = (query, key, value, past_key, past_value, seqlens_k, head_sink, host_seqlens_k, ws, cos_cache, sin_cache,
-            position_ids, host_ids, attention_bias, q_norm_weight, k_norm_weight, output_qk)
+            position_ids, host_ids, attention_bias, q_norm_weight, k_norm_weight, k_scale, v_scale, output_qk)
     return p, keep, output, present_key, present_value
 
 

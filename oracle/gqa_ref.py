@@ -56,6 +56,32 @@ def rms_norm(x, weight, eps):
     return (xf / denom * np.asarray(weight, np.float32)).astype(x.dtype)
 
 
+def int_encode(x, scale, bits):
+    """Integer cache codes of ``x [..., D]`` (test_quantized_kv.py:22-38 with paged = False):
+    rint(x * (1 / scale)) clipped to the code range (scale 0 -> 1); int4 codes +8-biased, two
+    per byte, the even channel in the low nibble."""
+    x, scale = np.asarray(x, np.float32), np.asarray(scale, np.float32)
+    inverse = np.divide(np.float32(1), scale, out=np.ones_like(scale), where=scale != 0)
+    limit = 2 ** (bits - 1)
+    codes = np.clip(np.rint(x * inverse), -limit, limit - 1).astype(np.int8)
+    if bits == 8:
+        return codes
+    biased = (codes.astype(np.int16) + 8).astype(np.uint8)
+    if x.shape[-1] % 2:
+        biased = np.concatenate([biased, np.full((*biased.shape[:-1], 1), 8, np.uint8)], -1)
+    return biased[..., ::2] | (biased[..., 1::2] << 4)
+
+
+def int_decode(codes, scale, bits, head):
+    """Cached values ``code * scale`` (test_quantized_kv.py:40-46)."""
+    if bits == 4:
+        values = np.stack([codes & 15, codes >> 4], -1).reshape(*codes.shape[:-1], codes.shape[-1] * 2)[..., :head]
+        values = values.astype(np.float32) - 8
+    else:
+        values = codes.astype(np.float32)
+    return values * np.asarray(scale, np.float32)
+
+
 def rotary_positions(b, seq, query_past, total, position_ids):
     """Positions of batch row ``b``'s query rows (attention.rs:538-585): ``query_past + s``
     without ids; with ids, the first id as an offset on a first prompt (``total == seq``),
@@ -71,7 +97,8 @@ def rotary_positions(b, seq, query_past, total, position_ids):
 def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_heads, kv_num_heads,
                           scale=None, causal=True, window=-1, softcap=0.0, sink=None,
                           smooth_softmax=-1, cos=None, sin=None, position_ids=None, interleaved=False,
-                          out_dtype=None, bias=None, q_norm=None, k_norm=None, norm_eps=1e-6, qk_output=0):
+                          out_dtype=None, bias=None, q_norm=None, k_norm=None, norm_eps=1e-6, qk_output=0,
+                          k_scale=None, v_scale=None):
     """Returns ``(output [B,S,H*D], present_k, present_v [B,KV,max(cap,total),D])``.
 
     ``q`` [B,S,H*D]; ``k``/``v`` [B,new_seq,KV*D] (new_seq may be 0); ``past_k``/``past_v``
@@ -82,7 +109,9 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
     ``[D]`` RMS-normalise the query heads and new key heads before the rotary embedding.
     ``qk_output`` 1 / 2 also returns the diagnostics ``[B, H, S, total]``: the visible logits
     (0 elsewhere) / the probabilities, zero from each row's length on (test_gqa_position_cache.py:
-    130-131, attention.rs:771-787).  Arrays keep
+    130-131, attention.rs:771-787).  int8 / uint8 (int4) ``past_k``/``past_v`` hold integer codes
+    with ``k_scale`` / ``v_scale`` ``[1]`` or ``[KV, D]``: present is in the same storage, new rows
+    are encoded, and the attention reads every row decoded (test_quantized_kv.py:122-193).  Arrays keep
     their dtype; math is fp32, the output is rounded to the activation dtype (or kept in
     ``out_dtype``, e.g. fp32 for tolerance checks)."""
     B, S, hidden = q.shape
@@ -95,8 +124,17 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
     pcap = max(cap, total)
     dt = q.dtype
     scale = 1.0 / np.sqrt(D) if not scale else float(scale)
-    pk = np.zeros((B, KV, pcap, D), dt)
-    pv = np.zeros((B, KV, pcap, D), dt)
+    bits = 0
+    if past_k is not None and past_k.dtype in (np.int8, np.uint8):
+        bits = 8 if past_k.dtype == np.int8 else 4
+        ksc, vsc = (np.asarray(x, np.float32) for x in (k_scale, v_scale))
+        ksc, vsc = (x.reshape(KV, 1, D) if x.size > 1 else x.reshape(1) for x in (ksc, vsc))
+        zero = 0 if bits == 8 else 0x88
+        pk = np.full((B, KV, pcap, past_k.shape[3]), zero, past_k.dtype)
+        pv = np.full((B, KV, pcap, past_k.shape[3]), zero, past_k.dtype)
+    else:
+        pk = np.zeros((B, KV, pcap, D), dt)
+        pv = np.zeros((B, KV, pcap, D), dt)
     out = np.empty((B, S, H * D), out_dtype or dt)
     diag = np.zeros((B, H, S, total), out_dtype or dt)
     if sink is None and smooth_softmax == 1:
@@ -124,10 +162,19 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
             if new_seq:
                 kb = rotate(kb, cos, sin, ids, interleaved)
         if rows:
-            pk[b, :, past:length] = kb[:, :rows]
-            pv[b, :, past:length] = v[b, :rows].reshape(rows, KV, D).transpose(1, 0, 2)
-        keys = np.repeat(pk[b, :, :length].astype(np.float32), g, 0)   # [H, length, D]
-        vals = np.repeat(pv[b, :, :length].astype(np.float32), g, 0)
+            vrows = v[b, :rows].reshape(rows, KV, D).transpose(1, 0, 2)
+            if bits:
+                pk[b, :, past:length] = int_encode(kb[:, :rows], ksc, bits)
+                pv[b, :, past:length] = int_encode(vrows, vsc, bits)
+            else:
+                pk[b, :, past:length] = kb[:, :rows]
+                pv[b, :, past:length] = vrows
+        if bits:
+            keys = np.repeat(int_decode(pk[b, :, :length], ksc, bits, D), g, 0)
+            vals = np.repeat(int_decode(pv[b, :, :length], vsc, bits, D), g, 0)
+        else:
+            keys = np.repeat(pk[b, :, :length].astype(np.float32), g, 0)   # [H, length, D]
+            vals = np.repeat(pv[b, :, :length].astype(np.float32), g, 0)
         qh = qb.astype(np.float32)  # [H, S, D]
         scores = qh @ keys.transpose(0, 2, 1) * np.float32(scale)
         if softcap > 0:

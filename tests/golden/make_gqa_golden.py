@@ -99,16 +99,42 @@ CASES += [
 ]
 BIAS["qk_scores_bias"] = (2, HEADS)
 
+# integer caches (kv_cache_bit_width, inputs 12 / 13; test_quantized_kv.py:81-193): name -> (bits,
+# k / v quant modes).  The reference's _encode encodes the past caches, its _scales gives the
+# scales and its _gqa_ref the expected output and present codes.
+INT = {
+    "int8_per_channel": (8, ("PER_CHANNEL", "PER_CHANNEL")),
+    "int4_per_tensor": (4, ("PER_TENSOR", "PER_TENSOR")),
+    "int8_fp16_composed_probs": (8, ("PER_TENSOR", "PER_CHANNEL")),
+    "int4_rot_window": (4, ("PER_CHANNEL", "PER_TENSOR")),
+    "int8_past_only": (8, ("PER_CHANNEL", "PER_CHANNEL")),
+}
+CASES += [
+    ("int8_per_channel", "float32", 2, 2, 2, 6, [3, 6], 6, True, -1, False),
+    ("int4_per_tensor", "float32", 2, 2, 2, 6, [4, 6], 6, True, -1, False),
+    ("int8_fp16_composed_probs", "float16", 1, 2, 2, 8, [6], 6, True, -1, True),
+    ("int4_rot_window", "float32", 2, 3, 3, 8, [5, 8], 8, True, 3, False),
+    ("int8_past_only", "float32", 2, 1, 0, 6, [4, 6], 6, True, -1, False),
+]
+QK["int8_fp16_composed_probs"] = 2
+BIAS["int8_fp16_composed_probs"] = (1, HEADS)
+ROTARY["int4_rot_window"] = (16, False, [[1, 2, 3], [4, 5, 6]])
 
-def load_reference(path):
+
+def load_functions(path, names, extra=None):
     with open(path) as f:
         tree = ast.parse(f.read(), filename=path)
-    wanted = [n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name in ("_rotate", "_reference")]
-    if len(wanted) != 2:
-        raise SystemExit(f"{path}: _rotate/_reference not found")
+    wanted = [n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name in names]
+    if len(wanted) != len(names):
+        raise SystemExit(f"{path}: {names} not all found")
     ns = {"np": np, "__builtins__": __builtins__}
+    ns.update(extra or {})
     exec(compile(ast.Module(body=wanted, type_ignores=[]), path, "exec"), ns)
-    return ns["_reference"]
+    return ns
+
+
+def load_reference(path):
+    return load_functions(path, ("_rotate", "_reference"))["_reference"]
 
 
 def make_feeds(index, dtype, batch, seq, new_seq, cap, lengths, total, composed):
@@ -149,6 +175,9 @@ def main():
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
     args = ap.parse_args()
     ref = load_reference(os.path.join(args.reference, "tests", "ops", "test_gqa_position_cache.py"))
+    gqa_ns = load_functions(os.path.join(args.reference, "tests", "ops", "test_gqa_position_cache.py"), ("_rotate",))
+    quant = load_functions(os.path.join(args.reference, "tests", "ops", "test_quantized_kv.py"),
+                           ("_encode", "_decode", "_scores", "_scales", "_gqa_ref"), {"_rotate": gqa_ns["_rotate"]})
     arrays, meta = {}, []
     for i, (name, dtype, batch, seq, new_seq, cap, lengths, total, causal, window, composed) in enumerate(CASES):
         feeds = make_feeds(i, dtype, batch, seq, new_seq, cap, lengths, total, composed)
@@ -159,7 +188,16 @@ def main():
         if name in BIAS:
             add_bias(feeds, i, BIAS[name], seq, total, dtype)
         mode = QK.get(name, 0)
-        res = ref(feeds, causal=causal, window=window, composed=composed, interleaved=interleaved, mode=mode)
+        if name in INT:  # encode the past caches, then the reference's integer GQA oracle
+            bits, modes = INT[name]
+            for side, key in enumerate(("k", "v")):
+                sc = quant["_scales"](KV, HEAD, modes[side], side)
+                feeds[f"{key}_scale"] = sc
+                shaped = sc.reshape(1, KV, 1, HEAD) if modes[side] == "PER_CHANNEL" else sc
+                feeds[f"p{key}"] = quant["_encode"](feeds[f"p{key}"], shaped, bits)
+            res = quant["_gqa_ref"](feeds, bits, causal=causal, window=window, composed=composed, mode=mode)
+        else:
+            res = ref(feeds, causal=causal, window=window, composed=composed, interleaved=interleaved, mode=mode)
         out, pk, pv = res[:3]
         for key, val in feeds.items():
             arrays[f"{name}/in/{key}"] = val
@@ -170,7 +208,9 @@ def main():
             arrays[f"{name}/out/qk"] = res[3]
         meta.append(dict(name=name, dtype=dtype, batch=batch, seq=seq, new_seq=new_seq, cap=cap,
                          total=total, causal=causal, window=window, composed=composed,
-                         interleaved=bool(interleaved), mode=mode))
+                         interleaved=bool(interleaved), mode=mode,
+                         bits=INT[name][0] if name in INT else 0,
+                         quant_modes=list(INT[name][1]) if name in INT else None))
     # q/k RMS norm inputs 14 / 15 (tests/ops/test_gqa11.py:52-130): the test's seeded inputs and
     # its own expectation, restated (fp32, head 8, past 2, three new rows, eps 1e-5).
     b, sq, past, nh, kvh, head = 1, 3, 2, 4, 2, 8

@@ -133,6 +133,41 @@ def test_reference_rotary_declines(mutate, reason):
     assert ok == 0 and why.startswith(reason), why
 
 
+def int_gnode(bits=8, modes=(b"PER_CHANNEL", b"PER_TENSOR")):
+    """Config-1 geometry with integer caches (kv_cache_bit_width, scales on inputs 12 / 13)."""
+    n = gnode(n_inputs=14)
+    dt = I8 if bits == 8 else _capi.DTYPE_UINT8
+    w = 128 if bits == 8 else 64
+    for i in (3, 4):
+        tensor(n.inputs[i], dt, [1, 8, 2048, w])
+    for i in (1, 2):
+        tensor(n.outputs[i], dt, [1, 8, -1, w])
+    n.kv_cache_bit_width = bits
+    n.k_quant_type, n.v_quant_type = modes
+    for i, m in ((12, modes[0]), (13, modes[1])):
+        tensor(n.inputs[i], F32, [8, 1, 128] if m == b"PER_CHANNEL" else [1])
+    return n
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_integer_caches_are_claimed(bits):
+    assert claim(int_gnode(bits)) == (1, "")
+
+
+@pytest.mark.parametrize("mutate,reason", [
+    (lambda n: setattr(n, "kv_cache_bit_width", 4), "kv_cache_bit_width must agree with cache storage"),
+    (lambda n: setattr(n, "k_quant_type", b"NONE"), "integer k cache requires PER_TENSOR or PER_CHANNEL"),
+    (lambda n: tensor(n.inputs[12], F32, [4]), "k_scale must contain 1024 elements"),
+    (lambda n: setattr(n.inputs[13], "present", 0), "quantized v cache requires a scale tensor"),
+    (lambda n: tensor(n.outputs[1], F32, [1, 8, -1, 128]), "output 1 must retain its cache dtype"),
+])
+def test_integer_cache_rules(mutate, reason):
+    n = int_gnode()
+    mutate(n)
+    ok, why = claim(n)
+    assert ok == 0 and reason in why, why
+
+
 def test_attention_bias_is_claimed():
     n = gnode()
     n.num_inputs = 11
@@ -147,9 +182,6 @@ def test_attention_bias_is_claimed():
 
 
 @pytest.mark.parametrize("mutate,reason", [
-    (lambda n: (tensor(n.inputs[3], I8, [1, 8, 2048, 128]), tensor(n.inputs[4], I8, [1, 8, 2048, 128]),
-                tensor(n.outputs[1], I8, [1, 8, -1, 128]), tensor(n.outputs[2], I8, [1, 8, -1, 128])),
-     "integer GroupQueryAttention caches are not implemented on B200"),
     (lambda n: (setattr(n, "sliding_window_cache", 1), _set("local_window_size", 64)(n)),
      "sliding_window_cache is not implemented on B200"),
 ])

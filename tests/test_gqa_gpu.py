@@ -73,6 +73,9 @@ def test_golden_cases(case, in_place):
                   sin_cache=dev(f["sin"]), position_ids=f.get("pos"))
     if "bias" in f:  # attention_bias [1|B, 1|H, S, total]
         kw["attention_bias"] = dev(f["bias"])
+    if case.get("bits"):  # integer caches: codes in pk / pv, scales (inputs 12 / 13)
+        kw.update(k_scale=dev(f["k_scale"]), v_scale=dev(f["v_scale"]), k_quant_type=case["quant_modes"][0],
+                  v_quant_type=case["quant_modes"][1])
     mode = case.get("mode", 0)
     res = gqa.group_query_attention(q, k, v, pk, pv, lengths, int(f["total"][0]), sink, check_status=True,
                                     qk_output=mode, **kw)
@@ -287,3 +290,41 @@ def test_config1_with_qk_norm_and_rotary(dtype):
 
 def test_qk_norm_prefill_rows():
     run_case(np.random.default_rng(42), dtype="float16", S=17, cap=64, lengths=[81, 30], H=8, KV=2, qk_norm=True)
+
+
+# ---- integer caches (kv_cache_bit_width 8 / 4, inputs 12 / 13) ---------------------------------
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("dtype,S,lengths,cap", [("float32", 1, [2049], 2048), ("bfloat16", 5, [300, 77], 320)])
+def test_integer_caches(bits, dtype, S, lengths, cap):
+    """Config-1 geometry (and a ragged prefill batch) with int8 / int4 caches: present codes
+    bit-exact, attention within the fp32 tolerance of the decoded-cache oracle."""
+    rng = np.random.default_rng(50 + bits + S)
+    H, KV, D = 32, 8, 128
+    B = len(lengths)
+    total = max(lengths)
+    tdt = TORCH_DT[dtype]
+    to = lambda a: torch.from_numpy(a).to(DEV).to(tdt)
+    q, k, v = (to((rng.standard_normal((B, S, n * D)) * 0.5).astype(np.float32)) for n in (H, KV, KV))
+    back = lambda t: t.float().cpu().numpy()
+    ks = rng.uniform(0.01, 0.05, (KV, D)).astype(np.float32)   # PER_CHANNEL keys
+    vs = np.array([0.03], np.float32)                          # PER_TENSOR values
+    pkf = (rng.standard_normal((B, KV, cap, D)) * 0.5).astype(np.float32)
+    pvf = (rng.standard_normal((B, KV, cap, D)) * 0.5).astype(np.float32)
+    pk = gqa_ref.int_encode(pkf, ks.reshape(KV, 1, D), bits)
+    pv = gqa_ref.int_encode(pvf, vs, bits)
+    qn, kn, vn = back(q), back(k), back(v)
+    if dtype != "float32":
+        import ml_dtypes
+        qn, kn, vn = (a.astype(ml_dtypes.bfloat16) for a in (qn, kn, vn))
+    lens = np.asarray(lengths) - 1
+    want, wk, wv = gqa_ref.group_query_attention(qn, kn, vn, pk, pv, lens, total, num_heads=H, kv_num_heads=KV,
+                                                 out_dtype=np.float32, k_scale=ks, v_scale=vs)
+    out, ok, ov = gqa.group_query_attention(
+        q, k, v, torch.from_numpy(pk).to(DEV), torch.from_numpy(pv).to(DEV),
+        torch.tensor(lens, dtype=torch.int32, device=DEV), total, num_heads=H, kv_num_heads=KV,
+        k_scale=torch.from_numpy(ks).to(DEV), v_scale=torch.from_numpy(vs).to(DEV), k_quant_type="PER_CHANNEL",
+        v_quant_type="PER_TENSOR", check_status=True)
+    torch.cuda.synchronize()
+    check(back(out), want, dtype)
+    np.testing.assert_array_equal(ok.cpu().numpy(), wk)
+    np.testing.assert_array_equal(ov.cpu().numpy(), wv)

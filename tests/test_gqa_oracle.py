@@ -28,7 +28,8 @@ def test_oracle_matches_reference_oracle(case):
         f["q"], f["k"] if case["new_seq"] else None, f["v"] if case["new_seq"] else None, f["pk"], f["pv"],
         f["lengths"], f["total"], num_heads=4, kv_num_heads=2, causal=case["causal"], window=case["window"],
         softcap=0.7 if case["composed"] else 0.0, sink=f.get("sink"), cos=f.get("cos"), sin=f.get("sin"),
-        position_ids=f.get("pos"), interleaved=case.get("interleaved", False), bias=f.get("bias"), qk_output=mode)
+        position_ids=f.get("pos"), interleaved=case.get("interleaved", False), bias=f.get("bias"), qk_output=mode,
+        k_scale=f.get("k_scale"), v_scale=f.get("v_scale"))
     out, pk, pv = res[:3]
     tol = 1e-5 if case["dtype"] == "float32" else 2e-3
     if mode:  # qk_output diagnostics
