@@ -82,7 +82,7 @@ struct AttnArgs {
   int v_head;      // value channels per head and output channels per head (head_size, or the
                    // LATENT v_head_size; LATENT values are read from the key rows)
   int decode_on;   // decode kernel enabled for this call (shape supported)
-  int decode_tile; // tokens per decode tile: kTile, or 2 * kTile for fp8 caches
+  int decode_tile; // tokens per decode tile: kTile, or kFp8HalfTiles * kTile for fp8 caches
   int prefill_tq;  // query tokens per prefill work item (2 x 128 rows / group) or 0 = prefill kernel off
 };
 
