@@ -323,6 +323,15 @@ typedef struct B200GqaParams {
   const float* k_scale;
   const float* v_scale;
   int32_t k_quant_per_channel, v_quant_per_channel;
+  /* sliding_window_cache=1 (attention.rs:1139-1379): a cache of capacity `cap` keeps
+   * resident(n) rows of a length-n sequence, n up to cap, otherwise n - gap * ceil((n - cap) /
+   * gap) with gap = cap - local_window_size + 1.  Batch row b (length = seqlens_k[b] + 1, past =
+   * length - seq) attends over its resident(past) past rows, which hold absolute positions
+   * past - resident(past) .., and its seq new rows, with the local window on absolute positions
+   * and attention_bias columns absolute; present (present_cap == cap, may equal past) then
+   * holds the last resident(length) rows of the sequence and zero rows (zero codes) after them.
+   * Requires new_seq == seq, 0 < local_window_size <= cap, present, qk_output 0. */
+  int32_t sliding_window_cache;
 } B200GqaParams;
 
 B200_API int b200_gqa_params_size(void);
@@ -338,7 +347,7 @@ B200_API int b200_group_query_attention(const B200GqaParams* p, void* stream);
 B200_API int b200_group_query_attention_read_status(const B200GqaParams* p, void* stream);
 
 /* Claim predicate, restating group_query_attention_claim (attention.rs:2407-2754) over a
- * plain node description, plus this build's own declines (sliding_window_cache, head size).  Returns 1 (claim) or 0
+ * plain node description, plus this build's own decline (head size).  Returns 1 (claim) or 0
  * (decline, reason written to `reason`). */
 typedef struct B200GqaNodeInfo {
   int32_t num_inputs;

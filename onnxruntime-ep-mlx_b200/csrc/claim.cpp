@@ -336,6 +336,12 @@ void gqa_claim(const GView& v) {
   if (sliding) {
     REQUIRE(window > 0, "sliding_window_cache=1 requires local_window_size > 0");
     REQUIRE(v.out_present(1) && v.out_present(2), "sliding_window_cache requires present key/value outputs");
+    const B200TensorInfo* pk = v.in(3);
+    const B200TensorInfo* pv = v.in(4);
+    REQUIRE(pk && pk->rank == 4 && pk->shape[2] >= window,
+            "sliding-window key cache capacity must be at least local_window_size");
+    REQUIRE(pv && pv->rank == 4 && pv->shape[2] >= window,
+            "sliding-window value cache capacity must be at least local_window_size");
   }
   const bool packed = v.in_present(0) && !v.in_present(1) && !v.in_present(2);
   REQUIRE(packed || (v.in_present(0) && v.in_present(1) && v.in_present(2)),
@@ -435,9 +441,9 @@ void gqa_claim(const GView& v) {
   REQUIRE(smooth >= -1 && smooth <= 1, "smooth_softmax must be -1 (schema default), 0 or 1");
   REQUIRE(n.qk_output >= 0 && n.qk_output <= 2 && (n.qk_output != 0) == v.out_present(3),
           "qk_output must be 0, 1 or 2 and enabled exactly when output_qk is present");
+  REQUIRE(!sliding || n.qk_output == 0, "sliding_window_cache with QK diagnostics is unsupported");
   REQUIRE(std::isfinite(n.softcap) && n.softcap >= 0.f, "softcap must be finite and non-negative");
   // Forms the reference accepts that this build does not implement (the node stays on ORT).
-  REQUIRE(!sliding, "sliding_window_cache is not implemented on B200");
   REQUIRE(head % 8 == 0 && head <= 256, "head_size must be a multiple of 8 up to 256 on B200, got %lld", (long long)head);
 }
 

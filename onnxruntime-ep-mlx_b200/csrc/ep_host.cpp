@@ -596,6 +596,7 @@ int b200_ep_node_compute_gqa(B200EpNode* n, const B200GqaParams* t, void* stream
     p.qk_output = (int32_t)a.qk_output;  // the tensors carry output_qk
     p.k_quant_per_channel = fixed_str(a.k_quant_type, sizeof a.k_quant_type) == "PER_CHANNEL";
     p.v_quant_per_channel = fixed_str(a.v_quant_type, sizeof a.v_quant_type) == "PER_CHANNEL";
+    p.sliding_window_cache = a.sliding_window_cache != 0;
     size_t need = 0;
     int rc = b200_group_query_attention_workspace_size(&p, &need);
     if (rc) return rc;

@@ -615,7 +615,7 @@ std::vector<T> host_values(const Bound& b, int32_t device) {
 
 // GroupQueryAttention (attention.rs:932-1454): inputs 0-15 as in B200GqaNodeInfo; outputs 0
 // ([batch, seq, num_heads * head_size]) and 1 / 2 (present caches [batch, kv_heads,
-// max(past capacity, total_sequence_length), head_size]).
+// max(past capacity, total_sequence_length), head_size]; the past capacity for a sliding cache).
 void ComputeInfo::run_gqa(OrtKernelContext* kctx, void* stream) {
   Bound in[16];
   for (size_t i = 0; i < 16; ++i) in[i] = input(kctx, i);
@@ -637,7 +637,8 @@ void ComputeInfo::run_gqa(OrtKernelContext* kctx, void* stream) {
   std::vector<int64_t> ids;
   if (in[9].present) ids = host_values<int64_t>(in[9], device);
   const int64_t cap = in[3].present ? in[3].dim(2) : 0;
-  const int64_t pcap = std::max<int64_t>(cap, total[0]);
+  // present: the past's capacity for a sliding cache (its rows move down), else room for total
+  const int64_t pcap = gqa.sliding_window_cache ? cap : std::max<int64_t>(cap, total[0]);
   // integer caches (kv_cache_bit_width): present rows keep the past's stored width
   const bool int_cache = in[3].present && (in[3].dtype == B200_DTYPE_INT8 || in[3].dtype == B200_DTYPE_UINT8);
   const int64_t width = int_cache ? in[3].dim(3) : D;

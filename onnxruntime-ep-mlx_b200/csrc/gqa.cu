@@ -65,6 +65,7 @@ struct GqaArgs {
   const float* kscale;                    // int caches: PER_TENSOR [1] or PER_CHANNEL [KV, D]
   const float* vscale;
   int kpc, vpc;                           // per-channel scales
+  int sliding, slide_gap;                 // sliding_window_cache=1; gap = cap - window + 1
   void* out;
   int row_tiles, splits, fused_copy, present_separate;
   float* part_o;   // [groups][splits][R][D]
@@ -121,15 +122,26 @@ template <typename T> __device__ __forceinline__ T ldg1(const T* p) {
   }
 }
 
-// Per batch row (:662-667): length, query_past, past (rows taken from the past cache).
+// Rows a sliding-window cache of capacity cap keeps of a length-n sequence (attention.rs:
+// 1173-1181): all of them up to the capacity, beyond it whole gaps reclaimed from the front.
+__host__ __device__ __forceinline__ int slide_resident(int n, int cap, int gap) {
+  return n <= cap ? n : n - gap * ((n - cap + gap - 1) / gap);
+}
+
+// Per batch row (:662-667): length, query_past, past (rows taken from the past cache) and
+// origin, the absolute position of past-cache row 0: 0, or for a sliding cache
+// past - resident(past) (:1186-1193), so key position pos < past is cache row pos - origin.
+// The visible keys of every query row start at or above the origin: resident(past) is past
+// itself up to the capacity and at least the window beyond it.
 struct BatchGeom {
-  int length, query_past, past;
+  int length, query_past, past, origin;
 };
 __device__ __forceinline__ BatchGeom batch_geom(const GqaArgs& a, int b) {
   BatchGeom g;
   g.length = a.seqlens[b] + 1;
   g.query_past = max(g.length - a.S, 0);
   g.past = a.new_seq == 0 ? g.length : g.query_past;
+  g.origin = a.sliding ? g.past - slide_resident(g.past, a.cap, a.slide_gap) : 0;
   return g;
 }
 
@@ -138,7 +150,7 @@ template <typename T>
 __device__ __forceinline__ const T* key_row(const GqaArgs& a, const BatchGeom& bg, int b, int kh, int pos, bool value) {
   if (pos < bg.past) {
     const T* base = static_cast<const T*>(value ? a.pv : a.pk);
-    return base + (((int64_t)b * a.KV + kh) * a.cap + pos) * a.D;
+    return base + (((int64_t)b * a.KV + kh) * a.cap + (pos - bg.origin)) * a.D;
   }
   const T* base = static_cast<const T*>(value ? a.v : a.k);
   const int64_t stride = value ? a.v_stride : a.k_stride;
@@ -236,7 +248,7 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
       float acc[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) acc[r] = 0.f;
-      if (pos < bg.length) {
+      if (pos < bg.length && pos >= bg.origin) {  // below the origin: not resident, never visible
         const T* krow = key_row<T>(a, bg, b, kh, pos, false);
         const bool copy = a.fused_copy && (a.present_separate || pos >= bg.past);
         T* kdst = copy ? present_row<T>(a, b, kh, pos, false) : nullptr;
@@ -319,7 +331,7 @@ __global__ void __launch_bounds__(kThreads) gqa_attention_kernel(const GqaArgs a
 #pragma unroll
         for (int u = 0; u < kGroup; ++u) {
           x0[u] = x1[u] = from_f<T>(0.f);
-          if (k0 + u < kend) {
+          if (k0 + u < kend && c * kKeys + k0 + u >= bg.origin) {
             const T* vrow = key_row<T>(a, bg, b, kh, c * kKeys + k0 + u, true);
             if (d0 < D) x0[u] = ldg1(vrow + d0);
             if (NC == 2 && d1 < D) x1[u] = ldg1(vrow + d1);
@@ -915,7 +927,8 @@ __device__ __forceinline__ float gqa_int_value(const GqaArgs& a, const BatchGeom
   const float scale = gqa_scale(a, value, kh, d);
   int code;
   if (pos < bg.past) {
-    const uint8_t* row = static_cast<const uint8_t*>(value ? a.pv : a.pk) + (((int64_t)b * a.KV + kh) * a.cap + pos) * a.cache_w;
+    const uint8_t* row =
+        static_cast<const uint8_t*>(value ? a.pv : a.pk) + (((int64_t)b * a.KV + kh) * a.cap + (pos - bg.origin)) * a.cache_w;
     if (a.cache_bits == 8) {
       code = (int)reinterpret_cast<const int8_t*>(row)[d];
     } else {
@@ -929,6 +942,19 @@ __device__ __forceinline__ float gqa_int_value(const GqaArgs& a, const BatchGeom
                     a.cache_bits);
   }
   return __fmul_rn((float)code, scale);
+}
+
+// Stored byte j of new row i (counted from the batch row's first new row) of kv head kh: an
+// int8 code, or two +8-biased int4 codes (channel 2j low, 2j + 1 high).
+template <typename T>
+__device__ __forceinline__ uint8_t gqa_new_code_byte(const GqaArgs& a, int side, int b, int kh, int i, int j) {
+  const T* x = static_cast<const T*>(side ? a.v : a.k) + ((int64_t)b * a.new_seq + i) * (side ? a.v_stride : a.k_stride) +
+               (int64_t)kh * a.D;
+  if (a.cache_bits == 8) return (uint8_t)(int8_t)gqa_code(to_f(x[j]), gqa_scale(a, side, kh, j), 8);
+  const int d0 = 2 * j, d1 = 2 * j + 1;
+  const int lo = gqa_code(to_f(x[d0]), gqa_scale(a, side, kh, d0), 4) + 8;
+  const int hi = d1 < a.D ? gqa_code(to_f(x[d1]), gqa_scale(a, side, kh, d1), 4) + 8 : 8;
+  return (uint8_t)(lo | (hi << 4));
 }
 
 // present rows of an integer cache: past rows copied (a separate present buffer), new rows
@@ -951,16 +977,7 @@ __global__ void __launch_bounds__(256) gqa_int_present_kernel(const GqaArgs a) {
     for (int j = threadIdx.x; j < a.cache_w; j += blockDim.x) {
       uint8_t byte = zero;
       if (is_new) {
-        const T* x = static_cast<const T*>(side ? a.v : a.k) +
-                     ((int64_t)b * a.new_seq + (r - bg.past)) * (side ? a.v_stride : a.k_stride) + (int64_t)kh * a.D;
-        if (a.cache_bits == 8) {
-          byte = (uint8_t)(int8_t)gqa_code(to_f(x[j]), gqa_scale(a, side, kh, j), 8);
-        } else {
-          const int d0 = 2 * j, d1 = 2 * j + 1;
-          const int lo = gqa_code(to_f(x[d0]), gqa_scale(a, side, kh, d0), 4) + 8;
-          const int hi = d1 < a.D ? gqa_code(to_f(x[d1]), gqa_scale(a, side, kh, d1), 4) + 8 : 8;
-          byte = (uint8_t)(lo | (hi << 4));
-        }
+        byte = gqa_new_code_byte<T>(a, side, b, kh, r - bg.past, j);
       } else if (r < a.cap) {
         byte = src[j];
       }
@@ -984,7 +1001,7 @@ __global__ void __launch_bounds__(128) gqa_int_attention_kernel(const GqaArgs a)
   const BatchGeom bg = batch_geom(a, b);
   const int pos = bg.query_past + s;
   const int end = a.causal ? min(pos + 1, bg.length) : bg.length;
-  const int start = a.window > 0 ? max(0, end - a.window) : 0;
+  const int start = max(a.window > 0 ? max(0, end - a.window) : 0, bg.origin);  // origin: see BatchGeom
   for (int d = threadIdx.x; d < 32 * EPL; d += blockDim.x)
     qs[d] = d < a.D ? to_f(static_cast<const T*>(a.q)[((int64_t)b * a.S + s) * a.q_stride + (int64_t)h * a.D + d]) : 0.f;
   __syncthreads();
@@ -1046,6 +1063,45 @@ __global__ void __launch_bounds__(128) gqa_int_attention_kernel(const GqaArgs a)
     for (int w = 0; w < kWarps; ++w) acc += red_o[w][d] * f[w];
     out[d] = from_f<T>(L > 0.f ? acc / L : 0.f);
   }
+}
+
+// present of a sliding cache (attention.rs:1341-1370): row r < after = resident(length) holds
+// absolute position length - after + r, a resident past row (moved down by the reclaimed rows)
+// or a new row (encoded for integer caches); rows from `after` on are zero (zero codes: 0, int4
+// 0x88).  Runs after the attention, which still reads the old rows, into dk / dv: present
+// itself, or workspace copies when present is the past buffer (rows move down, so an in-place
+// copy would overwrite rows other CTAs have yet to read).  One CTA per (batch, kv head, row).
+template <typename T>
+__global__ void __launch_bounds__(128) gqa_slide_present_kernel(const GqaArgs a, void* dk, void* dv) {
+  const int64_t row = blockIdx.x;  // (b * KV + kh) * cap + r
+  const int r = (int)(row % a.cap), kh = (int)((row / a.cap) % a.KV), b = (int)(row / ((int64_t)a.cap * a.KV));
+  const BatchGeom bg = batch_geom(a, b);
+  const int after = slide_resident(bg.length, a.cap, a.slide_gap);
+  const int pos = bg.length - after + r;  // absolute position held by row r < after
+  for (int side = 0; side < 2; ++side) {
+    if (a.cache_bits) {
+      uint8_t* dst = static_cast<uint8_t*>(side ? dv : dk) + row * a.cache_w;
+      const uint8_t zero = a.cache_bits == 8 ? 0 : 0x88;
+      const uint8_t* src = pos < bg.past ? static_cast<const uint8_t*>(side ? a.pv : a.pk) +
+                                               (((int64_t)b * a.KV + kh) * a.cap + (pos - bg.origin)) * a.cache_w
+                                         : nullptr;
+      for (int j = threadIdx.x; j < a.cache_w; j += blockDim.x) {
+        uint8_t byte = zero;
+        if (r < after) byte = src ? src[j] : gqa_new_code_byte<T>(a, side, b, kh, pos - bg.past, j);
+        dst[j] = byte;
+      }
+    } else {
+      T* dst = static_cast<T*>(side ? dv : dk) + row * a.D;
+      const T* src = r < after ? key_row<T>(a, bg, b, kh, pos, side == 1) : nullptr;
+      for (int d = threadIdx.x; d < a.D; d += blockDim.x) dst[d] = src ? src[d] : from_f<T>(0.f);
+    }
+  }
+}
+
+template <typename T>
+cudaError_t launch_slide_present(const GqaArgs& a, void* dk, void* dv, cudaStream_t stream) {
+  gqa_slide_present_kernel<T><<<(unsigned)((int64_t)a.B * a.KV * a.cap), 128, 0, stream>>>(a, dk, dv);
+  return cudaGetLastError();
 }
 
 template <typename T>
@@ -1158,8 +1214,16 @@ int sm_count(const B200GqaParams* p) {
 
 struct GqaPlan {
   int rows = kMaxRows, row_tiles = 1, splits = 1, fused = 0;
-  size_t status = 0, counters = 0, part_o = 0, part_ml = 0, q_rot = 0, k_rot = 0, total = 0;
+  size_t status = 0, counters = 0, part_o = 0, part_ml = 0, q_rot = 0, k_rot = 0, slide = 0, slide_bytes = 0,
+         total = 0;
 };
+
+// Bytes of one stored cache row: integer codes (int8: D, int4: ceil(D / 2)) or D activations.
+size_t cache_row_bytes(const B200GqaParams* p) {
+  if (p->cache_dtype == B200_DTYPE_INT8) return (size_t)p->head_size;
+  if (p->cache_dtype == B200_DTYPE_UINT8) return (size_t)(p->head_size + 1) / 2;
+  return (size_t)p->head_size * (p->dtype == B200_DTYPE_FLOAT ? 4 : 2);
+}
 
 size_t act_size(int dtype) { return dtype == B200_DTYPE_FLOAT ? 4 : 2; }
 
@@ -1190,6 +1254,10 @@ GqaPlan gqa_plan(const B200GqaParams* p) {
     P.counters = take(sizeof(int) * groups);
     P.part_o = take(sizeof(float) * groups * P.splits * P.rows * p->head_size);
     P.part_ml = take(sizeof(float) * groups * P.splits * P.rows * 2);
+  }
+  if (p->sliding_window_cache) {  // staged present K and V, for a present that is the past buffer
+    P.slide_bytes = (size_t)p->batch * p->kv_num_heads * std::max(p->cap, 0) * cache_row_bytes(p);
+    P.slide = take(2 * P.slide_bytes);
   }
   P.total = std::max<size_t>(off, 256);
   return P;
@@ -1257,14 +1325,49 @@ int check_gqa(const B200GqaParams* p) {
       gqa_rope_smem(p->num_heads, p->kv_num_heads, p->head_size) > 227 * 1024)
     return gfail(B200_ERR_UNSUPPORTED, "GroupQueryAttention: the query and key heads of one row exceed the prologue's "
                                        "shared memory");
-  // attention.rs:637-652
-  if (p->attention_bias &&
+  // attention.rs:637-652 (a sliding cache checks the bias with its own message, at run time)
+  if (p->attention_bias && !p->sliding_window_cache &&
       ((p->bias_batch != 1 && p->bias_batch != p->batch) || (p->bias_heads != 1 && p->bias_heads != p->num_heads) ||
        p->bias_seq != p->seq || p->bias_total != p->total_sequence_length))
     return gfail(B200_ERR_FAIL, "GroupQueryAttention: attention_bias must broadcast to [batch,heads,sequence,total]");
   // attention.rs:992-997
-  if (p->new_seq != p->seq && (p->new_seq != 0 || !p->past_key))
+  if (p->new_seq != p->seq && (p->new_seq != 0 || !p->past_key || p->sliding_window_cache))
     return gfail(B200_ERR_FAIL, "GroupQueryAttention: K/V must match Q sequence or be empty with paired non-sliding past");
+  if (p->sliding_window_cache) {  // attention.rs:2455-2475, :2735-2738
+    if (!p->present_key)
+      return gfail(B200_ERR_INVALID_ARGUMENT, "sliding_window_cache requires present key/value outputs");
+    if (p->qk_output)
+      return gfail(B200_ERR_UNSUPPORTED, "sliding_window_cache with QK diagnostics is unsupported");
+    if ((int64_t)p->batch * p->kv_num_heads * std::max(p->cap, 1) > INT32_MAX)
+      return gfail(B200_ERR_UNSUPPORTED, "GroupQueryAttention: sliding cache rows exceed one launch");
+  }
+  return B200_OK;
+}
+
+// Runtime checks of a sliding cache, in the reference's order and words (attention.rs:
+// 1140-1171): every length in [seq - 1, total - 1] with the maximum total - 1; a bias with
+// absolute [.., seq, total] columns; 0 < local_window_size <= capacity.  present keeps the
+// past's capacity (the reference's present is that buffer).
+int validate_sliding(const B200GqaParams* p) {
+  const int64_t total = p->total_sequence_length;
+  const int32_t* L = p->host_seqlens_k;
+  bool bad = total <= 0;
+  int64_t mx = -1;
+  for (int b = 0; b < p->batch; ++b) {
+    const int64_t n = L[b];
+    if (n < 0 || n >= total || n + 1 < p->seq) bad = true;
+    mx = std::max(mx, n);
+  }
+  if (bad || mx != total - 1) return gfail(B200_ERR_FAIL, "GroupQueryAttention: invalid sliding sequence lengths");
+  if (p->attention_bias &&
+      ((p->bias_batch != 1 && p->bias_batch != p->batch) || (p->bias_heads != 1 && p->bias_heads != p->num_heads) ||
+       p->bias_seq != p->seq || p->bias_total != total))
+    return gfail(B200_ERR_FAIL,
+                 "GroupQueryAttention: sliding attention_bias requires absolute total_sequence_length columns");
+  if (p->local_window_size <= 0 || p->cap < p->local_window_size)
+    return gfail(B200_ERR_FAIL, "GroupQueryAttention: sliding cache requires 0 < local_window_size <= capacity");
+  if (p->present_cap != p->cap)
+    return gfail(B200_ERR_INVALID_ARGUMENT, "GroupQueryAttention: a sliding present must have the past's capacity");
   return B200_OK;
 }
 
@@ -1515,7 +1618,7 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
   try {
     int rc = check_gqa(p);
     if (rc) return rc;
-    rc = validate_lengths(p);
+    rc = p->sliding_window_cache ? validate_sliding(p) : validate_lengths(p);
     if (rc) return rc;
     rc = validate_rotary(p);
     if (rc) return rc;
@@ -1570,6 +1673,10 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
       a.kpc = p->k_quant_per_channel != 0;
       a.vpc = p->v_quant_per_channel != 0;
     }
+    if (p->sliding_window_cache) {
+      a.sliding = 1;
+      a.slide_gap = p->cap - p->local_window_size + 1;
+    }
     char* ws = static_cast<char*>(p->workspace);
     a.status = reinterpret_cast<int*>(ws + P.status);
     if (P.splits > 1) {
@@ -1621,18 +1728,39 @@ int b200_group_query_attention(const B200GqaParams* p, void* stream_ptr) {
         a.k_stride = (int64_t)a.KV * a.D;
       }
     }
+    // A sliding cache's present is written after the attention (its rows move), so the
+    // attention launches see no present.
+    GqaArgs run = a;
+    if (a.sliding) {
+      run.ok = run.ov = nullptr;
+      run.fused_copy = 0;
+    }
     if (a.cache_bits) {  // integer caches: the codec kernels (a correctness path)
-      if (a.dtype == B200_DTYPE_FLOAT) e = launch_int<float>(a, stream, &launches);
-      else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_int<__half>(a, stream, &launches);
-      else e = launch_int<__nv_bfloat16>(a, stream, &launches);
+      if (a.dtype == B200_DTYPE_FLOAT) e = launch_int<float>(run, stream, &launches);
+      else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_int<__half>(run, stream, &launches);
+      else e = launch_int<__nv_bfloat16>(run, stream, &launches);
     } else {
       // Rows past some batch's length exist in present only when a length is below its capacity.
       bool tail_rows = false;
       for (int b = 0; b < p->batch; ++b) tail_rows |= p->host_seqlens_k[b] + 1 < a.pcap;
       const bool cluster = cluster_path(p, P);
-      if (a.dtype == B200_DTYPE_FLOAT) e = launch_gqa<float>(a, P, cluster, tail_rows, stream, &launches);
-      else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_gqa<__half>(a, P, cluster, tail_rows, stream, &launches);
-      else e = launch_gqa<__nv_bfloat16>(a, P, cluster, tail_rows, stream, &launches);
+      if (a.dtype == B200_DTYPE_FLOAT) e = launch_gqa<float>(run, P, cluster, tail_rows, stream, &launches);
+      else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_gqa<__half>(run, P, cluster, tail_rows, stream, &launches);
+      else e = launch_gqa<__nv_bfloat16>(run, P, cluster, tail_rows, stream, &launches);
+    }
+    if (e == cudaSuccess && a.sliding && a.cap > 0) {
+      const bool in_place = p->present_key == p->past_key || p->present_value == p->past_value ||
+                            p->present_key == p->past_value || p->present_value == p->past_key;
+      void* dk = in_place ? static_cast<void*>(ws + P.slide) : a.ok;
+      void* dv = in_place ? static_cast<void*>(ws + P.slide + P.slide_bytes) : a.ov;
+      if (a.dtype == B200_DTYPE_FLOAT) e = launch_slide_present<float>(a, dk, dv, stream);
+      else if (a.dtype == B200_DTYPE_FLOAT16) e = launch_slide_present<__half>(a, dk, dv, stream);
+      else e = launch_slide_present<__nv_bfloat16>(a, dk, dv, stream);
+      ++launches;
+      if (e == cudaSuccess && in_place) {
+        e = cudaMemcpyAsync(a.ok, dk, P.slide_bytes, cudaMemcpyDeviceToDevice, stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(a.ov, dv, P.slide_bytes, cudaMemcpyDeviceToDevice, stream);
+      }
     }
     add_launches(launches);
     if (e == cudaSuccess && p->qk_output) {  // diagnostics after the attention of the call

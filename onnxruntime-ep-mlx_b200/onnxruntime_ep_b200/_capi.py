@@ -102,7 +102,7 @@ class GqaParams(ctypes.Structure):
         ("bias_total", _i32), ("q_norm_weight", _vp), ("k_norm_weight", _vp), ("qk_norm_epsilon", _f32),
         ("qk_output", _i32), ("output_qk", _vp),
         ("cache_dtype", _i32), ("k_scale", _vp), ("v_scale", _vp), ("k_quant_per_channel", _i32),
-        ("v_quant_per_channel", _i32),
+        ("v_quant_per_channel", _i32), ("sliding_window_cache", _i32),
     ]
 
 

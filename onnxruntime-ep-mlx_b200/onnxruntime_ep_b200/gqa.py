@@ -9,7 +9,9 @@ rust/src/ops/attention.rs:932-1454, per-batch form :586-848, claim :2407-2754):
 
 ``present`` follows the reference's contracts: by default a new ``[B, KV, max(cap, total), D]``
 buffer (growing: past rows, then the new rows); passing ``present_key=past_key,
-present_value=past_value`` writes the new rows in place (shared buffer).  Errors raise
+present_value=past_value`` writes the new rows in place (shared buffer).
+``sliding_window_cache=1`` keeps the past's capacity and moves resident rows down as the
+window slides (attention.rs:1139-1379).  Errors raise
 ``B200Error`` with the reference's messages.  There is no CPU fallback.
 """
 
@@ -46,7 +48,7 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
                  do_rotary=0, rotary_interleaved=0, cos_cache=None, sin_cache=None, position_ids=None,
                  attention_bias=None, q_norm_weight=None, k_norm_weight=None, qk_norm_epsilon=1e-6,
                  qk_output=0, output_qk=None, k_scale=None, v_scale=None, k_quant_type="NONE",
-                 v_quant_type="NONE"):
+                 v_quant_type="NONE", sliding_window_cache=0):
     """Fill a ``B200GqaParams``.  Returns ``(params, keepalive, output, present_key, present_value)``.
 
     ``do_rotary=1`` takes ``cos_cache``/``sin_cache`` ``[positions, rotary_dim/2]`` (inputs 7 and
@@ -58,7 +60,9 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
     seq, total]`` (allocated when not given) with the visible logits / the probabilities.  int8 /
     uint8 (int4) ``past_key``/``past_value`` select the integer caches, with ``k_scale`` /
     ``v_scale`` fp32 (inputs 12 / 13) and ``k_quant_type`` / ``v_quant_type`` PER_TENSOR or
-    PER_CHANNEL; present is allocated in the same storage."""
+    PER_CHANNEL; present is allocated in the same storage.  ``sliding_window_cache=1`` keeps a
+    sliding-window cache of the past's capacity (present has ``cap`` rows: the last
+    ``resident(length)`` rows of each sequence, then zeros; it may be the past buffer)."""
     H, KV = int(num_heads), int(kv_num_heads)
     packed = key is None and value is None  # packed QKV in query (inputs 1 and 2 absent)
     B, S = int(query.shape[0]), int(query.shape[1])
@@ -77,7 +81,7 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
         host_seqlens_k = seqlens_k.detach().to("cpu", torch.int32).numpy()
     host_seqlens_k = np.ascontiguousarray(np.asarray(host_seqlens_k, dtype=np.int32))
     dev = query.device
-    pcap = max(cap, total)
+    pcap = cap if sliding_window_cache else max(cap, total)
     int_cache = past_key is not None and past_key.dtype in (torch.int8, torch.uint8)
     if with_present and present_key is None:
         if int_cache:
@@ -101,6 +105,7 @@ def build_params(query, key, value, past_key, past_value, seqlens_k, total_seque
     p.batch, p.seq, p.new_seq, p.cap = B, S, new_seq, cap
     p.present_cap = pcap if present_key is not None else 0
     p.total_sequence_length = total
+    p.sliding_window_cache = int(bool(sliding_window_cache))
     p.query = _ptr(query)
     if packed:
         row = (H + 2 * KV) * D

@@ -17,7 +17,15 @@ Semantics:
   ``cap * tanh(s / cap)``; a sink joins only the softmax denominator;
 * ``smooth_softmax == 1`` is a zero sink in every head (attention.rs:1311-1312);
 * rotary embedding of the new query / key rows before K joins present, positions as
-  gqa_rotary_rows (attention.rs:538-585) and the oracle's ``_rotate`` (:71-85).
+  gqa_rotary_rows (attention.rs:538-585) and the oracle's ``_rotate`` (:71-85);
+* ``sliding_window_cache=1`` (attention.rs:1139-1379; the reference's integer oracle
+  ``_gqa_ref(sliding=True)``, tests/ops/test_quantized_kv.py:122-193, and the inline expectation
+  of test_gqa_position_cache.py:427-488): a length-``n`` sequence keeps ``resident(n)`` cache
+  rows, ``n`` up to the capacity and otherwise ``n - gap * ceil((n - cap) / gap)`` with
+  ``gap = cap - window + 1``; the queries read the ``resident(past)`` cache rows (absolute
+  positions from ``past - resident(past)``) and the new rows, windowed on absolute positions,
+  bias columns absolute; present (capacity ``cap``) holds the last ``resident(length)`` rows of
+  the sequence, then zeros.
 
 Parity pinning: ``tests/golden/make_gqa_golden.py`` runs the reference's ``_reference`` on
 seeded inputs and commits its outputs (``gqa_golden.npz``); ``tests/test_gqa_oracle.py``
@@ -94,11 +102,21 @@ def rotary_positions(b, seq, query_past, total, position_ids):
     return ids[b * seq:(b + 1) * seq]
 
 
+def sliding_resident(length, cap, window):
+    """Cache rows a sliding-window cache of capacity ``cap`` keeps of a length-``length``
+    sequence (attention.rs:1173-1181): all of them up to the capacity; beyond it whole gaps of
+    ``cap - window + 1`` rows are reclaimed from the front."""
+    if length <= cap:
+        return length
+    gap = cap - window + 1
+    return length - gap * ((length - cap + gap - 1) // gap)
+
+
 def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_heads, kv_num_heads,
                           scale=None, causal=True, window=-1, softcap=0.0, sink=None,
                           smooth_softmax=-1, cos=None, sin=None, position_ids=None, interleaved=False,
                           out_dtype=None, bias=None, q_norm=None, k_norm=None, norm_eps=1e-6, qk_output=0,
-                          k_scale=None, v_scale=None):
+                          k_scale=None, v_scale=None, sliding=False):
     """Returns ``(output [B,S,H*D], present_k, present_v [B,KV,max(cap,total),D])``.
 
     ``q`` [B,S,H*D]; ``k``/``v`` [B,new_seq,KV*D] (new_seq may be 0); ``past_k``/``past_v``
@@ -111,7 +129,9 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
     (0 elsewhere) / the probabilities, zero from each row's length on (test_gqa_position_cache.py:
     130-131, attention.rs:771-787).  int8 / uint8 (int4) ``past_k``/``past_v`` hold integer codes
     with ``k_scale`` / ``v_scale`` ``[1]`` or ``[KV, D]``: present is in the same storage, new rows
-    are encoded, and the attention reads every row decoded (test_quantized_kv.py:122-193).  Arrays keep
+    are encoded, and the attention reads every row decoded (test_quantized_kv.py:122-193).
+    ``sliding`` is sliding_window_cache=1 (``window`` > 0, new rows present, present of the
+    past's capacity; ``qk_output`` 0), as ``sliding_resident`` describes.  Arrays keep
     their dtype; math is fp32, the output is rounded to the activation dtype (or kept in
     ``out_dtype``, e.g. fp32 for tolerance checks)."""
     B, S, hidden = q.shape
@@ -121,7 +141,9 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
     new_seq = 0 if k is None else k.shape[1]
     total = int(np.asarray(total).reshape(-1)[0])
     cap = 0 if past_k is None else past_k.shape[2]
-    pcap = max(cap, total)
+    pcap = cap if sliding else max(cap, total)
+    if sliding:
+        assert window > 0 and new_seq == S and past_k is not None and window <= cap and not qk_output
     dt = q.dtype
     scale = 1.0 / np.sqrt(D) if not scale else float(scale)
     bits = 0
@@ -144,7 +166,7 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
         query_past = max(length - S, 0)
         past = length if new_seq == 0 else query_past
         rows = 0 if new_seq == 0 else length - past
-        if past_k is not None:
+        if past_k is not None and not sliding:
             pk[b, :, :past] = past_k[b, :, :past]
             pv[b, :, :past] = past_v[b, :, :past]
             if length < cap:
@@ -161,36 +183,47 @@ def group_query_attention(q, k, v, past_k, past_v, seqlens_k, total, *, num_head
             qb = rotate(qb, cos, sin, ids, interleaved)
             if new_seq:
                 kb = rotate(kb, cos, sin, ids, interleaved)
-        if rows:
+        newk = newv = None
+        if rows:  # new rows in the cache's storage form
             vrows = v[b, :rows].reshape(rows, KV, D).transpose(1, 0, 2)
-            if bits:
-                pk[b, :, past:length] = int_encode(kb[:, :rows], ksc, bits)
-                pv[b, :, past:length] = int_encode(vrows, vsc, bits)
-            else:
-                pk[b, :, past:length] = kb[:, :rows]
-                pv[b, :, past:length] = vrows
-        if bits:
-            keys = np.repeat(int_decode(pk[b, :, :length], ksc, bits, D), g, 0)
-            vals = np.repeat(int_decode(pv[b, :, :length], vsc, bits, D), g, 0)
+            newk = int_encode(kb[:, :rows], ksc, bits) if bits else kb[:, :rows]
+            newv = int_encode(vrows, vsc, bits) if bits else vrows
+        if sliding:  # resident past rows ++ new rows; present keeps the last resident(length)
+            before, after = sliding_resident(past, cap, window), sliding_resident(length, cap, window)
+            origin = past - before
+            stored_k = np.concatenate([past_k[b, :, :before], newk.astype(past_k.dtype)], 1)
+            stored_v = np.concatenate([past_v[b, :, :before], newv.astype(past_v.dtype)], 1)
+            pk[b, :, :after] = stored_k[:, before + rows - after:]
+            pv[b, :, :after] = stored_v[:, before + rows - after:]
         else:
-            keys = np.repeat(pk[b, :, :length].astype(np.float32), g, 0)   # [H, length, D]
-            vals = np.repeat(pv[b, :, :length].astype(np.float32), g, 0)
+            origin = 0
+            if rows:
+                pk[b, :, past:length] = newk
+                pv[b, :, past:length] = newv
+            stored_k, stored_v = pk[b, :, :length], pv[b, :, :length]
+        n = stored_k.shape[1]  # keys at absolute positions origin .. origin + n - 1 (= length - 1)
+        if bits:
+            keys = np.repeat(int_decode(stored_k, ksc, bits, D), g, 0)
+            vals = np.repeat(int_decode(stored_v, vsc, bits, D), g, 0)
+        else:
+            keys = np.repeat(stored_k.astype(np.float32), g, 0)   # [H, n, D]
+            vals = np.repeat(stored_v.astype(np.float32), g, 0)
         qh = qb.astype(np.float32)  # [H, S, D]
         scores = qh @ keys.transpose(0, 2, 1) * np.float32(scale)
         if softcap > 0:
             scores = softcap * np.tanh(scores / softcap)
         if bias is not None:
-            scores = scores + np.asarray(bias)[0 if bias.shape[0] == 1 else b, :, :, :length].astype(np.float32)
+            scores = scores + np.asarray(bias)[0 if bias.shape[0] == 1 else b, :, :, origin:length].astype(np.float32)
         end = np.minimum(query_past + np.arange(S) + 1, length) if causal else np.full(S, length)
         start = np.maximum(0, end - window) if window > 0 else np.zeros(S, int)
-        cols = np.arange(length)[None]
+        cols = origin + np.arange(n)[None]
         visible = (cols >= start[:, None]) & (cols < end[:, None])
         logits = np.where(visible[None], scores, -np.inf)
         if sink is not None:
             s = np.asarray(sink, np.float32).reshape(H, 1, 1)
             logits = np.concatenate([logits, np.broadcast_to(s, (H, S, 1))], -1)
         e = np.exp(logits - logits.max(-1, keepdims=True))
-        probs = (e / e.sum(-1, keepdims=True))[..., :length]
+        probs = (e / e.sum(-1, keepdims=True))[..., :n]
         if qk_output:
             diag[b, :, :, :length] = np.where(visible[None], scores, 0) if qk_output == 1 else probs
         out[b] = (probs @ vals).transpose(1, 0, 2).reshape(S, H * D).astype(out.dtype)

@@ -12,8 +12,11 @@ the test module itself imports onnx helpers that are absent here.  Its geometry 
 4 q heads, 2 kv heads, head size 32, scale 1/sqrt(32); composed cases use softcap 0.7 and the
 feed ``sink``.  Inputs are seeded numpy (``default_rng(365 + case index)``) and stored with
 the outputs, so the fixtures are self-contained.  The oracle writes new rows into a copy of
-the past buffer, so every case has ``cap >= total`` (the growing contract, ``total > cap``,
-is covered by the GPU tests against ``oracle/gqa_ref.py``).
+the past buffer, so every non-sliding case has ``cap >= total`` (the growing contract,
+``total > cap``, is covered by the GPU tests against ``oracle/gqa_ref.py``).  Sliding-window
+cases (``sliding`` in the metadata) come from the reference's integer oracle ``_gqa_ref``
+(tests/ops/test_quantized_kv.py:122-193) and from the inline expectation of
+tests/ops/test_gqa_position_cache.py:427-488, restated in ``sliding_float_case``.
 """
 
 from __future__ import annotations
@@ -120,6 +123,101 @@ QK["int8_fp16_composed_probs"] = 2
 BIAS["int8_fp16_composed_probs"] = (1, HEADS)
 ROTARY["int4_rot_window"] = (16, False, [[1, 2, 3], [4, 5, 6]])
 
+# sliding_window_cache=1 over integer caches (test_quantized_kv.py:249-259 geometries: capacity 6,
+# window 3, lengths past the capacity, a chunk longer than the capacity): the reference's
+# _gqa_ref(sliding=True) gives the expected output and the present codes (capacity rows).
+SLIDING = {"int8_slide_decode", "int4_slide_chunk_rot", "int8_slide_seq_over_cap", "int4_slide_composed_bias"}
+INT.update({
+    "int8_slide_decode": (8, ("PER_CHANNEL", "PER_CHANNEL")),
+    "int4_slide_chunk_rot": (4, ("PER_TENSOR", "PER_CHANNEL")),
+    "int8_slide_seq_over_cap": (8, ("PER_TENSOR", "PER_TENSOR")),
+    "int4_slide_composed_bias": (4, ("PER_CHANNEL", "PER_TENSOR")),
+})
+CASES += [
+    ("int8_slide_decode", "float32", 2, 1, 1, 6, [8, 6], 8, True, 3, False),
+    ("int4_slide_chunk_rot", "float32", 1, 3, 3, 6, [9], 9, True, 3, False),
+    ("int8_slide_seq_over_cap", "float32", 1, 8, 8, 6, [12], 12, True, 3, False),
+    ("int4_slide_composed_bias", "float16", 2, 2, 2, 6, [9, 7], 9, True, 3, True),
+]
+ROTARY["int4_slide_chunk_rot"] = (16, False, [[6, 7, 8]])
+BIAS["int4_slide_composed_bias"] = (2, HEADS)
+
+# sliding_window_cache=1 over float caches: the inline expectation of
+# test_gqa_position_cache.py:422-488 (absolute bias columns, rotary with position ids, composed =
+# softcap 0.7 + sink), restated on seeded inputs.  name -> (dtype, batch, seq, cap, window,
+# broadcast bias, composed, step); step picks total from (max(seq, cap), cap + seq,
+# cap + seq + 1, max(seq, cap)) as the test's loop does, the second batch row one shorter.
+SLIDE_FLOAT = {
+    "slide_decode": ("float32", 1, 1, 4, 2, False, False, 1),
+    "slide_decode_fp16_composed": ("float16", 1, 1, 4, 2, True, True, 2),
+    "slide_batch_broadcast": ("float32", 2, 1, 4, 3, True, False, 2),
+    "slide_batch_composed": ("float32", 2, 1, 4, 3, False, True, 1),
+    "slide_chunk_composed": ("float32", 1, 3, 4, 2, False, True, 1),
+    "slide_chunk_fp16": ("float16", 1, 3, 4, 2, True, False, 2),
+    "slide_first_prompt": ("float32", 1, 5, 3, 2, False, False, 0),
+    "slide_long_chunk_composed": ("float32", 1, 5, 3, 2, True, True, 2),
+}
+
+
+def resident(length, cap, window):
+    gap = cap - window + 1
+    return length if length <= cap else length - gap * ((length - cap + gap - 1) // gap)
+
+
+def sliding_float_case(rotate, index, dtype, batch, seq, cap, window, broadcast, composed, step):
+    """Feeds and the expectation of test_gqa_position_cache.py:427-488 for one step."""
+    dt = np.dtype(dtype)
+    rng = np.random.default_rng(4365 + index)
+    total = (max(seq, cap), cap + seq, cap + seq + 1, max(seq, cap))[step]
+    lengths = np.full(batch, total, int)
+    if batch == 2:
+        lengths[1] -= 1
+    all_k = rng.normal(size=(batch, KV, 32, HEAD)).astype(dt)
+    all_v = rng.normal(size=all_k.shape).astype(dt)
+    feeds = dict(
+        q=rng.normal(size=(batch, seq, HEADS * HEAD)).astype(dt),
+        k=np.empty((batch, seq, KV * HEAD), dt), v=np.empty((batch, seq, KV * HEAD), dt),
+        pk=np.zeros((batch, KV, cap, HEAD), dt), pv=np.zeros((batch, KV, cap, HEAD), dt),
+        lengths=(lengths - 1).astype(np.int32), total=np.array([total], np.int32),
+        cos=rng.uniform(0.5, 1.5, (64, 16)).astype(dt), sin=rng.uniform(-0.5, 0.5, (64, 16)).astype(dt),
+        pos=np.tile(np.arange(seq, dtype=np.int64) + 3 + step, (batch, 1)),
+        bias=rng.uniform(-3, 3, (1 if broadcast else batch, 1 if broadcast else HEADS, seq, total)).astype(dt),
+    )
+    if composed:
+        feeds["sink"] = np.array([-1, 0, 1, 2], dt)
+    expected = np.empty_like(feeds["q"])
+    expected_k, expected_v = np.zeros_like(feeds["pk"]), np.zeros_like(feeds["pv"])
+    for b, length in enumerate(lengths):
+        past = length - seq
+        before, after = resident(past, cap, window), resident(length, cap, window)
+        feeds["pk"][b, :, :before] = all_k[b, :, past - before:past]
+        feeds["pv"][b, :, :before] = all_v[b, :, past - before:past]
+        feeds["k"][b] = all_k[b, :, past:length].transpose(1, 0, 2).reshape(seq, KV * HEAD)
+        feeds["v"][b] = all_v[b, :, past:length].transpose(1, 0, 2).reshape(seq, KV * HEAD)
+        ids = int(feeds["pos"].flat[0]) + np.arange(seq) if total == seq else feeds["pos"][b]
+        q = feeds["q"][b].reshape(seq, HEADS, HEAD).transpose(1, 0, 2)
+        q = rotate(q, feeds["cos"], feeds["sin"], ids, False).astype(np.float32)
+        keys = all_k[b, :, :length].copy()
+        keys[:, past:] = rotate(all_k[b, :, past:length], feeds["cos"], feeds["sin"], ids, False)
+        expected_k[b, :, :after] = keys[:, length - after:length]
+        expected_v[b, :, :after] = all_v[b, :, length - after:length]
+        keys = np.repeat(keys, HEADS // KV, 0).astype(np.float32)
+        vals = np.repeat(all_v[b, :, :length], HEADS // KV, 0).astype(np.float32)
+        scores = q @ keys.transpose(0, 2, 1) / np.sqrt(HEAD)
+        if composed:
+            scores = 0.7 * np.tanh(scores / 0.7)
+        scores += feeds["bias"][0 if broadcast else b, :, :, :length].astype(np.float32)
+        columns = np.arange(length)[None]
+        end = past + np.arange(seq) + 1
+        visible = (columns < end[:, None]) & (columns >= np.maximum(0, end - window)[:, None])
+        scores = np.where(visible[None], scores, -np.inf)
+        if composed:
+            scores = np.concatenate([scores, np.broadcast_to(feeds["sink"][:, None, None], (HEADS, seq, 1))], -1)
+        e = np.exp(scores - scores.max(-1, keepdims=True))
+        probs = (e / e.sum(-1, keepdims=True))[..., :length]
+        expected[b] = (probs @ vals).transpose(1, 0, 2).reshape(seq, HEADS * HEAD)
+    return feeds, expected, expected_k, expected_v, total
+
 
 def load_functions(path, names, extra=None):
     with open(path) as f:
@@ -195,7 +293,8 @@ def main():
                 feeds[f"{key}_scale"] = sc
                 shaped = sc.reshape(1, KV, 1, HEAD) if modes[side] == "PER_CHANNEL" else sc
                 feeds[f"p{key}"] = quant["_encode"](feeds[f"p{key}"], shaped, bits)
-            res = quant["_gqa_ref"](feeds, bits, causal=causal, window=window, composed=composed, mode=mode)
+            res = quant["_gqa_ref"](feeds, bits, causal=causal, window=window, composed=composed, mode=mode,
+                                    sliding=name in SLIDING)
         else:
             res = ref(feeds, causal=causal, window=window, composed=composed, interleaved=interleaved, mode=mode)
         out, pk, pv = res[:3]
@@ -210,7 +309,19 @@ def main():
                          total=total, causal=causal, window=window, composed=composed,
                          interleaved=bool(interleaved), mode=mode,
                          bits=INT[name][0] if name in INT else 0,
-                         quant_modes=list(INT[name][1]) if name in INT else None))
+                         quant_modes=list(INT[name][1]) if name in INT else None, sliding=name in SLIDING))
+    for j, (name, spec) in enumerate(SLIDE_FLOAT.items()):
+        dtype, batch, seq, cap, window, broadcast, composed, step = spec
+        feeds, out, pk, pv, total = sliding_float_case(gqa_ns["_rotate"], j, dtype, batch, seq, cap, window,
+                                                       broadcast, composed, step)
+        for key, val in feeds.items():
+            arrays[f"{name}/in/{key}"] = val
+        arrays[f"{name}/out/output"] = out
+        arrays[f"{name}/out/present_k"] = pk
+        arrays[f"{name}/out/present_v"] = pv
+        meta.append(dict(name=name, dtype=dtype, batch=batch, seq=seq, new_seq=seq, cap=cap, total=total,
+                         causal=True, window=window, composed=composed, interleaved=False, mode=0, bits=0,
+                         quant_modes=None, sliding=True))
     # q/k RMS norm inputs 14 / 15 (tests/ops/test_gqa11.py:52-130): the test's seeded inputs and
     # its own expectation, restated (fp32, head 8, past 2, three new rows, eps 1e-5).
     b, sq, past, nh, kvh, head = 1, 3, 2, 4, 2, 8

@@ -270,3 +270,49 @@ def test_latent_node_through_the_glue(ep):
     finally:
         ctx.close()
         g.close()
+
+
+def test_sliding_gqa_node_through_the_glue(ep):
+    """A sliding_window_cache GroupQueryAttention node: present is requested at the past's
+    capacity and holds the resident rows (attention.rs:1139-1379); lengths past the capacity."""
+    Hg, KVg, Dg, cap, window = 8, 2, 64, 64, 32
+    rng = np.random.default_rng(17)
+    lens = np.array([199, 49], np.int32)
+    total = np.array([200], np.int32)
+    qn = rng.standard_normal((2, 1, Hg * Dg), np.float32)
+    kn = rng.standard_normal((2, 1, KVg * Dg), np.float32)
+    vn = rng.standard_normal((2, 1, KVg * Dg), np.float32)
+    pkn = rng.standard_normal((2, KVg, cap, Dg), np.float32)
+    pvn = rng.standard_normal((2, KVg, cap, Dg), np.float32)
+    want, wk, wv = gqa_ref.group_query_attention(qn, kn, vn, pkn, pvn, lens, total, num_heads=Hg, kv_num_heads=KVg,
+                                                 window=window, sliding=True)
+    g = oh.Graph()
+    ctx = oh.KernelContext()
+    try:
+        oh.gqa_node(g, "sw", H=Hg, KV=KVg, d=Dg, dt=oh.F32, B=2, S=1, cap=cap,
+                    attrs=dict(sliding_window_cache=1, local_window_size=window))
+        rc, claimed, _ = ep.capability(g)
+        assert rc == 0 and claimed == [0], ep.report()
+        idx = ep.compile(g, 0)
+        assert idx >= 0, oh.last_error()
+        dev = {k: to_dev(v) for k, v in dict(query=qn, key=kn, value=vn, past_key=pkn, past_value=pvn).items()}
+        for k, v in dev.items():
+            _bind(ctx, f"sw.{k}", v, oh.F32)
+        meta = dict(seqlens_k=lens.copy(), total=total.copy())  # kept alive until Compute has run
+        for k, v in meta.items():
+            _bind(ctx, f"sw.{k}", v, oh.I32)
+        out = torch.empty((2, 1, Hg * Dg), device="cuda")
+        pk = torch.empty((2, KVg, cap, Dg), device="cuda")
+        pv = torch.empty_like(pk)
+        ctx.output("sw.out", oh.F32, (2, 1, Hg * Dg), out.data_ptr(), out.numel() * 4)
+        ctx.output("sw.present_key", oh.F32, (2, KVg, cap, Dg), pk.data_ptr(), pk.numel() * 4)
+        ctx.output("sw.present_value", oh.F32, (2, KVg, cap, Dg), pv.data_ptr(), pv.numel() * 4)
+        rc = ep.compute(idx, ctx)
+        assert rc == 0, oh.last_error()
+        assert ctx.requested("sw.present_key") == (2, KVg, cap, Dg)
+        got = out.cpu().numpy()
+        assert float(np.abs(got - want).max()) <= 2e-5 + 2e-5 * float(np.abs(want).max())
+        assert np.array_equal(pk.cpu().numpy(), wk) and np.array_equal(pv.cpu().numpy(), wv)
+    finally:
+        ctx.close()
+        g.close()

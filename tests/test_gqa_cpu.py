@@ -181,15 +181,53 @@ def test_attention_bias_is_claimed():
     assert ok == 0 and "input 10 must have output dtype" in why
 
 
+def _sliding(window=64):
+    def f(n):
+        n.sliding_window_cache = 1
+        if window is not None:
+            _set("local_window_size", window)(n)
+    return f
+
+
+@pytest.mark.parametrize("bits", [0, 8, 4])
+def test_sliding_window_cache_is_claimed(bits):
+    n = int_gnode(bits) if bits else gnode()
+    _sliding()(n)
+    assert claim(n) == (1, "")
+
+
+# attention.rs:2455-2475, :2588-2591, :2735-2738
 @pytest.mark.parametrize("mutate,reason", [
-    (lambda n: (setattr(n, "sliding_window_cache", 1), _set("local_window_size", 64)(n)),
-     "sliding_window_cache is not implemented on B200"),
+    (_sliding(None), "sliding_window_cache=1 requires local_window_size > 0"),
+    (lambda n: (_sliding()(n), setattr(n, "num_outputs", 1)), "sliding_window_cache requires present key/value outputs"),
+    (_sliding(4096), "sliding-window key cache capacity must be at least local_window_size"),
+    (lambda n: (_sliding()(n), tensor(n.inputs[4], F32, [1, 8, 32, 128])),
+     "sliding-window value cache capacity must be at least local_window_size"),
+    (lambda n: (_sliding()(n), setattr(n, "qk_output", 1), setattr(n, "num_outputs", 4),
+                tensor(n.outputs[3], F32, [1, 32, 1, -1])),
+     "sliding_window_cache with QK diagnostics is unsupported"),
 ])
-def test_b200_declines(mutate, reason):
+def test_sliding_window_cache_rules(mutate, reason):
     n = gnode()
     mutate(n)
     ok, why = claim(n)
-    assert ok == 0 and why.startswith(reason), why
+    assert ok == 0 and reason in why, why
+
+
+def test_sliding_integer_rows_alignment():
+    n = gnode(D=40, n_inputs=14)  # int8 rows of 40 channels: not a multiple of 16
+    for i in (3, 4):
+        tensor(n.inputs[i], I8, [1, 8, 2048, 40])
+    for i in (1, 2):
+        tensor(n.outputs[i], I8, [1, 8, -1, 40])
+    n.kv_cache_bit_width = 8
+    n.k_quant_type = n.v_quant_type = b"PER_TENSOR"
+    for i in (12, 13):
+        tensor(n.inputs[i], F32, [1])
+    assert claim(n) == (1, "")
+    _sliding()(n)
+    ok, why = claim(n)
+    assert ok == 0 and "sliding integer cache rows must satisfy pinned 16-byte alignment" in why, why
 
 
 def params(lengths, total, S=1, new_seq=1, cap=2048, B=None, causal=1, window=-1, present_cap=None):
@@ -225,6 +263,64 @@ def test_length_validation_messages(lengths, total, S, new_seq, cap, message):
     rc = _capi.LIB.b200_group_query_attention(ctypes.byref(p), None)
     assert rc == _capi.B200_ERR_FAIL
     assert _capi.LIB.b200_last_error().decode() == message
+
+
+def sliding_params(lengths, total, S=1, cap=16, window=4, present_cap=None):
+    p, keep = params(lengths, total, S=S, new_seq=S, cap=cap, window=window,
+                     present_cap=cap if present_cap is None else present_cap)
+    p.sliding_window_cache = 1
+    return p, keep
+
+
+# attention.rs:1140-1171 (lengths, bias columns, window / capacity), in that order
+@pytest.mark.parametrize("lengths,total,S,cap,window,message", [
+    ([3, 9], 9, 1, 16, 4, "GroupQueryAttention: invalid sliding sequence lengths"),
+    ([3, 7], 9, 1, 16, 4, "GroupQueryAttention: invalid sliding sequence lengths"),
+    ([1, 8], 9, 3, 16, 4, "GroupQueryAttention: invalid sliding sequence lengths"),
+    ([40], 41, 1, 16, 17, "GroupQueryAttention: sliding cache requires 0 < local_window_size <= capacity"),
+])
+def test_sliding_validation_messages(lengths, total, S, cap, window, message):
+    p, keep = sliding_params(lengths, total, S=S, cap=cap, window=window)
+    assert _capi.LIB.b200_group_query_attention(ctypes.byref(p), None) == _capi.B200_ERR_FAIL
+    assert _capi.LIB.b200_last_error().decode() == message
+
+
+def test_sliding_bias_needs_absolute_columns():
+    p, keep = sliding_params([40], 41)
+    p.attention_bias = ctypes.c_void_p(0x4000)
+    p.bias_batch, p.bias_heads, p.bias_seq, p.bias_total = 1, 1, 1, 16  # the cache's columns
+    assert _capi.LIB.b200_group_query_attention(ctypes.byref(p), None) == _capi.B200_ERR_FAIL
+    assert _capi.LIB.b200_last_error().decode() == (
+        "GroupQueryAttention: sliding attention_bias requires absolute total_sequence_length columns")
+
+
+def test_sliding_contract_errors():
+    p, keep = sliding_params([40], 41, present_cap=41)
+    assert _capi.LIB.b200_group_query_attention(ctypes.byref(p), None) == _capi.B200_ERR_INVALID_ARGUMENT
+    assert "a sliding present must have the past's capacity" in _capi.LIB.b200_last_error().decode()
+    p, keep = sliding_params([40], 41)
+    p.new_seq = 0
+    assert _capi.LIB.b200_group_query_attention(ctypes.byref(p), None) == _capi.B200_ERR_FAIL
+    assert _capi.LIB.b200_last_error().decode() == (
+        "GroupQueryAttention: K/V must match Q sequence or be empty with paired non-sliding past")
+    p, keep = sliding_params([40], 41)
+    p.qk_output, p.output_qk = 1, ctypes.c_void_p(0x5000)
+    assert _capi.LIB.b200_group_query_attention(ctypes.byref(p), None) == _capi.B200_ERR_UNSUPPORTED
+    assert _capi.LIB.b200_last_error().decode() == "sliding_window_cache with QK diagnostics is unsupported"
+    p, keep = sliding_params([40], 41)
+    p.present_key = p.present_value = None
+    assert _capi.LIB.b200_group_query_attention(ctypes.byref(p), None) == _capi.B200_ERR_INVALID_ARGUMENT
+    assert _capi.LIB.b200_last_error().decode() == "sliding_window_cache requires present key/value outputs"
+
+
+def test_sliding_workspace_holds_staged_present():
+    p, keep = sliding_params([40], 41, cap=16)
+    n0, n1 = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    assert _capi.LIB.b200_group_query_attention_workspace_size(ctypes.byref(p), ctypes.byref(n1)) == 0
+    p.sliding_window_cache = 0
+    p.present_cap = 41
+    assert _capi.LIB.b200_group_query_attention_workspace_size(ctypes.byref(p), ctypes.byref(n0)) == 0
+    assert n1.value - n0.value >= 2 * 1 * 8 * 16 * 128 * 4  # K and V rows of the capacity, fp32
 
 
 def test_new_rows_must_match_query_sequence():

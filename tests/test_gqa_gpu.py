@@ -76,6 +76,8 @@ def test_golden_cases(case, in_place):
     if case.get("bits"):  # integer caches: codes in pk / pv, scales (inputs 12 / 13)
         kw.update(k_scale=dev(f["k_scale"]), v_scale=dev(f["v_scale"]), k_quant_type=case["quant_modes"][0],
                   v_quant_type=case["quant_modes"][1])
+    if case.get("sliding"):  # sliding_window_cache=1: present keeps the past's capacity
+        kw["sliding_window_cache"] = 1
     mode = case.get("mode", 0)
     res = gqa.group_query_attention(q, k, v, pk, pv, lengths, int(f["total"][0]), sink, check_status=True,
                                     qk_output=mode, **kw)
@@ -90,7 +92,7 @@ def test_golden_cases(case, in_place):
 
 def run_case(rng, *, dtype="bfloat16", B=1, S=1, H=32, KV=8, D=128, cap=2048, lengths=None, total=None,
              causal=1, window=-1, softcap=0.0, sink=False, smooth=-1, packed=False, new_rows=True, past=True,
-             in_place=False, rotary=None, bias=None, qk_norm=False):
+             in_place=False, rotary=None, bias=None, qk_norm=False, sliding=False):
     npdt = np.float32
     lengths = [cap + S] * B if lengths is None else lengths
     B = len(lengths)
@@ -146,11 +148,11 @@ def run_case(rng, *, dtype="bfloat16", B=1, S=1, H=32, KV=8, D=128, cap=2048, le
     want, wk, wv = gqa_ref.group_query_attention(
         qn, kn if new_rows else None, vn if new_rows else None, pkr, pvr, np.asarray(lengths) - 1, total,
         num_heads=H, kv_num_heads=KV, causal=bool(causal), window=window, softcap=softcap, sink=skr,
-        smooth_softmax=smooth, out_dtype=np.float32, bias=bias_n, **rot, **norm_n)
+        smooth_softmax=smooth, out_dtype=np.float32, bias=bias_n, sliding=sliding, **rot, **norm_n)
     want, wk, wv = (np.asarray(x, np.float32) for x in (want, wk, wv))
     lens = torch.tensor(np.asarray(lengths) - 1, dtype=torch.int32, device=DEV)
     kw = dict(num_heads=H, kv_num_heads=KV, causal=causal, local_window_size=window, softcap=softcap,
-              smooth_softmax=smooth, attention_bias=bias_t, **kw_rot, **norm_t)
+              smooth_softmax=smooth, attention_bias=bias_t, sliding_window_cache=int(sliding), **kw_rot, **norm_t)
     if in_place:
         kw.update(present_key=pkt, present_value=pvt)
     if packed:
@@ -298,6 +300,10 @@ def test_qk_norm_prefill_rows():
 def test_integer_caches(bits, dtype, S, lengths, cap):
     """Config-1 geometry (and a ragged prefill batch) with int8 / int4 caches: present codes
     bit-exact, attention within the fp32 tolerance of the decoded-cache oracle."""
+    run_int(bits, dtype, S, lengths, cap)
+
+
+def run_int(bits, dtype, S, lengths, cap, window=-1, sliding=False, in_place=False):
     rng = np.random.default_rng(50 + bits + S)
     H, KV, D = 32, 8, 128
     B = len(lengths)
@@ -318,13 +324,57 @@ def test_integer_caches(bits, dtype, S, lengths, cap):
         qn, kn, vn = (a.astype(ml_dtypes.bfloat16) for a in (qn, kn, vn))
     lens = np.asarray(lengths) - 1
     want, wk, wv = gqa_ref.group_query_attention(qn, kn, vn, pk, pv, lens, total, num_heads=H, kv_num_heads=KV,
-                                                 out_dtype=np.float32, k_scale=ks, v_scale=vs)
+                                                 out_dtype=np.float32, k_scale=ks, v_scale=vs, window=window,
+                                                 sliding=sliding)
+    pkt, pvt = torch.from_numpy(pk).to(DEV), torch.from_numpy(pv).to(DEV)
+    extra = dict(present_key=pkt, present_value=pvt) if in_place else {}
     out, ok, ov = gqa.group_query_attention(
-        q, k, v, torch.from_numpy(pk).to(DEV), torch.from_numpy(pv).to(DEV),
-        torch.tensor(lens, dtype=torch.int32, device=DEV), total, num_heads=H, kv_num_heads=KV,
+        q, k, v, pkt, pvt, torch.tensor(lens, dtype=torch.int32, device=DEV), total, num_heads=H, kv_num_heads=KV,
         k_scale=torch.from_numpy(ks).to(DEV), v_scale=torch.from_numpy(vs).to(DEV), k_quant_type="PER_CHANNEL",
-        v_quant_type="PER_TENSOR", check_status=True)
+        v_quant_type="PER_TENSOR", local_window_size=window, sliding_window_cache=int(sliding), check_status=True,
+        **extra)
     torch.cuda.synchronize()
     check(back(out), want, dtype)
     np.testing.assert_array_equal(ok.cpu().numpy(), wk)
     np.testing.assert_array_equal(ov.cpu().numpy(), wv)
+
+
+# ---- sliding_window_cache=1 (attention.rs:1139-1379) -------------------------------------------
+# The cache keeps resident(n) rows of a length-n sequence (whole gaps of cap - window + 1 rows
+# reclaimed from the front past the capacity); present (the past's capacity, or the past buffer
+# itself) holds the last resident(length) rows, then zeros.  Output within the fp32 tolerance of
+# the oracle, present bit-exact over all capacity rows.
+@pytest.mark.parametrize("in_place", [False, True])
+@pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
+def test_sliding_decode(dtype, in_place):
+    """32q/8kv, d128, a 256-row cache with a 128-token window: two lengths past the capacity
+    (rows reclaimed and moved down), one below it."""
+    run_case(np.random.default_rng(60), dtype=dtype, cap=256, window=128, lengths=[1000, 300, 200],
+             sliding=True, in_place=in_place)
+
+
+@pytest.mark.parametrize("S,lengths", [(8, [700, 410]), (100, [700, 100]), (300, [700, 300])])
+def test_sliding_chunks(S, lengths):
+    """Chunks of 8 rows, longer than the window, and longer than the capacity (the rows a chunk
+    drops are still read by its first queries)."""
+    run_case(np.random.default_rng(61 + S), dtype="bfloat16", S=S, H=8, KV=2, cap=128, window=64, lengths=lengths,
+             sliding=True, in_place=True)
+
+
+def test_sliding_window_equals_capacity():
+    """gap 1: every row past the capacity reclaims one."""
+    run_case(np.random.default_rng(62), dtype="float16", S=2, H=8, KV=2, cap=64, window=64, lengths=[200, 65, 64],
+             sliding=True)
+
+
+def test_sliding_rotary_bias_composed():
+    """Rotary at absolute positions, absolute bias columns, softcap and sink together."""
+    run_case(np.random.default_rng(63), dtype="float16", S=3, H=16, KV=4, cap=96, window=40, lengths=[500, 97, 60],
+             sliding=True, rotary=(64, False, None), bias=(3, 16), softcap=30.0, sink=True, in_place=True)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("in_place", [False, True])
+def test_sliding_integer_caches(bits, in_place):
+    """int8 / int4 sliding caches: resident codes moved, new rows encoded, zero codes after."""
+    run_int(bits, "bfloat16", 4, [700, 300, 130], 256, window=100, sliding=True, in_place=in_place)

@@ -1,6 +1,7 @@
 """oracle/gqa_ref.py against the reference's own GroupQueryAttention oracle
-(tests/ops/test_gqa_position_cache.py:88-134, rotary :71-85, attention_bias :119-121), fixtures in
-tests/golden/gqa_golden.npz."""
+(tests/ops/test_gqa_position_cache.py:88-134, rotary :71-85, attention_bias :119-121), its integer
+oracle (tests/ops/test_quantized_kv.py:122-193, sliding caches included) and the sliding-cache
+expectation of test_gqa_position_cache.py:427-488, fixtures in tests/golden/gqa_golden.npz."""
 
 import json
 import os
@@ -29,7 +30,7 @@ def test_oracle_matches_reference_oracle(case):
         f["lengths"], f["total"], num_heads=4, kv_num_heads=2, causal=case["causal"], window=case["window"],
         softcap=0.7 if case["composed"] else 0.0, sink=f.get("sink"), cos=f.get("cos"), sin=f.get("sin"),
         position_ids=f.get("pos"), interleaved=case.get("interleaved", False), bias=f.get("bias"), qk_output=mode,
-        k_scale=f.get("k_scale"), v_scale=f.get("v_scale"))
+        k_scale=f.get("k_scale"), v_scale=f.get("v_scale"), sliding=case.get("sliding", False))
     out, pk, pv = res[:3]
     tol = 1e-5 if case["dtype"] == "float32" else 2e-3
     if mode:  # qk_output diagnostics
