@@ -25,7 +25,9 @@
 //      - warpgroups 0 and 1 (softmax and epilogue of q tile 0 / 1, one row per thread =
 //        tensor-memory lane): exp2-domain softmax with a lazily rescaled running max (O is
 //        rescaled in tensor memory only when the max grows by more than 2^8); P goes back over
-//        the S columns as a hi + lo pair of 16-bit values (~16 mantissa bits); the epilogue
+//        the S columns: fp16 P (11 significant bits, one P . V MMA per 16 keys) for fp16
+//        activations; for bf16 a hi + lo pair of bf16 values (~16 bits, two MMAs), since one
+//        bf16 P (8 bits) costs up to ~3e-3 on unit-scale data; the epilogue
 //        normalises (sink) and stores the rows;
 //  * tensor memory: S0/P0 columns [0,128), S1/P1 [128,256), O0 [256,384), O1 [384,512);
 //  * registers: warpgroups 0-1 grow to 200 per thread and warpgroup 2 shrinks to 96
@@ -145,6 +147,36 @@ __device__ __forceinline__ Item decode_item(const AttnArgs& a, const DecodePlan&
 // local memory)
 __device__ __forceinline__ int nkv_of(const Item& m, int w) { return w ? m.nkv[1] : m.nkv[0]; }
 
+// Rows of K/V tile j that hold the sequence's keys; fewer than kBN only for an item's last tile
+// (earlier tiles end below kv_hi <= total).
+__device__ __forceinline__ int tile_rows(const Item& m, int j) { return min(kBN, m.total - (m.kv_lo + j * kBN)); }
+
+// Page `page` of a V stage (16 rows of both 64-channel boxes) by plain loads: rows [0, rows)
+// from the cache (block `blk`, slots from position `pos0`), the rest zero.  The stores follow the
+// TMA's 128B swizzle (16-byte piece c of row r at piece c ^ (r & 7); the stage is 1024-byte
+// aligned), and a proxy fence orders them before the tensor core's reads.  A whole warp; `blk`
+// out of range (already reported by the caller) fills zeros.  Out of line: it runs once per
+// sequence end at most, and the producer's loop stays small.
+__device__ __noinline__ void fill_tail_page(uint8_t* stage, const AttnArgs& a, int32_t blk, int pos0, int kh, int page,
+                                            int rows, int lane) {
+  const bool blk_ok = blk >= 0 && blk < a.num_blocks;
+  const int D = a.head_size;
+  const int64_t slot0 = (int64_t)blk * a.block_size + pos0 % a.block_size;
+  for (int i = lane; i < kTile * 16; i += 32) {  // i = row (16) x box (2) x 16-byte piece (8)
+    const int r = i >> 4, box = (i >> 3) & 1, piece = i & 7;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < rows && blk_ok) {
+      const uint8_t* src = static_cast<const uint8_t*>(a.value_cache) +
+                           (((slot0 + r) * a.kv_heads + kh) * D + box * 64) * 2 + piece * 16;
+      v = *reinterpret_cast<const uint4*>(src);
+    }
+    const int row = page * kTile + r;
+    *reinterpret_cast<uint4*>(stage + box * kBoxBytes + row * 128 + ((piece ^ (row & 7)) * 16)) = v;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+}
+
 }  // namespace
 
 bool prefill_supported(int head_size, int block_size, int group, int act_dtype, int cache_dtype) {
@@ -220,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   auto drain_idx = [&](uint64_t* bar, uint32_t index) { mbar_wait(bar, index & 1u); };
 
   if (warp >= 2 * (kWgThreads / 32)) {
-    // warpgroup 2: producer, MMA issuer and two idle warps give registers to the softmax
+    // warpgroup 2: producers, MMA issuer and an idle warp give registers to the softmax
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));
     if (warp == kProducerWarp || warp == kVProducerWarp) {
       // ------------------------------------------------------------------ TMA producers
@@ -269,9 +301,20 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           const int z = blk_ok ? blk * a.block_size + pos0 % a.block_size : (int)oob_z;
           const int st = (int)(c % (uint32_t)stages);
           if (c >= (uint32_t)stages && !(ok = wait_warp(&empty_bar[st], c / stages - 1))) break;
-          if (lane == 0) mbar_arrive_expect_tx(&full_bar[st], kTileBytes);
+          // A V page that reaches past the sequence's last key (rows `rows` of 16 are the
+          // sequence's): its rows come by plain loads and its unused slots are zeroed, since
+          // whatever they hold, NaN included, must not meet P = 0 in the MMA.  Pages wholly past
+          // the end load zero-filled by TMA.
+          const int rows = is_v ? tile_rows(m, j) & (kTile - 1) : 0;
+          const int tail_page = tile_rows(m, j) >> 4;
+          if (rows) {
+            const int32_t tblk = __shfl_sync(0xffffffffu, blk, 2 * tail_page);
+            const int tpos = __shfl_sync(0xffffffffu, pos0, 2 * tail_page);
+            fill_tail_page(smem + kSmemV + st * kTileBytes, a, tblk, tpos, m.kh, tail_page, rows, lane);
+          }
+          if (lane == 0) mbar_arrive_expect_tx(&full_bar[st], rows ? kTileBytes - kTile * 256 : kTileBytes);
           __syncwarp();
-          if (loader)
+          if (loader && !(rows && page == tail_page))
             tma_load_3d(smem + (ring - sbase) + st * kTileBytes + half * kBoxBytes + page * (kTile * 128), map,
                         &full_bar[st], half * 64, m.kh, z);
           if (lane == 0) PF_TRACE(c * 16 + (is_v ? 13 : 12));
@@ -315,11 +358,12 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
 #pragma unroll
               for (int kk = 0; kk < kBN / 16; ++kk) {
                 const uint64_t vdesc = vdesc0 + (uint64_t)(kk * (2048 >> 4));
-                // P of keys 16kk..16kk+15: hi at chunk kk/2's columns (kk%2)*8.., lo 16 columns on
+                // P of keys 16kk..16kk+15 at chunk kk/2's columns (kk%2)*8..; bf16: the lo halves
+                // 16 columns on
                 const uint32_t pcol = pbuf + (kk >> 1) * 32 + (kk & 1) * 8;
                 if (leader) {
                   tc::mma_ts(obuf, pcol, vdesc, kIdPV, (j > 1 || kk > 0) ? 1u : 0u);
-                  tc::mma_ts(obuf, pcol + 16, vdesc, kIdPV, 1u);
+                  if (kBF16) tc::mma_ts(obuf, pcol + 16, vdesc, kIdPV, 1u);
                 }
               }
               if (leader && j == nkv_of(m, w)) tc::commit(&bars.o_done[w]);  // the item's last P . V
@@ -464,8 +508,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           }
           tc::wait_st();
         }
-        // P = 2^(s * kscale - mu) as hi + lo 16-bit halves, per 32-column chunk of S: hi over the
-        // chunk's first 16 columns, lo over its last 16 (each chunk is read before it is overwritten)
+        // P = 2^(s * kscale - mu) per 32-column chunk of S, over the chunk's first 16 columns (fp16,
+        // or bf16 hi halves with the lo halves over its last 16; each chunk is read before it is
+        // overwritten)
         const float mu = m_run == -INFINITY ? 0.f : m_run;
         const float kscale = raw ? qk_scale : 1.0f;
         const float2 ks2 = make_float2(kscale, kscale), nmu2 = make_float2(-mu, -mu);
@@ -479,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
             const float2 p = (kPolyEvery > 0 && i % kPolyEvery == kPolyEvery - 1) ? tc::exp2_poly2(e)
                                                                                    : make_float2(tc::ex2(e.x), tc::ex2(e.y));
             ls[i & 1] = tc::add2(ls[i & 1], p);
-            if (kBF16) {
+            if constexpr (kBF16) {
               // hi = p truncated to bf16 (its upper 16 bits), lo = p - hi exactly, then rounded
               const uint32_t u0 = __float_as_uint(p.x), u1 = __float_as_uint(p.y);
               hi[i] = __byte_perm(u0, u1, 0x7632);
@@ -487,13 +532,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
               lo[i] = MMA::pack(l.x, l.y);
             } else {
               hi[i] = MMA::pack(p.x, p.y);
-              const float2 h = MMA::unpack(hi[i]);
-              const float2 l = tc::sub2(p, h);
-              lo[i] = MMA::pack(l.x, l.y);
             }
           }
           tc::st16u(sbuf + c * 32, hi);
-          tc::st16u(sbuf + c * 32 + 16, lo);
+          if constexpr (kBF16) tc::st16u(sbuf + c * 32 + 16, lo);
         };
         // Chunk c+1's tensor-memory load is in flight while chunk c is exponentiated.
         float xa[32], xb[32];

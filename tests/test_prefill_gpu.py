@@ -86,7 +86,13 @@ def test_prefill_fast_and_generic_agree():
     feeds = mixed_feeds(23, H, KV, [512, 77], [0, 1000])
     fast, _, _ = run_float_case(feeds, H, KV)
     slow, _, _ = run_float_case(feeds, H, KV, force_generic=True)
-    assert np.abs(fast - slow).max() <= 4e-3
+    want, _, _ = oracle(feeds, H, KV)
+    check(fast, want)
+    check(slow, want)
+    # each within 2e-3 of the oracle beyond rounding: a value near a bf16 boundary may round to
+    # neighbouring outputs, one output ulp apart
+    ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(slow), 2.0 ** -126))) - 7)
+    assert np.all(np.abs(fast - slow) <= 4e-3 + ulp)
 
 
 @pytest.mark.parametrize("metadata", ["host", "device"])
@@ -105,3 +111,54 @@ def test_prefill_with_remapped_slots_uses_reference_semantics(metadata):
     want, wkc, wvc = oracle(feeds, H, KV)
     check(out, want)
     np.testing.assert_array_equal(kc.view(np.uint16), wkc.view(np.uint16))
+
+
+def _unused_slots(feeds):
+    """(block, slot) of every cache slot past a sequence's last key in its last block."""
+    bs = feeds["key_cache"].shape[1]
+    totals = np.diff(feeds["cumulative_sequence_length"]) + feeds["past_seqlens"]
+    slots = []
+    for b, n in enumerate(totals):
+        if n % bs:
+            blk = feeds["block_table"][b, (n - 1) // bs]
+            slots += [(blk, s) for s in range(n % bs, bs)]
+    return slots
+
+
+@pytest.mark.parametrize("dtype", [ref.BF16, np.float16])
+def test_prefill_ignores_unused_slots(dtype):
+    """NaN in the slots past each sequence's last key (the tail of its last page): the output
+    is the oracle's, which reads only the sequence's keys (as the reference's gather does)."""
+    H, KV = 32, 4
+    feeds = mixed_feeds(41, H, KV, [300, 200, 129], [0, 150, 37], dtype=dtype)
+    nan = np.array(np.nan, np.float32).astype(dtype)
+    unused = _unused_slots(feeds)
+    assert len(unused) > 0
+    for blk, s in unused:
+        feeds["key_cache"][blk, s] = nan
+        feeds["value_cache"][blk, s] = nan
+    out, kc, vc = run_float_case(feeds, H, KV)
+    want, wkc, wvc = oracle(feeds, H, KV)
+    assert np.isfinite(out).all()
+    check(out, want, dtype_is_bf16=dtype is ref.BF16)
+    np.testing.assert_array_equal(kc.view(np.uint16), wkc.view(np.uint16))
+    np.testing.assert_array_equal(vc.view(np.uint16), wvc.view(np.uint16))
+
+
+def test_prefill_bf16_values_beyond_fp16():
+    """bf16 V values beyond the fp16 range (P . V stays in bf16, P as hi + lo halves): finite
+    outputs, the oracle's result within the precision of a 16-bit-significand P."""
+    H, KV, D = 32, 4, 128
+    feeds = mixed_feeds(43, H, KV, [300, 200], [0, 150])
+    big = np.array([7.0e4, -2.5e5], np.float32).astype(ref.BF16)
+    feeds["value"][5, :D] = big[0]                      # a new row of sequence 0, kv head 0
+    blk = feeds["block_table"][1, 20 // 16]              # a cached row of sequence 1, kv head 2
+    feeds["value_cache"][blk, 20 % 16, 2] = big[1]
+    out, kc, vc = run_float_case(feeds, H, KV)
+    want, wkc, wvc = oracle(feeds, H, KV)
+    assert np.isfinite(out).all() and np.abs(want).max() > 100.0
+    # On a wide tile P carries about 16 significant bits (hi + lo bf16 halves), so an output of
+    # magnitude X (here up to ~1e4) may differ from the fp32 oracle by ~2^-16 X besides rounding.
+    excess = tolerance.excess(out, want, 8) - 2.0 ** -15 * np.abs(want)
+    assert excess.max() <= 2e-3, tolerance.report(out, want)
+    np.testing.assert_array_equal(vc.view(np.uint16), wvc.view(np.uint16))
