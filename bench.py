@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--pool-blocks", type=int, default=NB_PER_GPU, help="KV pool blocks per GPU")
     ap.add_argument("--mixed-chunks", type=int, default=8, help="mixed workload: prefill chunks")
     ap.add_argument("--mixed-decode", type=int, default=120, help="mixed workload: decode rows")
+    ap.add_argument("--mixed-dtype", default="bf16", choices=["bf16", "fp16"],
+                    help="mixed workload: activation and cache type (config 4 is bf16)")
     ap.add_argument("--workload", default="decode", choices=["decode", "mixed", "append", "gqa", "fp8"],
                     help="decode = BASELINE config 3 (the metric); mixed = config 4 (8 x 2048-token "
                          "prefill chunks + 120 decode rows, 64q/8kv); append = config 2 (KV append alone); "
@@ -590,13 +592,14 @@ def run_mixed(args):
     nt = int(cum[-1])
     g = torch.Generator(device=dev)
     g.manual_seed(4)
-    kc = torch.empty((NB, BS, KVm, D), dtype=torch.bfloat16, device=dev)
+    tdt = torch.float16 if args.mixed_dtype == "fp16" else torch.bfloat16
+    kc = torch.empty((NB, BS, KVm, D), dtype=tdt, device=dev)
     vc = torch.empty_like(kc)
     kc.normal_(0.0, 1.0, generator=g)
     vc.normal_(0.0, 1.0, generator=g)
-    q = torch.randn((nt, Hm * D), generator=g, device=dev).to(torch.bfloat16)
-    k = torch.randn((nt, KVm * D), generator=g, device=dev).to(torch.bfloat16)
-    v = torch.randn((nt, KVm * D), generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn((nt, Hm * D), generator=g, device=dev).to(tdt)
+    k = torch.randn((nt, KVm * D), generator=g, device=dev).to(tdt)
+    v = torch.randn((nt, KVm * D), generator=g, device=dev).to(tdt)
     host = {"cumulative_sequence_length": cum, "past_seqlens": past.astype(np.int32), "block_table": bt}
     p, keep, out = paged.build_params(q, k, v, kc, vc, torch.from_numpy(cum).to(dev),
                                       torch.from_numpy(past.astype(np.int32)).to(dev),
@@ -636,9 +639,9 @@ def run_mixed(args):
     del keep
 
     # CPU baseline: one of the prefill chunks and 15 of the decode rows through the C oracle on all
-    # host threads, scaled to the whole call (x n_pre chunks, x n_dec / 15 decode rows)
+    # host threads, scaled to the whole call (x n_pre chunks, x n_dec / 15 decode rows); bf16 only
     cpu = None
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and args.mixed_dtype == "bf16":
         bf = ml_dtypes.bfloat16
         crng = np.random.default_rng(44)
         sel = np.arange(n_pre, n_pre + min(15, n_dec))
@@ -684,9 +687,11 @@ def run_mixed(args):
                "sample": f"1 prefill chunk of {s_pre} tokens ({times['prefill']:.2f} s) and {len(sel)} of the "
                          f"{n_dec} decode rows ({times['decode']:.3f} s) through the C oracle, scaled to the "
                          f"whole call (x{n_pre} chunks, x{n_dec}/{len(sel)} rows)"}
-    return {"metric": "mixed ragged PagedAttention call time (config 4)", "value": ms, "unit": "ms/call",
+    fp16 = args.mixed_dtype == "fp16"
+    return {"metric": "mixed ragged PagedAttention call time (config 4%s)" % (", fp16 activations" if fp16 else ""),
+            "value": ms, "unit": "ms/call",
             "higher_is_better": False, "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 3),
-            "dtype": "bf16", "data": "synthetic (seeded)",
+            "dtype": args.mixed_dtype, "data": "synthetic (seeded)",
             "config": {"workload": "BASELINE config 4: 8 prefill chunks x 2048 tokens (causal) + 120 decode rows "
                                    "(ctx U[1024,16384]), 64q/8kv, d128, bs16", "num_tokens": nt,
                        "l2": "inputs larger than L2 (%.2f GB of decode KV per call)" % (decode_kv / 1e9)},
