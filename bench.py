@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--pool-blocks", type=int, default=NB_PER_GPU, help="KV pool blocks per GPU")
     ap.add_argument("--mixed-chunks", type=int, default=8, help="mixed workload: prefill chunks")
     ap.add_argument("--mixed-decode", type=int, default=120, help="mixed workload: decode rows")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: rebuild [B, H*d] by the peer-memory gather kernel or by NCCL all-gather + permute")
     ap.add_argument("--mixed-dtype", default="bf16", choices=["bf16", "fp16"],
                     help="mixed workload: activation and cache type (config 4 is bf16)")
     ap.add_argument("--workload", default="decode", choices=["decode", "mixed", "append", "gqa", "fp8"],
@@ -139,7 +141,7 @@ def config3_config(n, meta):
             "num_blocks_per_gpu": meta["NB"], "kv_heads_per_gpu": kvh,
             "l2": "inputs larger than L2 (KV pool 2 x %.1f GiB per GPU, %.2f GB read per step per GPU)" %
                   (pool_gib, kv_bytes / 1e9),
-            "parallelism": f"kv-head shard x{n}" + (" + NCCL all-gather" if n > 1 else "")}
+            "parallelism": f"kv-head shard x{n}" + (" + all-gather of the head-sharded outputs" if n > 1 else "")}
 
 
 # --------------------------------------------------------------------------------------------
@@ -313,6 +315,14 @@ def run_reference(args):
 # --------------------------------------------------------------------------------------------
 # B200 arm, config 3 (the headline)
 # --------------------------------------------------------------------------------------------
+def gather_note(n, pg):
+    """How a step at N > 1 rebuilds [B, H*d] from the head-sharded outputs."""
+    if n == 1:
+        return ""
+    return ", peer-memory gather kernel (all-gather + head permute over NVLink)" if pg is not None else \
+        ", NCCL all-gather and head permute"
+
+
 def capture_step(fn, dev, result):
     """`fn` (the C-ABI call, plus the all-gather and permute at N > 1) captured once in a CUDA
     graph on `dev`.  The capture is accepted only if a replay rewrites `result` (cleared first)
@@ -407,11 +417,18 @@ def run_b200(args):
     stream = torch.cuda.current_stream(dev)
     sp = ctypes.c_void_p(stream.cuda_stream)
     pp = ctypes.byref(p)
-    gathered = torch.empty((n, B, qh * D), dtype=torch.bfloat16, device=dev) if n > 1 else None
-    final = torch.empty((B, H * D), dtype=torch.bfloat16, device=dev) if n > 1 else out
+    pg, gathered, final = None, None, out
+    if n > 1 and args.gather == "peer":  # one kernel: peer stores into every rank's [B, H*d]
+        pg = sharding.PeerGather(B, qh * D, torch.bfloat16, dev)
+        final = pg.output
+    elif n > 1:
+        gathered = torch.empty((n, B, qh * D), dtype=torch.bfloat16, device=dev)
+        final = torch.empty((B, H * D), dtype=torch.bfloat16, device=dev)
 
     def gather():
-        if n > 1:  # one NCCL all-gather of the head-sharded outputs, then the head permute
+        if pg is not None:
+            pg(out)
+        elif n > 1:  # one NCCL all-gather of the head-sharded outputs, then the head permute
             dist.all_gather_into_tensor(gathered, out)
             final.copy_(sharding.reassemble(gathered))
         return final
@@ -520,8 +537,8 @@ def run_b200(args):
             "data": "synthetic (seeded numpy metadata, torch-seeded N(0,1)/sqrt(128) values)",
             "config": config3_config(n, meta),
             "step": ("host validation of the step's metadata + CUDA-graph replay of the C-ABI call"
-                     + (", NCCL all-gather and head permute" if n > 1 else "")) if graph is not None
-            else f"eager C-ABI call (graph {graph_note})",
+                     + gather_note(n, pg)) if graph is not None
+            else f"eager C-ABI call{gather_note(n, pg)} (graph {graph_note})",
             "eager_ms_per_step": eager_ms / args.steps,
             "kv_read_gbs": kv_bytes / (attn_ms / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -535,6 +552,11 @@ def run_b200(args):
         }
     graph = None  # released before the process group goes
     del keep
+    if pg is not None:
+        status = pg.read_status()
+        pg.close()
+        if status:
+            raise RuntimeError(f"peer gather: device status {status} (a bounded wait ran out)")
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -960,11 +982,18 @@ def run_fp8(args):
                                       k_scale=ks, v_scale=vs, host_metadata=host)
     stream = torch.cuda.current_stream(dev)
     sp, pp = ctypes.c_void_p(stream.cuda_stream), ctypes.byref(p)
-    gathered = torch.empty((n, B5, qh * D), dtype=torch.bfloat16, device=dev) if n > 1 else None
-    final = torch.empty((B5, H5 * D), dtype=torch.bfloat16, device=dev) if n > 1 else out
+    pg, gathered, final = None, None, out
+    if n > 1 and args.gather == "peer":  # one kernel: peer stores into every rank's [B, H*d]
+        pg = sharding.PeerGather(B5, qh * D, torch.bfloat16, dev)
+        final = pg.output
+    elif n > 1:
+        gathered = torch.empty((n, B5, qh * D), dtype=torch.bfloat16, device=dev)
+        final = torch.empty((B5, H5 * D), dtype=torch.bfloat16, device=dev)
 
     def gather():
-        if n > 1:
+        if pg is not None:
+            pg(out)
+        elif n > 1:
             dist.all_gather_into_tensor(gathered, out)
             final.copy_(sharding.reassemble(gathered))
         return final
@@ -1059,10 +1088,10 @@ def run_fp8(args):
                                        "bs16, B=256, ctx U[4096,32768], per-(block, kv head) scales U(0.01,0.1)",
                            "kv_heads_per_gpu": kvh, "num_blocks": NB,
                            "l2": f"inputs larger than L2 ({kv_bytes / 1e9:.2f} GB of KV per step per GPU)",
-                           "parallelism": f"kv-head shard x{n}" + (" + NCCL all-gather" if n > 1 else "")},
-                "step": ("host validation + CUDA-graph replay of the C-ABI call"
-                         + (", NCCL all-gather and head permute" if n > 1 else "")) if graph is not None
-                else f"eager C-ABI call (graph {graph_note})",
+                           "parallelism": f"kv-head shard x{n}" + ((" + peer-memory gather" if pg is not None
+                                                                     else " + NCCL all-gather") if n > 1 else "")},
+                "step": ("host validation + CUDA-graph replay of the C-ABI call" + gather_note(n, pg))
+                if graph is not None else f"eager C-ABI call{gather_note(n, pg)} (graph {graph_note})",
                 "eager_ms_per_step": eager_ms / steps,
                 "kv_read_gbs": kv_bytes / (attn_ms / 1e3) / 1e9,
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -1072,6 +1101,11 @@ def run_fp8(args):
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(), "gpu_launches": int(launches)}
     graph = None  # released before the process group goes
     del keep
+    if pg is not None:
+        status = pg.read_status()
+        pg.close()
+        if status:
+            raise RuntimeError(f"peer gather: device status {status} (a bounded wait ran out)")
     if dist:
         dist.barrier()
         dist.destroy_process_group()

@@ -1,4 +1,5 @@
-"""ctypes binding of ``include/b200_paged.h`` and ``include/b200_ep.h`` (the library's C ABI).
+"""ctypes binding of ``include/b200_paged.h``, ``include/b200_ep.h`` and ``include/b200_shard.h``
+(the library's C ABI).
 
 The library is loaded from this package folder.  A missing or stale library raises at import
 time: there is no CPU fallback for the claimed path.
@@ -161,6 +162,16 @@ class PagedTensors(ctypes.Structure):
 
 B200_ORT_OK, B200_ORT_INVALID_ARGUMENT, B200_ORT_EP_FAIL = 0, 1, 2
 
+SHARD_MAX_RANKS = 8
+
+
+class ShardGatherParams(ctypes.Structure):
+    """Mirror of ``B200ShardGatherParams`` (include/b200_shard.h)."""
+
+    _fields_ = [("world", _i32), ("rank", _i32), ("rows", _i32), ("slice_bytes", _i32), ("local", _vp),
+                ("outputs", _vp * SHARD_MAX_RANKS), ("flags", _vp * SHARD_MAX_RANKS), ("state", _vp),
+                ("status", _vp), ("num_sms", _i32)]
+
 # Every entry point the headers declare, with its ctypes signature.
 SIGNATURES = {
     "b200_version": (ctypes.c_int, []),
@@ -214,6 +225,13 @@ SIGNATURES = {
     "b200_ep_stream_create": (ctypes.c_int, [_i32, ctypes.POINTER(_vp)]),
     "b200_ep_stream_sync": (ctypes.c_int, [_vp]),
     "b200_ep_stream_destroy": (ctypes.c_int, [_i32, _vp]),
+    # include/b200_shard.h
+    "b200_shard_gather_params_size": (ctypes.c_int, []),
+    "b200_shard_gather": (ctypes.c_int, [ctypes.POINTER(ShardGatherParams), _vp]),
+    "b200_ipc_handle_size": (ctypes.c_int, []),
+    "b200_ipc_get_handle": (ctypes.c_int, [_vp, _vp]),
+    "b200_ipc_open_handle": (ctypes.c_int, [_i32, _vp, ctypes.POINTER(_vp)]),
+    "b200_ipc_close_handle": (ctypes.c_int, [_i32, _vp]),
 }
 
 
@@ -248,6 +266,8 @@ def load() -> ctypes.CDLL:
         raise ImportError("libb200_paged.so: B200GqaParams layout differs from the binding")
     if lib.b200_gqa_node_info_size() != ctypes.sizeof(GqaNodeInfo):
         raise ImportError("libb200_paged.so: B200GqaNodeInfo layout differs from the binding")
+    if lib.b200_shard_gather_params_size() != ctypes.sizeof(ShardGatherParams):
+        raise ImportError("libb200_paged.so: B200ShardGatherParams layout differs from the binding")
     for which, cls in enumerate((EpOptions, KvPoolDesc, KvPoolInfo, PagedTensors)):
         if lib.b200_ep_struct_size(which) != ctypes.sizeof(cls):
             raise ImportError(f"libb200_paged.so: {cls.__name__} layout differs from the binding")
