@@ -47,7 +47,6 @@ __device__ bool wait_all(const uint32_t* words, int world, uint32_t e) {
   for (int t = 0; t < world; ++t) {
     while ((int32_t)(ld_acquire_sys(words + t) - e) < 0) {
       if (globaltimer_ns() - start > kWaitLimitNs) return false;
-      __nanosleep(100);
     }
   }
   return true;
@@ -84,12 +83,12 @@ __global__ void __launch_bounds__(kGatherThreads) shard_gather_kernel(const __gr
   if (threadIdx.x == 0) {
     __threadfence_system();
     last = atomicAdd(&g.state[1], 1u) == gridDim.x - 1;
+    if (last) __threadfence_system();  // every CTA's arrival (and so its stores) before the exit flags
   }
   __syncthreads();
   if (!last) return;
 
   // exit (last CTA): release the exit flags, then wait for every rank's
-  __threadfence_system();
   if ((int)threadIdx.x < g.world) st_release_sys(g.flags[threadIdx.x] + g.world + g.rank, e);
   __syncthreads();
   if (threadIdx.x == 0) {
