@@ -181,8 +181,9 @@ B200_API int b200_kv_append(const B200PagedAttentionParams* p, void* stream);
  * overlap on the GPU race and must be serialised by the caller.  The first call on a device
  * resolves the array's address (cudaGetSymbolAddress) and should come before any stream
  * capture; the address is kept until exit, so cudaDeviceReset is not supported alongside this
- * entry point.  The scratch need grows with the token count (RoPE / q-k norm rows), the batch
- * and the SM count (decode partial rows: SMs x resident decode CTAs x 4 warps x 16 rows x
+ * entry point.  The scratch need grows with the token count (RoPE / q-k norm rows, and for
+ * bf16 prefill an fp16 copy of the new V rows, 2 x tokens x kv heads x head_size bytes), the
+ * batch and the SM count (decode partial rows: SMs x resident decode CTAs x 4 warps x 16 rows x
  * head_size x 4 bytes, about 9.7 MB at head_size 256 on 148 SMs), so a num_sms override far
  * above the device's count can push a call past the limit.  Without device_status the status
  * word lives in the static array too: read it with b200_read_status_static_scratch.  The call

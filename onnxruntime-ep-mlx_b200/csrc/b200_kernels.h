@@ -84,6 +84,12 @@ struct AttnArgs {
   int decode_on;   // decode kernel enabled for this call (shape supported)
   int decode_tile; // tokens per decode tile: kTile, or kFp8HalfTiles * kTile for fp8 caches
   int prefill_tq;  // query tokens per prefill work item (2 x 128 rows / group) or 0 = prefill kernel off
+  // bf16 prefill over an fp16 copy of this call's new V rows (every prefill sequence without a
+  // cached prefix): *v_shadow_wide is cleared by the plan kernel and set by the copy kernel when
+  // a value lies beyond the fp16 range; the shadow-V prefill then exits and the bf16 prefill,
+  // launched after it with prefill_fallback = 1, runs instead (it exits when the word is clear).
+  int* v_shadow_wide;
+  int prefill_fallback;
 };
 
 enum Route : int { kRouteDecode = 0, kRoutePrefill = 1, kRouteGeneric = 2 };
@@ -139,12 +145,18 @@ struct PrefillMaps {
   CUtensorMap k_map;  // cache views, as DecodeMaps
   CUtensorMap v_map;
   CUtensorMap q_map;  // [nt, H, d] view of the (processed) queries: box {64, group, 128/group}
+  CUtensorMap vs_map; // [nt, KV, d] fp16 copy of the new V rows (shadow-V prefill): box {64, 1, 16}
 };
 bool prefill_supported(int head_size, int block_size, int group, int act_dtype, int cache_dtype);
 // Query tokens of one prefill work item (a pair of 128-row q tiles) for query-head group `group`.
 int prefill_tokens_per_item(int group);
+// shadow_v: the shadow-V instantiation first, then the bf16 one as its fallback (see AttnArgs).
 cudaError_t launch_prefill(const AttnArgs& a, const DecodePlan& plan, const PrefillMaps& maps, int num_sms,
-                           cudaStream_t stream);
+                           cudaStream_t stream, bool shadow_v = false);
+// fp16 copy [nt, KV, d] of the new V rows (a.v_new, row stride a.v_stride), flagging values
+// beyond the fp16 range (bf16 magnitude bits 0x4780 and above, inf and NaN included) in
+// *a.v_shadow_wide.
+cudaError_t launch_v_shadow(const AttnArgs& a, void* shadow, cudaStream_t stream);
 
 cudaError_t launch_tc_selftest(bool bf16, const void* a, const void* b, const void* v, float* c_qk, float* c_pv,
                                float* c_ts, int* status, cudaStream_t stream, int* cu_result);

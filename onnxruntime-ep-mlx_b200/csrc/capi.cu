@@ -61,6 +61,7 @@ struct Layout {
   size_t q_proc = 0, k_proc = 0;
   size_t total_tiles = 0, seq_tile_off = 0, done = 0, part_o = 0, part_ml = 0;
   size_t route = 0, pf_tile_off = 0, pf_total = 0;
+  size_t v_shadow = 0;  // bf16 prefill: fp16 copy of the new V rows [nt, KV, d] (0 = none)
   int min_tiles_per_warp = 0;
   bool fast_decode = false;
   bool fast_prefill = false;
@@ -121,6 +122,8 @@ Layout make_layout(const B200PagedAttentionParams* p) {
     L.part_o = take(sizeof(float) * part_rows * d);
     L.part_ml = take(sizeof(float) * part_rows * 2);
   }
+  if (L.fast_prefill && p->act_dtype == B200_DTYPE_BFLOAT16 && nt > 0)
+    L.v_shadow = take(2 * nt * p->kv_num_heads * d);
   L.total = off;
   return L;
 }
@@ -560,6 +563,8 @@ int b200_paged_attention(const B200PagedAttentionParams* p, void* stream_ptr) {
       a.decode_on = L.fast_decode;
       a.decode_tile = p->cache_dtype == B200_DTYPE_FLOAT8E4M3FN ? b200::kFp8HalfTiles * b200::kTile : b200::kTile;
       a.prefill_tq = L.fast_prefill ? b200::prefill_tokens_per_item(group) : 0;
+      // the status block's second word: the shadow-V range flag (cleared by the plan kernel)
+      a.v_shadow_wide = L.v_shadow ? reinterpret_cast<int*>(ws + L.status + 64) : nullptr;
       if ((rc = encode_cache_map(&maps.k_map, p->key_cache, p))) return rc;
       if ((rc = encode_cache_map(&maps.v_map, p->value_cache, p))) return rc;
       if (L.fast_prefill) {
@@ -598,6 +603,30 @@ int b200_paged_attention(const B200PagedAttentionParams* p, void* stream_ptr) {
       }
       if (any_prefill && (p->host_slot_mapping || p->slot_mapping || duplicates)) any_generic = true;
     }
+    // bf16 prefill over an fp16 copy of the new V rows when no prefill sequence has a cached
+    // prefix (every key it reads is a new row of this call); known only with host metadata.
+    bool shadow_v = false;
+    if (any_prefill && host_meta && L.v_shadow && a.v_shadow_wide &&
+        ((reinterpret_cast<uintptr_t>(a.v_new) | (uintptr_t)(a.v_stride * 2)) & 15) == 0) {
+      const int32_t* cum = p->host_cumulative_sequence_length;
+      shadow_v = true;
+      for (int b = 0; b < p->batch && shadow_v; ++b) {
+        const int nq = cum[b + 1] - cum[b];
+        const bool prefill = nq > 0 && !(L.fast_decode && nq * group <= b200::kDecodeRows);
+        if (prefill && p->host_past_seqlens[b] != 0) shadow_v = false;
+      }
+    }
+    if (shadow_v) {
+      void* shadow = ws + L.v_shadow;
+      const uint64_t dims[3] = {(uint64_t)p->head_size, (uint64_t)p->kv_num_heads, (uint64_t)p->num_tokens};
+      const uint64_t strides[2] = {(uint64_t)p->head_size * 2, (uint64_t)p->kv_num_heads * p->head_size * 2};
+      const uint32_t box[3] = {64, 1, (uint32_t)b200::kTile};
+      int r = b200::encode_tensor_map(&pmaps.vs_map, false, 3, shadow, dims, strides, box);
+      if (r) return fail(B200_ERR_CUDA, "PagedAttention: cuTensorMapEncodeTiled (V copy) failed (" + std::to_string(r) + ")");
+      cudaError_t e = b200::launch_v_shadow(a, shadow, stream);
+      if (e != cudaSuccess) return cuda_fail(e, "v_shadow_kernel");
+      count_launches(1);
+    }
     if (p->attention_event_begin) {
       cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(p->attention_event_begin), stream);
       if (e != cudaSuccess) return cuda_fail(e, "event record");
@@ -608,9 +637,9 @@ int b200_paged_attention(const B200PagedAttentionParams* p, void* stream_ptr) {
       count_launches(1);
     }
     if (any_prefill) {
-      cudaError_t e = b200::launch_prefill(a, plan, pmaps, device_sm_count(p), stream);
+      cudaError_t e = b200::launch_prefill(a, plan, pmaps, device_sm_count(p), stream, shadow_v);
       if (e != cudaSuccess) return cuda_fail(e, "paged_prefill_kernel");
-      count_launches(1);
+      count_launches(shadow_v ? 2 : 1);
     }
     if (any_generic) {
       cudaError_t e = b200::launch_generic(a, stream);

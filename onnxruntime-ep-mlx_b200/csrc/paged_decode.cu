@@ -96,6 +96,7 @@ __device__ __forceinline__ int route_of(const AttnArgs& a, int b, int& dtiles, i
 __global__ void __launch_bounds__(1024) decode_plan_kernel(AttnArgs a, DecodePlan plan) {
   __shared__ int warp_sums[32];
   if (threadIdx.x == 0 && a.status) *a.status = 0;  // first kernel of every call clears status
+  if (threadIdx.x == 0 && a.v_shadow_wide) *a.v_shadow_wide = 0;
   int carry = 0, pcarry = 0;
   for (int base = 0; base < a.batch; base += blockDim.x) {
     const int b = base + threadIdx.x;

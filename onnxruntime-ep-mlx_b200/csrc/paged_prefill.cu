@@ -35,6 +35,7 @@
 //    the launcher checks before the first launch (a split above it would never complete);
 //  * every mbarrier wait is bounded (%globaltimer); a timeout sets the status word, the CTA
 //    waits (bounded) for its own copies and MMAs in flight, frees tensor memory and returns.
+#include <algorithm>
 #include <atomic>
 #include <type_traits>
 
@@ -187,14 +188,23 @@ bool prefill_supported(int head_size, int block_size, int group, int act_dtype, 
 
 int prefill_tokens_per_item(int group) { return kQTiles * kBM / group; }
 
-template <typename T>
+// SHADOW (bf16 only): V tiles come from an fp16 copy of the call's new V rows (maps.vs_map; every
+// prefill sequence has no cached prefix), so P is one fp16 value as for fp16 activations.
+template <typename T, bool SHADOW>
 __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid_constant__ AttnArgs a,
                                                                      const __grid_constant__ PrefillMaps maps,
                                                                      const DecodePlan plan) {
   using MMA = mma_op<T>;  // packing helpers only
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr bool kHiLo = kBF16 && !SHADOW;  // P as a hi + lo pair of bf16 values
   constexpr uint32_t kIdQK = tc::idesc_f16(kBM, kBN, kBF16, false, false);
-  constexpr uint32_t kIdPV = tc::idesc_f16(kBM, kD, kBF16, false, true);
+  constexpr uint32_t kIdPV = tc::idesc_f16(kBM, kD, kHiLo, false, true);
+  // The shadow-V launch steps aside when the copy found a value beyond the fp16 range; the bf16
+  // launch after it runs only then.
+  if (a.v_shadow_wide && (SHADOW || a.prefill_fallback)) {
+    const int wide = *a.v_shadow_wide;
+    if (SHADOW ? wide != 0 : wide == 0) return;
+  }
 
   extern __shared__ uint8_t dyn_smem[];
   __shared__ __align__(8) Bars bars;
@@ -263,7 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
       const int stages = is_v ? kVStages : kKStages;
       uint64_t* full_bar = is_v ? bars.v_full : bars.k_full;
       uint64_t* empty_bar = is_v ? bars.v_empty : bars.k_empty;
-      const CUtensorMap* map = is_v ? &maps.v_map : &maps.k_map;
+      const bool from_shadow = SHADOW && is_v;  // V rows of the call's fp16 copy: no pages
+      const CUtensorMap* map = from_shadow ? &maps.vs_map : is_v ? &maps.v_map : &maps.k_map;
       const uint32_t ring = sbase + (is_v ? kSmemV : kSmemK);
       uint32_t qc0 = 0, qc1 = 0, c = 0;  // Q loads per buffer, tiles loaded on this ring (scalars: no local memory)
       const int64_t oob_z = (int64_t)a.num_blocks * a.block_size;  // past the cache: zero fill
@@ -298,14 +309,17 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           if (j + 1 < m.n) blk_next = block_of(j + 1);  // in flight during the stage wait below
           const bool blk_ok = blk >= 0 && blk < a.num_blocks;
           if (!is_v && loader && pos0 < m.total && !blk_ok) set_status(a.status, kStatusBadBlock);
-          const int z = blk_ok ? blk * a.block_size + pos0 % a.block_size : (int)oob_z;
+          // copy row of position pos0 (no cached prefix): its token, or past the call's rows
+          // (zero fill); rows past the sequence's end are the next sequence's, finite, and get P = 0
+          const int z = from_shadow ? m.c0 + pos0 - m.past
+                                    : blk_ok ? blk * a.block_size + pos0 % a.block_size : (int)oob_z;
           const int st = (int)(c % (uint32_t)stages);
           if (c >= (uint32_t)stages && !(ok = wait_warp(&empty_bar[st], c / stages - 1))) break;
           // A V page that reaches past the sequence's last key (rows `rows` of 16 are the
           // sequence's): its rows come by plain loads and its unused slots are zeroed, since
           // whatever they hold, NaN included, must not meet P = 0 in the MMA.  Pages wholly past
           // the end load zero-filled by TMA.
-          const int rows = is_v ? tile_rows(m, j) & (kTile - 1) : 0;
+          const int rows = is_v && !from_shadow ? tile_rows(m, j) & (kTile - 1) : 0;
           const int tail_page = tile_rows(m, j) >> 4;
           if (rows) {
             const int32_t tblk = __shfl_sync(0xffffffffu, blk, 2 * tail_page);
@@ -363,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
                 const uint32_t pcol = pbuf + (kk >> 1) * 32 + (kk & 1) * 8;
                 if (leader) {
                   tc::mma_ts(obuf, pcol, vdesc, kIdPV, (j > 1 || kk > 0) ? 1u : 0u);
-                  if (kBF16) tc::mma_ts(obuf, pcol + 16, vdesc, kIdPV, 1u);
+                  if (kHiLo) tc::mma_ts(obuf, pcol + 16, vdesc, kIdPV, 1u);
                 }
               }
               if (leader && j == nkv_of(m, w)) tc::commit(&bars.o_done[w]);  // the item's last P . V
@@ -524,18 +538,21 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
             const float2 p = (kPolyEvery > 0 && i % kPolyEvery == kPolyEvery - 1) ? tc::exp2_poly2(e)
                                                                                    : make_float2(tc::ex2(e.x), tc::ex2(e.y));
             ls[i & 1] = tc::add2(ls[i & 1], p);
-            if constexpr (kBF16) {
+            if constexpr (kHiLo) {
               // hi = p truncated to bf16 (its upper 16 bits), lo = p - hi exactly, then rounded
               const uint32_t u0 = __float_as_uint(p.x), u1 = __float_as_uint(p.y);
               hi[i] = __byte_perm(u0, u1, 0x7632);
               const float2 l = tc::sub2(p, make_float2(__uint_as_float(u0 & 0xffff0000u), __uint_as_float(u1 & 0xffff0000u)));
               lo[i] = MMA::pack(l.x, l.y);
+            } else if constexpr (kBF16) {  // shadow V: fp16 P
+              const __half2 h = __floats2half2_rn(p.x, p.y);
+              hi[i] = *reinterpret_cast<const uint32_t*>(&h);
             } else {
               hi[i] = MMA::pack(p.x, p.y);
             }
           }
           tc::st16u(sbuf + c * 32, hi);
-          if constexpr (kBF16) tc::st16u(sbuf + c * 32 + 16, lo);
+          if constexpr (kHiLo) tc::st16u(sbuf + c * 32 + 16, lo);
         };
         // Chunk c+1's tensor-memory load is in flight while chunk c is exponentiated.
         float xa[32], xb[32];
@@ -596,16 +613,16 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   if (warp == kMmaWarp) tc::dealloc(tmem, 512);
 }
 
-cudaError_t launch_prefill(const AttnArgs& a, const DecodePlan& plan, const PrefillMaps& maps, int num_sms,
-                           cudaStream_t stream) {
+template <typename T, bool SHADOW>
+cudaError_t launch_prefill_t(const AttnArgs& a, const DecodePlan& plan, const PrefillMaps& maps, int num_sms,
+                             cudaStream_t stream) {
   const size_t smem = kSmemBytes + 1024;
-  const bool bf = a.act_dtype == B200_DTYPE_BFLOAT16;
-  auto kernel = bf ? paged_prefill_kernel<__nv_bfloat16> : paged_prefill_kernel<__half>;
+  auto kernel = paged_prefill_kernel<T, SHADOW>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  static std::atomic<uint32_t> ready[2][64];  // per dtype and device: attributes set and checked
-  std::atomic<uint32_t>& flag = ready[bf ? 1 : 0][dev & 63];
+  static std::atomic<uint32_t> ready[64];  // per device: attributes set and checked
+  std::atomic<uint32_t>& flag = ready[dev & 63];
   if (!flag.load(std::memory_order_acquire)) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -617,6 +634,47 @@ cudaError_t launch_prefill(const AttnArgs& a, const DecodePlan& plan, const Pref
     flag.store(1, std::memory_order_release);
   }
   kernel<<<num_sms, kThreads, smem, stream>>>(a, maps, plan);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill(const AttnArgs& a, const DecodePlan& plan, const PrefillMaps& maps, int num_sms,
+                           cudaStream_t stream, bool shadow_v) {
+  if (a.act_dtype != B200_DTYPE_BFLOAT16) return launch_prefill_t<__half, false>(a, plan, maps, num_sms, stream);
+  if (!shadow_v) return launch_prefill_t<__nv_bfloat16, false>(a, plan, maps, num_sms, stream);
+  cudaError_t e = launch_prefill_t<__nv_bfloat16, true>(a, plan, maps, num_sms, stream);
+  if (e != cudaSuccess) return e;
+  AttnArgs fb = a;
+  fb.prefill_fallback = 1;
+  return launch_prefill_t<__nv_bfloat16, false>(fb, plan, maps, num_sms, stream);
+}
+
+// fp16 copy of the new V rows, 8 channels per thread; a value beyond the fp16 range (bf16
+// magnitude bits >= 0x4780: bit 15 of (bits & 0x7fff) + 0x3880) sets the flag word.
+__global__ void __launch_bounds__(256) v_shadow_kernel(const AttnArgs a, uint4* shadow) {
+  const int vecs = a.kv_heads * a.head_size / 8;  // 16-byte pieces of one token's V row
+  const int64_t n = (int64_t)a.num_tokens * vecs;
+  uint32_t over = 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / vecs;
+    const int c = (int)(i - t * vecs);
+    const uint4 v = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.v_new) + t * a.v_stride + c * 8);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      over |= (w[k] & 0x7fff7fffu) + 0x38803880u;
+      const __half2 h = __floats2half2_rn(__uint_as_float(w[k] << 16), __uint_as_float(w[k] & 0xffff0000u));
+      o[k] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    shadow[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if (__any_sync(0xffffffffu, (over & 0x80008000u) != 0) && (threadIdx.x & 31) == 0) atomicOr(a.v_shadow_wide, 1);
+}
+
+cudaError_t launch_v_shadow(const AttnArgs& a, void* shadow, cudaStream_t stream) {
+  const int64_t n = (int64_t)a.num_tokens * a.kv_heads * a.head_size / 8;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 8));
+  v_shadow_kernel<<<grid, 256, 0, stream>>>(a, static_cast<uint4*>(shadow));
   return cudaGetLastError();
 }
 

@@ -125,12 +125,13 @@ def _unused_slots(feeds):
     return slots
 
 
-@pytest.mark.parametrize("dtype", [ref.BF16, np.float16])
-def test_prefill_ignores_unused_slots(dtype):
+@pytest.mark.parametrize("dtype,pasts", [(ref.BF16, [0, 150, 37]), (np.float16, [0, 150, 37]), (ref.BF16, [0, 0, 0])])
+def test_prefill_ignores_unused_slots(dtype, pasts):
     """NaN in the slots past each sequence's last key (the tail of its last page): the output
-    is the oracle's, which reads only the sequence's keys (as the reference's gather does)."""
+    is the oracle's, which reads only the sequence's keys (as the reference's gather does).
+    Without cached prefixes (pasts 0) the bf16 prefill reads V from the call's fp16 copy."""
     H, KV = 32, 4
-    feeds = mixed_feeds(41, H, KV, [300, 200, 129], [0, 150, 37], dtype=dtype)
+    feeds = mixed_feeds(41, H, KV, [300, 200, 129], pasts, dtype=dtype)
     nan = np.array(np.nan, np.float32).astype(dtype)
     unused = _unused_slots(feeds)
     assert len(unused) > 0
@@ -145,11 +146,14 @@ def test_prefill_ignores_unused_slots(dtype):
     np.testing.assert_array_equal(vc.view(np.uint16), wvc.view(np.uint16))
 
 
-def test_prefill_bf16_values_beyond_fp16():
+@pytest.mark.parametrize("pasts", [[0, 150], [0, 20]])
+def test_prefill_bf16_values_beyond_fp16(pasts):
     """bf16 V values beyond the fp16 range (P . V stays in bf16, P as hi + lo halves): finite
-    outputs, the oracle's result within the precision of a 16-bit-significand P."""
+    outputs, the oracle's result within the precision of a 16-bit-significand P.  With
+    pasts [0, 20] the value in the cache sits in a cached prefix; the new-row value of sequence 0
+    alone would send a no-prefix call from its fp16 V copy to the bf16 fallback launch."""
     H, KV, D = 32, 4, 128
-    feeds = mixed_feeds(43, H, KV, [300, 200], [0, 150])
+    feeds = mixed_feeds(43, H, KV, [300, 200], pasts)
     big = np.array([7.0e4, -2.5e5], np.float32).astype(ref.BF16)
     feeds["value"][5, :D] = big[0]                      # a new row of sequence 0, kv head 0
     blk = feeds["block_table"][1, 20 // 16]              # a cached row of sequence 1, kv head 2
@@ -159,6 +163,34 @@ def test_prefill_bf16_values_beyond_fp16():
     assert np.isfinite(out).all() and np.abs(want).max() > 100.0
     # On a wide tile P carries about 16 significant bits (hi + lo bf16 halves), so an output of
     # magnitude X (here up to ~1e4) may differ from the fp32 oracle by ~2^-16 X besides rounding.
+    excess = tolerance.excess(out, want, 8) - 2.0 ** -15 * np.abs(want)
+    assert excess.max() <= 2e-3, tolerance.report(out, want)
+    np.testing.assert_array_equal(vc.view(np.uint16), wvc.view(np.uint16))
+
+
+@pytest.mark.parametrize("H,KV", [(32, 4), (64, 8), (16, 16)])
+def test_prefill_bf16_without_prefix_reads_fp16_v_copy(H, KV):
+    """bf16 prefill sequences without a cached prefix (decode rows may have one): P . V runs on
+    an fp16 copy of the call's new V rows with one fp16 P; the output is the oracle's within the
+    usual bound, caches bit-exact."""
+    nqs, pasts = [300, 200, 1, 129, 16], [0, 0, 500, 0, 0]
+    feeds = mixed_feeds(47 + H, H, KV, nqs, pasts)
+    out, kc, vc = run_float_case(feeds, H, KV)
+    want, wkc, wvc = oracle(feeds, H, KV)
+    check(out, want)
+    np.testing.assert_array_equal(kc.view(np.uint16), wkc.view(np.uint16))
+    np.testing.assert_array_equal(vc.view(np.uint16), wvc.view(np.uint16))
+
+
+def test_prefill_bf16_fp16_copy_out_of_range_falls_back():
+    """A new V value beyond the fp16 range in a no-prefix call: the fp16-copy launch steps aside
+    and the bf16 launch computes the call, with the oracle's result."""
+    H, KV, D = 32, 4, 128
+    feeds = mixed_feeds(53, H, KV, [300, 200], [0, 0])
+    feeds["value"][310, D:2 * D] = np.array(9.0e4, np.float32).astype(ref.BF16)  # sequence 1, kv head 1
+    out, kc, vc = run_float_case(feeds, H, KV)
+    want, wkc, wvc = oracle(feeds, H, KV)
+    assert np.isfinite(out).all() and np.abs(want).max() > 100.0
     excess = tolerance.excess(out, want, 8) - 2.0 ** -15 * np.abs(want)
     assert excess.max() <= 2e-3, tolerance.report(out, want)
     np.testing.assert_array_equal(vc.view(np.uint16), wvc.view(np.uint16))
