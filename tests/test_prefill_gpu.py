@@ -194,3 +194,29 @@ def test_prefill_bf16_fp16_copy_out_of_range_falls_back():
     excess = tolerance.excess(out, want, 8) - 2.0 ** -15 * np.abs(want)
     assert excess.max() <= 2e-3, tolerance.report(out, want)
     np.testing.assert_array_equal(vc.view(np.uint16), wvc.view(np.uint16))
+
+
+@pytest.mark.parametrize("dtype,pasts", [(ref.BF16, [0, 0, 500, 0]), (ref.BF16, [0, 150, 500, 37]),
+                                         (np.float16, [0, 0, 500, 0])])
+def test_prefill_packed_qkv(dtype, pasts):
+    """Packed QKV (key and value inside the query rows, attention.rs:3877-3890): the prefill,
+    the fp16 V copy and decode read K and V at the packed row stride; output and caches are the
+    oracle's."""
+    from onnxruntime_ep_b200 import paged_attention
+    from gpu_helpers import to_dev, to_np
+
+    H, KV = 32, 4
+    feeds = mixed_feeds(59, H, KV, [300, 200, 1, 129], pasts, dtype=dtype)
+    packed = np.concatenate([feeds["query"], feeds["key"], feeds["value"]], axis=1)
+    meta = {n: torch.from_numpy(feeds[n]) for n in ("cumulative_sequence_length", "past_seqlens", "block_table")}
+    out, kc, vc = paged_attention(
+        to_dev(packed), None, None, to_dev(feeds["key_cache"]), to_dev(feeds["value_cache"]),
+        meta["cumulative_sequence_length"], meta["past_seqlens"], meta["block_table"],
+        num_heads=H, kv_num_heads=KV, check_status=True)
+    torch.cuda.synchronize()
+    want, wkc, wvc = ref.paged_attention(
+        packed, None, None, feeds["key_cache"], feeds["value_cache"],
+        feeds["cumulative_sequence_length"], feeds["past_seqlens"], feeds["block_table"], H, KV)
+    check(out.float().cpu().numpy(), want, dtype_is_bf16=dtype is ref.BF16)
+    np.testing.assert_array_equal(to_np(kc).view(np.uint16), wkc.view(np.uint16))
+    np.testing.assert_array_equal(to_np(vc).view(np.uint16), wvc.view(np.uint16))
