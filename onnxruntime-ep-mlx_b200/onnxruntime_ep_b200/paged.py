@@ -31,7 +31,7 @@ _DTYPES = {
 _workspaces: dict[int, torch.Tensor] = {}
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+def _shared_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """Per-device scratch buffer, grown on demand (never shrunk)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     buf = _workspaces.get(idx)
@@ -64,8 +64,13 @@ def build_params(query, key, value, key_cache, value_cache, cum, past, block_tab
                  is_causal=1, local_window_size=-1, softcap=0.0, do_rotary=0, rotary_interleaved=0,
                  rotary_offset=0, qk_norm_epsilon=1e-6, k_quant_type="NONE", v_quant_type="NONE",
                  output=None, host_metadata=None, min_tiles_per_warp=0, force_generic=False,
-                 kv_only=False, kv_cache_layout="SEPARATE", v_head_size=0):
+                 kv_only=False, kv_cache_layout="SEPARATE", v_head_size=0, workspace=None):
     """Fill a ``B200PagedAttentionParams``.  Returns ``(params, keepalive, output)``.
+
+    The scratch is this device's shared buffer unless ``workspace`` (a uint8 CUDA tensor of at
+    least ``b200_paged_attention_workspace_size`` bytes) is given.  Params built on the shared
+    buffer must be used in one stream order: calls that may overlap on the GPU need private
+    workspaces.  The keepalive holds the buffer, so a later, larger build does not free it.
 
     ``kv_cache_layout="LATENT"``: one kv head, ``value`` and ``value_cache`` are ``None``, and the
     values are the first ``v_head_size`` channels of the key rows (output ``[nt, H*v_head_size]``)."""
@@ -170,7 +175,15 @@ def build_params(query, key, value, key_cache, value_cache, cum, past, block_tab
     p.force_generic = int(bool(force_generic))
     nbytes = ctypes.c_size_t(0)
     check(LIB.b200_paged_attention_workspace_size(ctypes.byref(p), ctypes.byref(nbytes)))
-    ws = workspace(device, nbytes.value)
+    if workspace is None:
+        ws = _shared_workspace(device, nbytes.value)
+    else:
+        ws = workspace
+        if ws.dtype != torch.uint8 or ws.device != device or not ws.is_contiguous() or ws.numel() < nbytes.value:
+            raise _capi.B200Error(_capi.B200_ERR_WORKSPACE,
+                                  "PagedAttention: workspace must be a contiguous uint8 tensor on the caches' "
+                                  f"device of at least {nbytes.value} bytes")
+    keep.append(ws)
     p.workspace = _ptr(ws)
     p.workspace_bytes = ws.numel()
     return p, keep, output

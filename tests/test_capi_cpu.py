@@ -110,3 +110,52 @@ def test_workspace_size_grows_with_tokens():
         assert _capi.LIB.b200_paged_attention_workspace_size(ctypes.byref(p), ctypes.byref(n)) == 0
         sizes.append(n.value)
     assert sizes[1] > sizes[0] > 0
+
+
+# ---------------------------------------------------------------------------------------------
+# Python helper: workspace ownership (host only; the params are filled, nothing is launched)
+# ---------------------------------------------------------------------------------------------
+def _cpu_call_tensors(nt=20, H=8, KV=2, D=128, B=2, bs=16):
+    torch = pytest.importorskip("torch")
+    q = torch.zeros((nt, H * D), dtype=torch.bfloat16)
+    k = torch.zeros((nt, KV * D), dtype=torch.bfloat16)
+    kc = torch.zeros((8, bs, KV, D), dtype=torch.bfloat16)
+    cum = torch.tensor([0, 12, nt], dtype=torch.int32)
+    past = torch.tensor([0, 3], dtype=torch.int32)
+    bt = torch.tensor([[0, 1], [2, 3]], dtype=torch.int32)
+    return (q, k, k, kc, kc, cum, past, bt), dict(num_heads=H, kv_num_heads=KV)
+
+
+def test_build_params_keeps_its_shared_workspace(monkeypatch):
+    """A later, larger build replaces the shared buffer; params built before it keep theirs
+    alive through the keepalive list instead of pointing at freed memory."""
+    torch = pytest.importorskip("torch")
+    from onnxruntime_ep_b200 import paged
+    bufs = []
+
+    def fake_shared(device, nbytes):
+        bufs.append(torch.empty(nbytes, dtype=torch.uint8))
+        return bufs[-1]
+
+    monkeypatch.setattr(paged, "_shared_workspace", fake_shared)
+    args, kw = _cpu_call_tensors()
+    p, keep, _ = paged.build_params(*args, **kw)
+    assert any(t is bufs[-1] for t in keep)
+    assert p.workspace == bufs[-1].data_ptr() and p.workspace_bytes == bufs[-1].numel()
+
+
+def test_build_params_private_workspace():
+    torch = pytest.importorskip("torch")
+    from onnxruntime_ep_b200 import paged
+    args, kw = _cpu_call_tensors()
+    need = ctypes.c_size_t(0)
+    p0, _, _ = paged.build_params(*args, **kw, workspace=torch.empty(64 << 20, dtype=torch.uint8))
+    _capi.check(_capi.LIB.b200_paged_attention_workspace_size(ctypes.byref(p0), ctypes.byref(need)))
+    ws = torch.empty(need.value, dtype=torch.uint8)
+    p, keep, _ = paged.build_params(*args, **kw, workspace=ws)
+    assert p.workspace == ws.data_ptr() and p.workspace_bytes == need.value
+    assert any(t is ws for t in keep)
+    for bad in (torch.empty(need.value - 1, dtype=torch.uint8), torch.empty(need.value, dtype=torch.int8),
+                torch.empty(2 * need.value, dtype=torch.uint8)[::2]):
+        with pytest.raises(_capi.B200Error, match="workspace"):
+            paged.build_params(*args, **kw, workspace=bad)
