@@ -152,7 +152,9 @@ B200_API uint64_t b200_launch_count(void);
 /* Message of the last failing call on this thread ("" if none). */
 B200_API const char* b200_last_error(void);
 
-/* Bytes of device workspace the call needs (depends on shapes only, not on metadata). */
+/* Bytes of device workspace the call needs (depends on shapes only, not on metadata).  The
+ * call's kernels read their plan from the workspace while they run, so calls that may overlap
+ * on the GPU (different streams, unordered threads) each need their own workspace. */
 B200_API int b200_paged_attention_workspace_size(const B200PagedAttentionParams* p, size_t* bytes);
 
 /* Host-side metadata validation, restating attention.rs:3934-3990.  Needs the host_*
