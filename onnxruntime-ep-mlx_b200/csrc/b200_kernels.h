@@ -108,6 +108,8 @@ cudaError_t launch_generic(const AttnArgs& a, cudaStream_t stream);
 // the decode tile stream (stream-K layout) and the prefill tile list.
 struct DecodePlan {
   int64_t* pf_total;     // [1]   prefill work items: q tiles x kv heads
+  unsigned long long* pf_next;  // [1] next prefill work item to hand out (CTAs take items
+                               //     by atomicAdd, in list order); zeroed by the plan kernel
   int* pf_tile_off;      // [B+1] exclusive prefix of prefill q tiles over sequences
   int64_t* total_tiles;  // [1]   tiles over all decode sequences x kv heads
   int* seq_tile_off;     // [B+1] exclusive prefix of decode tiles (per kv head) over sequences

@@ -60,7 +60,7 @@ struct Layout {
   uint32_t owner_cap = 0;
   size_t q_proc = 0, k_proc = 0;
   size_t total_tiles = 0, seq_tile_off = 0, done = 0, part_o = 0, part_ml = 0;
-  size_t route = 0, pf_tile_off = 0, pf_total = 0;
+  size_t route = 0, pf_tile_off = 0, pf_total = 0, pf_next = 0;
   size_t v_shadow = 0;  // bf16 prefill: fp16 copy of the new V rows [nt, KV, d] (0 = none)
   int min_tiles_per_warp = 0;
   bool fast_decode = false;
@@ -108,6 +108,7 @@ Layout make_layout(const B200PagedAttentionParams* p) {
     L.route = take(sizeof(int) * (size_t)p->batch);
     L.pf_tile_off = take(sizeof(int) * ((size_t)p->batch + 1));
     L.pf_total = take(sizeof(int64_t));
+    L.pf_next = take(sizeof(unsigned long long));
   }
   if (L.fast_decode || L.fast_prefill) {
     // Stream-K decode: at most 2 partial slots of 8 rows per warp of the persistent grid, whose
@@ -559,6 +560,7 @@ int b200_paged_attention(const B200PagedAttentionParams* p, void* stream_ptr) {
       plan.min_tiles_per_warp = L.min_tiles_per_warp;
       plan.pf_tile_off = reinterpret_cast<int*>(ws + L.pf_tile_off);
       plan.pf_total = reinterpret_cast<int64_t*>(ws + L.pf_total);
+      plan.pf_next = reinterpret_cast<unsigned long long*>(ws + L.pf_next);
       a.route = reinterpret_cast<int*>(ws + L.route);
       a.decode_on = L.fast_decode;
       a.decode_tile = p->cache_dtype == B200_DTYPE_FLOAT8E4M3FN ? b200::kFp8HalfTiles * b200::kTile : b200::kTile;

@@ -119,6 +119,7 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(AttnArgs a, DecodePla
     plan.pf_tile_off[a.batch] = pcarry;
     *plan.total_tiles = (int64_t)carry * a.kv_heads;
     *plan.pf_total = (int64_t)pcarry * a.kv_heads;
+    if (plan.pf_next) *plan.pf_next = 0;
   }
 }
 

@@ -10,7 +10,8 @@
 //    tokens x the g query heads of the kv head, so each K/V tile serves the whole head group
 //    (native GQA), and the two q tiles of an item share every K/V tile they load;
 //  * persistent CTAs (one per SM: 224 KB of shared memory and all 512 tensor-memory columns)
-//    take items round-robin, longest (latest q tiles) first;
+//    take items from the list (longest, i.e. latest q tiles, first) by an atomic counter when
+//    ready for the next one;
 //  * warp-specialised, the roles synchronised only through mbarriers:
 //      - warp 8 (TMA producer): Q tiles [128 x 128] by a 3-D box pair from the [nt, H, d]
 //        query view, one buffer per q tile; K tiles (2 stages) and V tiles (3 stages) of 128
@@ -93,6 +94,12 @@ constexpr int kSoftmaxRegs = 200;  // setmaxnreg split: 2 x 128 x 200 + 128 x 96
 constexpr int kControlRegs = 96;
 constexpr int kSplitRegs = 2 * kWgThreads * kSoftmaxRegs + kWgThreads * kControlRegs;
 static_assert(kSplitRegs <= kThreads * 168, "register split exceeds the 384 x 168 launch allocation");
+// Work items are handed out at run time: warp 8 takes the next item of the list with an atomicAdd
+// on plan.pf_next when it is ready for it and passes it through a kSched-slot queue in shared
+// memory to the other roles, so CTAs that finish early take more items (the list is longest
+// first) instead of a fixed round-robin share.
+constexpr int kSched = 4;
+constexpr int kSchedTakers = 2 * kWgThreads / 32 + 2;  // softmax warps, MMA warp, V producer warp
 
 struct Bars {
   uint64_t q_full[kQTiles], q_empty[kQTiles];
@@ -103,6 +110,7 @@ struct Bars {
   // earlier MMAs, so s_full[w] for tile j also says that P . V of tile j-1 has landed in O.
   uint64_t s_full[kQTiles], p_full[kQTiles], o_done[kQTiles];
   uint64_t drain;
+  uint64_t sched_full[kSched], sched_empty[kSched];  // item queue: published / taken by every taker warp
 };
 
 // One item of the prefill work list, as every role decodes it.
@@ -210,6 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   __shared__ __align__(8) Bars bars;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int s_failed;
+  __shared__ volatile long long s_item[kSched];
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -236,6 +245,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
       mbar_init(&bars.v_empty[i], 1);
     }
     mbar_init(&bars.drain, 1);
+    for (int i = 0; i < kSched; ++i) {
+      mbar_init(&bars.sched_full[i], 1);
+      mbar_init(&bars.sched_empty[i], kSchedTakers);
+    }
     fence_mbar_init();
     s_failed = 0;
   }
@@ -260,6 +273,28 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   auto failed_warp = [&]() -> bool { return __any_sync(0xffffffffu, s_failed != 0); };
   // After a failure: bounded wait for a copy or commit this CTA issued, without the early exit.
   auto drain_idx = [&](uint64_t* bar, uint32_t index) { mbar_wait(bar, index & 1u); };
+  // k-th work item of this CTA (n_items or more: none left).  Warp 8 takes it from the list and
+  // publishes it; every taker warp reads it and frees the slot.  False when a wait ran out.
+  auto fetch_item = [&](uint32_t k, int64_t& it) -> bool {
+    const uint32_t slot = k % kSched;
+    if (k >= (uint32_t)kSched && !wait_warp(&bars.sched_empty[slot], k / kSched - 1)) return false;
+    long long v = 0;
+    if (lane == 0) {
+      v = (long long)atomicAdd(plan.pf_next, 1ull);
+      s_item[slot] = v;
+      mbar_arrive(&bars.sched_full[slot]);
+    }
+    it = __shfl_sync(0xffffffffu, v, 0);
+    return true;
+  };
+  auto take_item = [&](uint32_t k, int64_t& it) -> bool {
+    const uint32_t slot = k % kSched;
+    if (!wait_warp(&bars.sched_full[slot], k / kSched)) return false;
+    it = s_item[slot];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars.sched_empty[slot]);
+    return true;
+  };
 
   if (warp >= 2 * (kWgThreads / 32)) {
     // warpgroup 2: producers, MMA issuer and an idle warp give registers to the softmax
@@ -281,7 +316,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
       const int page = (lane & 15) >> 1, half = lane & 1;
       const bool loader = lane < 16;
       bool ok = true;
-      for (int64_t it = blockIdx.x; it < n_items && ok && !failed_warp(); it += gridDim.x) {
+      for (uint32_t k = 0; ok && !failed_warp(); ++k) {
+        int64_t it;
+        if (!(ok = is_v ? take_item(k, it) : fetch_item(k, it)) || it >= n_items) break;
         const Item m = decode_item(a, plan, it);
         if (m.skip) continue;
         if (!is_v) {
@@ -346,7 +383,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
       const bool leader = tc::elect_one();
       uint32_t qc0 = 0, qc1 = 0, pc0 = 0, pc1 = 0, kvc = 0;
       bool issued = false, ok = true;
-      for (int64_t it = blockIdx.x; it < n_items && ok && !failed_warp(); it += gridDim.x) {
+      for (uint32_t k = 0; ok && !failed_warp(); ++k) {
+        int64_t it;
+        if (!(ok = take_item(k, it)) || it >= n_items) break;
         const Item m = decode_item(a, plan, it);
         if (m.skip) continue;
         // Step j issues PV0(j-1), S0(j), PV1(j-1), S1(j) (step n: the last PVs only), each from
@@ -432,7 +471,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
     const float qk_scale = a.softcap > 0.f ? a.scale : a.scale * kLog2eP;
     uint32_t t = 0;      // tiles this warpgroup has processed
     uint32_t items = 0;  // items this warpgroup has finished (o_done completions)
-    for (int64_t it = blockIdx.x; it < n_items && !failed_warp(); it += gridDim.x) {
+    for (uint32_t k = 0; !failed_warp(); ++k) {
+      int64_t it;
+      if (!take_item(k, it) || it >= n_items) break;
       const Item m = decode_item(a, plan, it);
       if (m.skip || nkv_of(m, w) == 0) continue;
       const int tl = row / g, hl = row % g;
