@@ -600,6 +600,7 @@ __global__ void __launch_bounds__(kClThreads) gqa_cluster_kernel(const GqaArgs a
       st4(kbuf + (size_t)k * D + d, ld4(key_row<T>(a, bg, b, kh, c0 + k, false) + d));
       st4(vbuf + (size_t)k * D + d, ld4(key_row<T>(a, bg, b, kh, c0 + k, true) + d));
     }
+    if (a.fused_copy) fence_proxy_async_smem();  // the new rows, for the bulk present stores
     if (np > 0 && !mbar_wait(&bar_k, phase)) failed = true;
     if (__syncthreads_or(failed)) {
       // one more bounded wait on each copy still in flight, then no further work
@@ -612,12 +613,14 @@ __global__ void __launch_bounds__(kClThreads) gqa_cluster_kernel(const GqaArgs a
       break;
     }
 
-    // ---- fused present rows of K (all rows when present is its own buffer, else the new ones)
-    if (a.fused_copy) {
+    // ---- fused present rows of K (all rows when present is its own buffer, else the new ones):
+    // contiguous in the BNSH present, so one bulk copy from the staging buffer
+    if (a.fused_copy && tid == 0) {
       const int first = a.present_separate ? 0 : np;
-      for (int i = tid; i < (nk - first) * kUnits; i += kClThreads) {
-        const int k = first + i / kUnits, d = (i % kUnits) * 4;
-        st4(present_row<T>(a, b, kh, c0 + k, false) + d, *reinterpret_cast<const typename Vec4<T>::raw*>(kbuf + (size_t)k * D + d));
+      if (nk > first) {
+        bulk_store(present_row<T>(a, b, kh, c0 + first, false), kbuf + (size_t)first * D,
+                   (uint32_t)((nk - first) * D * (int)sizeof(T)));
+        bulk_commit();
       }
     }
 
@@ -690,12 +693,13 @@ __global__ void __launch_bounds__(kClThreads) gqa_cluster_kernel(const GqaArgs a
       break;
     }
 
-    // ---- fused present rows of V
-    if (a.fused_copy) {
+    // ---- fused present rows of V, as for K
+    if (a.fused_copy && tid == 0) {
       const int first = a.present_separate ? 0 : np;
-      for (int i = tid; i < (nk - first) * kUnits; i += kClThreads) {
-        const int k = first + i / kUnits, d = (i % kUnits) * 4;
-        st4(present_row<T>(a, b, kh, c0 + k, true) + d, *reinterpret_cast<const typename Vec4<T>::raw*>(vbuf + (size_t)k * D + d));
+      if (nk > first) {
+        bulk_store(present_row<T>(a, b, kh, c0 + first, true), vbuf + (size_t)first * D,
+                   (uint32_t)((nk - first) * D * (int)sizeof(T)));
+        bulk_commit();
       }
     }
 
@@ -717,8 +721,10 @@ __global__ void __launch_bounds__(kClThreads) gqa_cluster_kernel(const GqaArgs a
         o[r][3] = fmaf(p, vx[3], o[r][3]);
       }
     }
+    if (tid == 0) bulk_wait_read();  // the present copies have read the staging buffers
     __syncthreads();  // the next chunk overwrites the staging buffers and the probabilities
   }
+  if (tid == 0) bulk_wait_read();  // also after a failed wait (loop left early)
 
   // ---- CTA partial: sum the key groups
 #pragma unroll
@@ -1446,8 +1452,9 @@ constexpr size_t kClSmemBudget = 220 * 1024;
 bool cluster_path(const B200GqaParams* p, const GqaPlan& P) {
   const int D = p->head_size;
   if (!P.fused || !(D == 64 || D == 128 || D == 256)) return false;
-  for (const void* ptr : {p->past_key, p->past_value})
-    if (reinterpret_cast<uintptr_t>(ptr) % 16) return false;  // cp.async stages 16-byte chunks
+  for (const void* ptr : {(const void*)p->past_key, (const void*)p->past_value, (const void*)p->present_key,
+                          (const void*)p->present_value})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16) return false;  // bulk copies move 16-byte units
   return true;
 }
 
