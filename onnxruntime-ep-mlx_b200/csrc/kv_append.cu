@@ -169,7 +169,8 @@ __device__ __forceinline__ void refine_route(const PrologueArgs& a, int t, int b
 
 // Plain reshape-and-cache (no norm / RoPE, cache in the activation type): one warp per token,
 // kCopyTokensPerCta tokens per CTA.  The token's [KV*d] K and V rows are contiguous in the
-// input and in the pool; each lane issues all its 16-byte loads of both rows before storing.
+// input and in the pool; each lane issues all its 16-byte loads of both rows before storing, and
+// with a slot_mapping the first group of loads goes out before the slot's owner is resolved.
 constexpr int kCopyTokensPerCta = 8;
 constexpr int kCopyUnroll = 4;
 
@@ -177,6 +178,25 @@ __global__ void __launch_bounds__(32 * kCopyTokensPerCta) kv_copy_kernel(Prologu
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * kCopyTokensPerCta + warp;
   if (t >= a.num_tokens) return;  // whole warp
+  const int64_t bytes = (int64_t)a.kv_heads * a.head_size * 2;
+  const int64_t n16 = bytes / 16;
+  const char* ksrc = reinterpret_cast<const char*>(a.key) + (int64_t)t * a.key_stride * 2;
+  const char* vsrc = reinterpret_cast<const char*>(a.value) + (int64_t)t * a.value_stride * 2;
+  const bool src_vec = ((reinterpret_cast<uintptr_t>(ksrc) | reinterpret_cast<uintptr_t>(vsrc) | bytes) & 15) == 0;
+  // With a slot_mapping, the row's first group of loads is in flight during the sequence search and
+  // the owner-table probe below (not for padding tokens, slot -1); the stores still wait for them.
+  uint4 kr[kCopyUnroll], vr[kCopyUnroll];
+  const bool pre = src_vec && a.slot_mapping && __ldg(a.slot_mapping + t) >= 0;  // warp-uniform
+  if (pre) {
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) {
+      const int64_t j = u * 32 + lane;
+      if (j < n16) {
+        kr[u] = __ldg(reinterpret_cast<const uint4*>(ksrc) + j);
+        vr[u] = __ldg(reinterpret_cast<const uint4*>(vsrc) + j);
+      }
+    }
+  }
   const int b = seq_of_token(a.cum, a.batch, t);
   int64_t slot = -1;
   const bool valid = token_slot(a, t, b, slot);
@@ -186,23 +206,19 @@ __global__ void __launch_bounds__(32 * kCopyTokensPerCta) kv_copy_kernel(Prologu
     refine_route(a, t, b, slot, write);
   }
   if (!write) return;  // whole warp
-  const int64_t bytes = (int64_t)a.kv_heads * a.head_size * 2;
   char* kdst = reinterpret_cast<char*>(a.key_cache) + slot * bytes;
   char* vdst = reinterpret_cast<char*>(a.value_cache) + slot * bytes;
-  const char* ksrc = reinterpret_cast<const char*>(a.key) + (int64_t)t * a.key_stride * 2;
-  const char* vsrc = reinterpret_cast<const char*>(a.value) + (int64_t)t * a.value_stride * 2;
-  const bool vec = ((reinterpret_cast<uintptr_t>(kdst) | reinterpret_cast<uintptr_t>(vdst) |
-                     reinterpret_cast<uintptr_t>(ksrc) | reinterpret_cast<uintptr_t>(vsrc) | bytes) & 15) == 0;
+  const bool vec = src_vec && ((reinterpret_cast<uintptr_t>(kdst) | reinterpret_cast<uintptr_t>(vdst)) & 15) == 0;
   if (vec) {
-    const int64_t n16 = bytes / 16;
     for (int64_t j0 = 0; j0 < n16; j0 += 32 * kCopyUnroll) {
-      uint4 kr[kCopyUnroll], vr[kCopyUnroll];
+      if (j0 > 0 || !pre) {
 #pragma unroll
-      for (int u = 0; u < kCopyUnroll; ++u) {
-        const int64_t j = j0 + u * 32 + lane;
-        if (j < n16) {
-          kr[u] = __ldg(reinterpret_cast<const uint4*>(ksrc) + j);
-          vr[u] = __ldg(reinterpret_cast<const uint4*>(vsrc) + j);
+        for (int u = 0; u < kCopyUnroll; ++u) {
+          const int64_t j = j0 + u * 32 + lane;
+          if (j < n16) {
+            kr[u] = __ldg(reinterpret_cast<const uint4*>(ksrc) + j);
+            vr[u] = __ldg(reinterpret_cast<const uint4*>(vsrc) + j);
+          }
         }
       }
 #pragma unroll
